@@ -1,0 +1,27 @@
+"""Shared test helpers: tolerances and seeded synthetic INT4 weights."""
+import numpy as np
+
+# Output tolerance for every dequant matvec/matmul: max relative error 1e-3
+# with fp32 accumulation, measured per element against the oracle and floored
+# at 1% of the largest oracle magnitude so that outputs near zero are compared
+# absolutely.
+REL_TOL = 1e-3
+REL_FLOOR = 1e-2
+
+
+def max_rel_err(y, ref) -> float:
+    y = np.asarray(y, np.float64).ravel()
+    ref = np.asarray(ref, np.float64).ravel()
+    floor = REL_FLOOR * max(np.abs(ref).max(), 1e-30)
+    return float((np.abs(y - ref) / np.maximum(np.abs(ref), floor)).max())
+
+
+def synthetic_int4(rng, out_f: int, in_f: int, group: int = 32):
+    """BASELINE config-1 style weights: uniform codes u in [0, 15] (q = u - 7),
+    fp16 scales of |N(0, 0.02)| magnitude kept as their exact fp32 value.
+    Returns (packed uint8 [out_f*in_f/2], scales_f32 [ngroups], scales_f16)."""
+    n = out_f * in_f
+    codes = rng.integers(0, 16, size=n, dtype=np.uint8)
+    packed = (codes[0::2] | (codes[1::2] << 4)).astype(np.uint8)
+    s16 = np.abs(rng.normal(0, 0.02, size=-(-n // group))).astype(np.float16)
+    return packed, s16.astype(np.float32), s16
