@@ -72,6 +72,29 @@ int gemv_int4(const float* x, size_t ldx, size_t batch, const uint8_t* packed, c
               size_t group, cudaStream_t stream);
 
 int gemv_device_error(int clear);
+int ops_device_error(int clear);
+int add_rmsnorm(const float* a, size_t lda, const float* b, size_t ldb, size_t b_split_stride, int nb,
+                float* residual, size_t ldr, const float* w, float eps, float* out, size_t ldo, size_t batch,
+                size_t dim, cudaStream_t stream);
+int silu_mul(const float* gate, const float* up, size_t ld_in, float* out, size_t ld_out, size_t batch, size_t n,
+             cudaStream_t stream);
+int embed_gather(const __half* table, size_t vocab, size_t dim, const int32_t* tokens, size_t batch, float* out,
+                 size_t ldo, cudaStream_t stream);
+int qkv_rope_append(const float* qkv, size_t ld, size_t split_stride, int nsplit, const float* bias,
+                    const float* cos_t, const float* sin_t, size_t positions, const int32_t* pos, size_t batch,
+                    size_t num_heads, size_t num_kv_heads, size_t head_dim, float* q_out, size_t ldq, float* pool,
+                    size_t page_floats, const int32_t* block_tables, size_t max_pages, size_t layer,
+                    cudaStream_t stream);
+size_t attention_workspace_floats(size_t lanes, size_t num_heads, size_t head_dim, size_t nsplit);
+int attention_chunk(size_t lanes, size_t num_kv_heads, size_t max_ctx);
+int paged_attention(const float* q, size_t ldq, const float* pool, size_t page_floats, const int32_t* block_tables,
+                    size_t max_pages, const int32_t* ctx_lens, size_t max_ctx, size_t lanes, size_t layer,
+                    size_t num_heads, size_t num_kv_heads, size_t head_dim, float* out, size_t ldo, float* workspace,
+                    size_t workspace_floats, int chunk, cudaStream_t stream);
+size_t argmax_workspace_bytes(size_t batch, size_t n);
+int argmax_rows(const float* logits, size_t ld, size_t batch, size_t n, const uint64_t* words, size_t word_count,
+                glacier_argmax_result* out, int32_t* tokens, int32_t* status, void* workspace, size_t ws_bytes,
+                cudaStream_t stream);
 
 }  // namespace glacier
 
@@ -85,9 +108,9 @@ int glacier_cuda_version(void) { return (0 << 16) | 1; }
 
 int glacier_cuda_device_status(int clear) {
   GLC_CHECK_CUDA(cudaDeviceSynchronize());
-  const int v = gemv_device_error(clear);
-  if (v < 0) return set_error(GLACIER_CUDA_ECUDA, "device status read failed");
-  return v;
+  const int v = gemv_device_error(clear), w = ops_device_error(clear);
+  if (v < 0 || w < 0) return set_error(GLACIER_CUDA_ECUDA, "device status read failed");
+  return v ? v : (w ? 2 : 0);
 }
 
 int glacier_cuda_int4_matvec_f32(const float* x, const uint8_t* packed, const float* scales,
@@ -115,6 +138,67 @@ int glacier_cuda_int4_linear(const float* x, size_t batch, const uint8_t* packed
                              out_features, out_features, in_features, group_size, (cudaStream_t)stream);
   return gemv_int4<float>(x, in_features, batch, packed, static_cast<const float*>(scales), 0, bias, y,
                           out_features, out_features, in_features, group_size, (cudaStream_t)stream);
+}
+
+int glacier_cuda_rmsnorm_f32(const float* x, const float* weight, float eps, float* out, size_t batch, size_t dim,
+                             void* stream) {
+  return add_rmsnorm(x, dim, nullptr, dim, 0, 0, nullptr, dim, weight, eps, out, dim, batch, dim,
+                     (cudaStream_t)stream);
+}
+
+int glacier_cuda_add_rmsnorm_f32(const float* a, const float* b, float* residual, const float* weight, float eps,
+                                 float* out, size_t batch, size_t dim, void* stream) {
+  GLC_REQUIRE(b && residual, "add_rmsnorm: null argument");
+  return add_rmsnorm(a, dim, b, dim, 0, 1, residual, dim, weight, eps, out, dim, batch, dim, (cudaStream_t)stream);
+}
+
+int glacier_cuda_silu_mul_f32(const float* gate, const float* up, size_t ld_in, float* out, size_t ld_out,
+                              size_t batch, size_t n, void* stream) {
+  return silu_mul(gate, up, ld_in, out, ld_out, batch, n, (cudaStream_t)stream);
+}
+
+int glacier_cuda_embedding_f16(const uint16_t* table, size_t vocab, size_t dim, const int32_t* tokens, size_t batch,
+                               float* out, void* stream) {
+  return embed_gather(reinterpret_cast<const __half*>(table), vocab, dim, tokens, batch, out, dim,
+                      (cudaStream_t)stream);
+}
+
+int glacier_cuda_qkv_rope_append_f32(const float* qkv, size_t ld, const float* bias, const float* cos_table,
+                                     const float* sin_table, size_t positions, const int32_t* pos, size_t batch,
+                                     size_t num_heads, size_t num_kv_heads, size_t head_dim, float* q_out, size_t ldq,
+                                     float* kv_pages, size_t page_floats, const int32_t* block_tables,
+                                     size_t max_pages, size_t layer, void* stream) {
+  return qkv_rope_append(qkv, ld, 0, 1, bias, cos_table, sin_table, positions, pos, batch, num_heads, num_kv_heads,
+                         head_dim, q_out, ldq, kv_pages, page_floats, block_tables, max_pages, layer,
+                         (cudaStream_t)stream);
+}
+
+size_t glacier_cuda_paged_attention_workspace(size_t lanes, size_t num_heads, size_t num_kv_heads, size_t head_dim,
+                                              size_t max_ctx) {
+  if (!lanes || !num_kv_heads || !max_ctx) return 0;
+  const int chunk = attention_chunk(lanes, num_kv_heads, max_ctx);
+  return attention_workspace_floats(lanes, num_heads, head_dim, ceil_div(max_ctx, (size_t)chunk));
+}
+
+int glacier_cuda_paged_attention_f32(const float* q, const float* kv_pages, size_t page_floats,
+                                     const int32_t* block_tables, size_t max_pages, const int32_t* ctx_lens,
+                                     size_t max_ctx, size_t lanes, size_t layer, size_t num_heads, size_t num_kv_heads,
+                                     size_t head_dim, float* out, float* workspace, size_t workspace_floats,
+                                     void* stream) {
+  GLC_REQUIRE(lanes > 0 && num_kv_heads > 0, "paged_attention: empty batch");
+  return paged_attention(q, num_heads * head_dim, kv_pages, page_floats, block_tables, max_pages, ctx_lens, max_ctx,
+                         lanes, layer, num_heads, num_kv_heads, head_dim, out, num_heads * head_dim, workspace,
+                         workspace_floats, attention_chunk(lanes, num_kv_heads, max_ctx), (cudaStream_t)stream);
+}
+
+size_t glacier_cuda_argmax_workspace(size_t batch, size_t n) { return argmax_workspace_bytes(batch, n); }
+
+int glacier_cuda_argmax_eligible_f32(const float* logits, size_t batch, size_t n, const uint64_t* words,
+                                     size_t word_count, int32_t* tokens, int32_t* status,
+                                     glacier_argmax_result* results, void* workspace, size_t workspace_bytes,
+                                     void* stream) {
+  return argmax_rows(logits, n, batch, n, words, word_count, results, tokens, status, workspace, workspace_bytes,
+                     (cudaStream_t)stream);
 }
 
 }  // extern "C"

@@ -48,6 +48,26 @@ int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base
 // Allows `bytes` of dynamic shared memory for `kernel` (once per kernel).
 int allow_dynamic_smem(const void* kernel, int bytes);
 
+// A device-resident INT4 weight: the reference's exact nibble packing plus one
+// scale row per output row (fp16 mirror or the original fp32), with the TMA
+// descriptors of the tensor-core GEMV encoded once.
+struct Int4Weight {
+  const uint8_t* packed = nullptr;  // [M, K/2] (or the flat packing when !row_groups)
+  const void* scales = nullptr;     // [M, scale_stride] or flat [ceil(M*K/group)]
+  bool f16 = true;
+  size_t scale_stride = 0;          // elements per scale row; 0 = flat reference array
+  size_t M = 0, K = 0, group = 0;
+  bool tc = false;                  // tensor-core GEMV eligible (maps valid)
+  CUtensorMap tmap_w, tmap_s;
+};
+
+// Validates the layout and encodes TMA maps when the tensor-core path applies.
+int int4_weight_prepare(Int4Weight& w);
+
+// y[b, :] = x[b, :] * dequant(W)^T + bias for b < batch (row strides ldx, ldy).
+int int4_linear(const Int4Weight& w, const float* x, size_t ldx, size_t batch, const float* bias, float* y,
+                size_t ldy, cudaStream_t stream);
+
 // Wall-clock limit for every bounded spin-wait in device code (nanoseconds).
 constexpr unsigned long long kSpinLimitNs = 2000000000ull;
 

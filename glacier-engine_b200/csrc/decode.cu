@@ -1,0 +1,523 @@
+// Device-resident model, paged KV pool and the batched decode step.
+//
+// The step is the reference's cached decode (forwardLayerCached,
+// src/generate.zig:1511-1967, and the loop at :5366-5450) for `lanes`
+// independent requests at once, each with its own position and block table
+// (decode_lane4.zig generalised to any lane count):
+//
+//   x = embed(token)                                  loadEmbeddingRow :3653
+//   per layer:  h = rmsnorm(x + down_prev)            (fused residual add)
+//               qkv = W_qkv h        (one GEMV over the fused [Wq; Wk; Wv])
+//               q, k = rope(q, k, pos); pages <- k, v; q += bias, ...
+//               a = paged_attention(q)                paged_attention.zig:108
+//               h2 = rmsnorm(x + W_o a)
+//               gu = W_gu h2         (one GEMV over the fused [Wgate; Wup])
+//               down = W_d (silu(gate) * up)
+//   logits = W_lm rmsnorm(x + down)  ->  eligible argmax  ->  token ids
+//
+// Row-major INT4 payloads concatenate by rows, so Q/K/V and gate/up are
+// uploaded straight into one fused device matrix each (no re-layout of the
+// codes).  Every buffer is reserved up front: a step allocates nothing and can
+// be captured in a CUDA graph.
+#include <math.h>
+#include <string.h>
+
+#include <memory>
+#include <vector>
+
+#include "common.cuh"
+
+namespace glacier {
+
+int add_rmsnorm(const float* a, size_t lda, const float* b, size_t ldb, size_t b_split_stride, int nb,
+                float* residual, size_t ldr, const float* w, float eps, float* out, size_t ldo, size_t batch,
+                size_t dim, cudaStream_t stream);
+int silu_mul(const float* gate, const float* up, size_t ld_in, float* out, size_t ld_out, size_t batch, size_t n,
+             cudaStream_t stream);
+int embed_gather(const __half* table, size_t vocab, size_t dim, const int32_t* tokens, size_t batch, float* out,
+                 size_t ldo, cudaStream_t stream);
+int qkv_rope_append(const float* qkv, size_t ld, size_t split_stride, int nsplit, const float* bias,
+                    const float* cos_t, const float* sin_t, size_t positions, const int32_t* pos, size_t batch,
+                    size_t num_heads, size_t num_kv_heads, size_t head_dim, float* q_out, size_t ldq, float* pool,
+                    size_t page_floats, const int32_t* block_tables, size_t max_pages, size_t layer,
+                    cudaStream_t stream);
+size_t attention_workspace_floats(size_t lanes, size_t num_heads, size_t head_dim, size_t nsplit);
+int attention_chunk(size_t lanes, size_t num_kv_heads, size_t max_ctx);
+int paged_attention(const float* q, size_t ldq, const float* pool, size_t page_floats, const int32_t* block_tables,
+                    size_t max_pages, const int32_t* ctx_lens, size_t max_ctx, size_t lanes, size_t layer,
+                    size_t num_heads, size_t num_kv_heads, size_t head_dim, float* out, size_t ldo, float* workspace,
+                    size_t workspace_floats, int chunk, cudaStream_t stream);
+size_t argmax_workspace_bytes(size_t batch, size_t n);
+int argmax_rows(const float* logits, size_t ld, size_t batch, size_t n, const uint64_t* words, size_t word_count,
+                glacier_argmax_result* out, int32_t* tokens, int32_t* status, void* workspace, size_t ws_bytes,
+                cudaStream_t stream);
+
+namespace {
+
+__global__ void ctx_from_pos_kernel(const int32_t* __restrict__ pos, int32_t* __restrict__ ctx, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) ctx[i] = pos[i] + 1;
+}
+
+struct DevBuf {
+  void* p = nullptr;
+  size_t bytes = 0;
+  ~DevBuf() {
+    if (p) cudaFree(p);
+  }
+  int alloc(size_t n) {
+    if (p) cudaFree(p);
+    p = nullptr;
+    bytes = 0;
+    if (n == 0) return GLACIER_CUDA_OK;
+    if (cudaMalloc(&p, n) != cudaSuccess) {
+      cudaGetLastError();
+      return set_error(GLACIER_CUDA_ENOMEM, "cudaMalloc(%zu) failed", n);
+    }
+    bytes = n;
+    return GLACIER_CUDA_OK;
+  }
+  template <typename T>
+  T* as() const {
+    return static_cast<T*>(p);
+  }
+};
+
+// A fused INT4 matrix whose row blocks are uploaded piece by piece.
+struct FusedWeight {
+  DevBuf packed, scales;
+  Int4Weight w;
+  std::vector<size_t> part_rows;   // rows of each part
+  std::vector<bool> loaded;
+  size_t scale_stride = 0;
+  bool f16 = true;
+
+  int init(const std::vector<size_t>& rows, size_t K, size_t group, bool scales_f16) {
+    part_rows = rows;
+    loaded.assign(rows.size(), false);
+    size_t M = 0;
+    for (size_t r : rows) M += r;
+    f16 = scales_f16;
+    const size_t esz = f16 ? 2 : 4;
+    const size_t groups = ceil_div(K, group);
+    scale_stride = ceil_div(groups * esz, 16) * 16 / esz;  // 16-byte aligned scale rows
+    int rc = packed.alloc(M * K / 2);
+    if (rc) return rc;
+    rc = scales.alloc(M * scale_stride * esz);
+    if (rc) return rc;
+    GLC_CHECK_CUDA(cudaMemset(scales.p, 0, scales.bytes));
+    w.packed = packed.as<uint8_t>();
+    w.scales = scales.p;
+    w.f16 = f16;
+    w.scale_stride = scale_stride;
+    w.M = M;
+    w.K = K;
+    w.group = group;
+    return GLACIER_CUDA_OK;
+  }
+
+  // One part given in the reference's Int4WeightData form: row-major packed
+  // codes and one f32 scale per group along the flat index.
+  int load_part(size_t part, const uint8_t* pk, size_t pk_bytes, const float* sc, size_t sc_count) {
+    GLC_REQUIRE(part < part_rows.size(), "weight part %zu out of range", part);
+    const size_t rows = part_rows[part], K = w.K, group = w.group;
+    const size_t groups = K / group;
+    GLC_REQUIRE(K % 2 == 0 && K % group == 0, "weight rows must hold whole bytes and groups (K=%zu g=%zu)", K,
+                group);
+    GLC_REQUIRE(pk_bytes == rows * K / 2, "packed bytes %zu != %zu", pk_bytes, rows * K / 2);
+    GLC_REQUIRE(sc_count == rows * groups, "scale count %zu != %zu", sc_count, rows * groups);
+    size_t row0 = 0;
+    for (size_t i = 0; i < part; ++i) row0 += part_rows[i];
+    GLC_CHECK_CUDA(cudaMemcpy(packed.as<uint8_t>() + row0 * K / 2, pk, pk_bytes, cudaMemcpyHostToDevice));
+    const size_t esz = f16 ? 2 : 4;
+    std::vector<uint8_t> host(rows * scale_stride * esz, 0);
+    for (size_t r = 0; r < rows; ++r)
+      for (size_t g = 0; g < groups; ++g) {
+        const float s = sc[r * groups + g];
+        if (f16) {
+          // Round-to-nearest-even fp16 mirror (int4_weights.zig:348-358 withF16Scales).
+          const __half h = __float2half_rn(s);
+          memcpy(&host[(r * scale_stride + g) * 2], &h, 2);
+        } else {
+          memcpy(&host[(r * scale_stride + g) * 4], &s, 4);
+        }
+      }
+    GLC_CHECK_CUDA(cudaMemcpy(scales.as<uint8_t>() + row0 * scale_stride * esz, host.data(), host.size(),
+                              cudaMemcpyHostToDevice));
+    loaded[part] = true;
+    return GLACIER_CUDA_OK;
+  }
+
+  bool complete() const {
+    for (bool b : loaded)
+      if (!b) return false;
+    return true;
+  }
+};
+
+struct Layer {
+  FusedWeight qkv, o, gu, d;
+  DevBuf bqkv, in_norm, post_norm;
+  bool has_bias[3] = {false, false, false};
+  bool norm_loaded[2] = {false, false};
+};
+
+}  // namespace
+
+}  // namespace glacier
+
+using namespace glacier;
+
+struct glacier_cuda_model {
+  glacier_cuda_model_config cfg;
+  int device = 0;
+  size_t q_dim = 0, kv_dim = 0, qkv_dim = 0;
+  std::vector<std::unique_ptr<Layer>> layers;
+  FusedWeight lm;
+  DevBuf embedding, final_norm, rope_cos, rope_sin;
+  bool emb_loaded = false, final_loaded = false, finalized = false;
+  // Reserved step workspace.
+  size_t max_lanes = 0, max_pages = 0;
+  DevBuf x, hn, qkv, q, attn, proj, gu, act, down, logits, ctx, att_ws, arg_ws, status;
+  size_t att_floats = 0, arg_bytes = 0;
+  int att_chunk = 0;
+};
+
+struct glacier_cuda_kv {
+  size_t num_pages = 0, page_floats = 0;
+  DevBuf pool;
+};
+
+namespace {
+
+int load_qio(const uint8_t* payload, size_t bytes, size_t expect_elems, size_t expect_group,
+             std::vector<float>& scales, const uint8_t** packed, size_t* packed_bytes) {
+  // src/model/qio.zig:49-70 readQuantHeader and :116-160 decodePage layout.
+  GLC_REQUIRE(payload && bytes >= 16, "qio: truncated header");
+  uint32_t magic, n, g;
+  memcpy(&magic, payload, 4);
+  memcpy(&n, payload + 4, 4);
+  memcpy(&g, payload + 8, 4);
+  GLC_REQUIRE(magic == 0x514F4954u, "qio: bad magic 0x%08x", magic);
+  GLC_REQUIRE(g != 0, "qio: zero group size");
+  GLC_REQUIRE(payload[12] == 1, "qio: precision %u is not INT4", (unsigned)payload[12]);
+  GLC_REQUIRE(n == expect_elems && g == expect_group, "qio: %u elements / group %u, expected %zu / %zu", n, g,
+              expect_elems, expect_group);
+  const size_t ngroups = ceil_div(n, g);
+  const size_t pk = ceil_div(n, 2);
+  GLC_REQUIRE(bytes >= 16 + ngroups * 4 + pk, "qio: truncated payload");
+  scales.resize(ngroups);
+  memcpy(scales.data(), payload + 16, ngroups * 4);
+  *packed = payload + 16 + ngroups * 4;
+  *packed_bytes = pk;
+  return GLACIER_CUDA_OK;
+}
+
+FusedWeight* weight_slot(glacier_cuda_model* m, int layer, int kind, size_t* part) {
+  *part = 0;
+  if (kind == GLACIER_CUDA_W_LM_HEAD) return layer == -1 ? &m->lm : nullptr;
+  if (layer < 0 || layer >= (int)m->layers.size()) return nullptr;
+  Layer& L = *m->layers[layer];
+  switch (kind) {
+    case GLACIER_CUDA_W_Q: *part = 0; return &L.qkv;
+    case GLACIER_CUDA_W_K: *part = 1; return &L.qkv;
+    case GLACIER_CUDA_W_V: *part = 2; return &L.qkv;
+    case GLACIER_CUDA_W_O: return &L.o;
+    case GLACIER_CUDA_W_GATE: *part = 0; return &L.gu;
+    case GLACIER_CUDA_W_UP: *part = 1; return &L.gu;
+    case GLACIER_CUDA_W_DOWN: return &L.d;
+    default: return nullptr;
+  }
+}
+
+size_t weight_out_features(const glacier_cuda_model* m, int kind) {
+  const auto& c = m->cfg;
+  switch (kind) {
+    case GLACIER_CUDA_W_Q: return m->q_dim;
+    case GLACIER_CUDA_W_K: case GLACIER_CUDA_W_V: return m->kv_dim;
+    case GLACIER_CUDA_W_O: case GLACIER_CUDA_W_DOWN: return c.dim;
+    case GLACIER_CUDA_W_GATE: case GLACIER_CUDA_W_UP: return c.hidden;
+    case GLACIER_CUDA_W_LM_HEAD: return c.vocab;
+    default: return 0;
+  }
+}
+
+size_t weight_in_features(const glacier_cuda_model* m, int kind) {
+  switch (kind) {
+    case GLACIER_CUDA_W_O: return m->q_dim;
+    case GLACIER_CUDA_W_DOWN: return m->cfg.hidden;
+    default: return m->cfg.dim;
+  }
+}
+
+int bind_device(const glacier_cuda_model* m) {
+  GLC_CHECK_CUDA(cudaSetDevice(m->device));
+  return GLACIER_CUDA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+glacier_cuda_model* glacier_cuda_model_create(const glacier_cuda_model_config* cfg) {
+  if (!cfg) {
+    set_error(GLACIER_CUDA_EINVAL, "model_create: null config");
+    return nullptr;
+  }
+  const auto& c = *cfg;
+  if (c.num_layers == 0 || c.dim == 0 || c.hidden == 0 || c.num_heads == 0 || c.num_kv_heads == 0 ||
+      c.head_dim == 0 || c.vocab == 0 || c.group_size == 0 || c.num_heads % c.num_kv_heads != 0 ||
+      c.head_dim % 2 != 0 || c.max_positions == 0) {
+    set_error(GLACIER_CUDA_EINVAL, "model_create: invalid configuration");
+    return nullptr;
+  }
+  auto m = std::make_unique<glacier_cuda_model>();
+  m->cfg = c;
+  if (cudaGetDevice(&m->device) != cudaSuccess) {
+    set_error(GLACIER_CUDA_ECUDA, "model_create: no CUDA device");
+    return nullptr;
+  }
+  m->q_dim = (size_t)c.num_heads * c.head_dim;
+  m->kv_dim = (size_t)c.num_kv_heads * c.head_dim;
+  m->qkv_dim = m->q_dim + 2 * m->kv_dim;
+  const bool f16 = c.scales_f16 != 0;
+  for (uint32_t l = 0; l < c.num_layers; ++l) {
+    auto L = std::make_unique<Layer>();
+    if (L->qkv.init({m->q_dim, m->kv_dim, m->kv_dim}, c.dim, c.group_size, f16) ||
+        L->o.init({c.dim}, m->q_dim, c.group_size, f16) ||
+        L->gu.init({c.hidden, c.hidden}, c.dim, c.group_size, f16) ||
+        L->d.init({c.dim}, c.hidden, c.group_size, f16) || L->bqkv.alloc(m->qkv_dim * 4) ||
+        L->in_norm.alloc((size_t)c.dim * 4) || L->post_norm.alloc((size_t)c.dim * 4))
+      return nullptr;
+    if (cudaMemset(L->bqkv.p, 0, L->bqkv.bytes) != cudaSuccess) {
+      set_error(GLACIER_CUDA_ECUDA, "model_create: memset failed");
+      return nullptr;
+    }
+    m->layers.push_back(std::move(L));
+  }
+  if (m->lm.init({c.vocab}, c.dim, c.group_size, f16) || m->embedding.alloc((size_t)c.vocab * c.dim * 2) ||
+      m->final_norm.alloc((size_t)c.dim * 4))
+    return nullptr;
+  // RoPE table (generate.zig:791-808): angle = pos / theta^(2i/hd) in f32.
+  const size_t half = c.head_dim / 2, P = c.max_positions;
+  std::vector<float> cs(P * half), sn(P * half);
+  for (size_t pos = 0; pos < P; ++pos)
+    for (size_t i = 0; i < half; ++i) {
+      const float exponent = (float)(2 * i) / (float)c.head_dim;
+      const float freq = 1.0f / powf(c.rope_theta, exponent);
+      const float angle = (float)pos * freq;
+      cs[pos * half + i] = cosf(angle);
+      sn[pos * half + i] = sinf(angle);
+    }
+  if (m->rope_cos.alloc(cs.size() * 4) || m->rope_sin.alloc(sn.size() * 4)) return nullptr;
+  if (cudaMemcpy(m->rope_cos.p, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemcpy(m->rope_sin.p, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
+    set_error(GLACIER_CUDA_ECUDA, "model_create: rope upload failed");
+    return nullptr;
+  }
+  return m.release();
+}
+
+void glacier_cuda_model_destroy(glacier_cuda_model* m) { delete m; }
+
+int glacier_cuda_model_load_int4(glacier_cuda_model* m, int layer, int kind, const uint8_t* packed,
+                                 size_t packed_bytes, const float* scales, size_t scale_count) {
+  GLC_REQUIRE(m && packed && scales, "model_load_int4: null argument");
+  GLC_REQUIRE(!m->finalized, "model_load_int4: model already finalized");
+  size_t part = 0;
+  FusedWeight* fw = weight_slot(m, layer, kind, &part);
+  GLC_REQUIRE(fw, "model_load_int4: bad layer %d / kind %d", layer, kind);
+  const int rc = bind_device(m);
+  if (rc) return rc;
+  return fw->load_part(part, packed, packed_bytes, scales, scale_count);
+}
+
+int glacier_cuda_model_load_qio(glacier_cuda_model* m, int layer, int kind, const uint8_t* payload,
+                                size_t payload_bytes) {
+  GLC_REQUIRE(m, "model_load_qio: null model");
+  const size_t out_f = weight_out_features(m, kind), in_f = weight_in_features(m, kind);
+  GLC_REQUIRE(out_f > 0, "model_load_qio: bad kind %d", kind);
+  std::vector<float> scales;
+  const uint8_t* pk = nullptr;
+  size_t pk_bytes = 0;
+  const int rc = load_qio(payload, payload_bytes, out_f * in_f, m->cfg.group_size, scales, &pk, &pk_bytes);
+  if (rc) return rc;
+  return glacier_cuda_model_load_int4(m, layer, kind, pk, pk_bytes, scales.data(), scales.size());
+}
+
+int glacier_cuda_model_load_f32(glacier_cuda_model* m, int layer, int kind, const float* data, size_t count) {
+  GLC_REQUIRE(m && data, "model_load_f32: null argument");
+  GLC_REQUIRE(!m->finalized, "model_load_f32: model already finalized");
+  int rc = bind_device(m);
+  if (rc) return rc;
+  const auto& c = m->cfg;
+  if (kind == GLACIER_CUDA_N_FINAL) {
+    GLC_REQUIRE(layer == -1 && count == c.dim, "model_load_f32: final norm needs %u values", c.dim);
+    GLC_CHECK_CUDA(cudaMemcpy(m->final_norm.p, data, count * 4, cudaMemcpyHostToDevice));
+    m->final_loaded = true;
+    return GLACIER_CUDA_OK;
+  }
+  GLC_REQUIRE(layer >= 0 && layer < (int)c.num_layers, "model_load_f32: bad layer %d", layer);
+  Layer& L = *m->layers[layer];
+  switch (kind) {
+    case GLACIER_CUDA_B_Q:
+    case GLACIER_CUDA_B_K:
+    case GLACIER_CUDA_B_V: {
+      const int part = kind - GLACIER_CUDA_B_Q;
+      const size_t off = part == 0 ? 0 : part == 1 ? m->q_dim : m->q_dim + m->kv_dim;
+      const size_t n = part == 0 ? m->q_dim : m->kv_dim;
+      GLC_REQUIRE(count == n, "model_load_f32: bias needs %zu values", n);
+      GLC_CHECK_CUDA(cudaMemcpy(L.bqkv.as<float>() + off, data, n * 4, cudaMemcpyHostToDevice));
+      L.has_bias[part] = true;
+      return GLACIER_CUDA_OK;
+    }
+    case GLACIER_CUDA_N_INPUT:
+    case GLACIER_CUDA_N_POST_ATTN: {
+      GLC_REQUIRE(count == c.dim, "model_load_f32: norm needs %u values", c.dim);
+      DevBuf& dst = kind == GLACIER_CUDA_N_INPUT ? L.in_norm : L.post_norm;
+      GLC_CHECK_CUDA(cudaMemcpy(dst.p, data, count * 4, cudaMemcpyHostToDevice));
+      L.norm_loaded[kind == GLACIER_CUDA_N_INPUT ? 0 : 1] = true;
+      return GLACIER_CUDA_OK;
+    }
+    default:
+      return set_error(GLACIER_CUDA_EINVAL, "model_load_f32: bad kind %d", kind);
+  }
+}
+
+int glacier_cuda_model_load_embedding_f16(glacier_cuda_model* m, const uint16_t* table, size_t count) {
+  GLC_REQUIRE(m && table, "model_load_embedding: null argument");
+  GLC_REQUIRE(count == (size_t)m->cfg.vocab * m->cfg.dim, "model_load_embedding: %zu values, expected %zu", count,
+              (size_t)m->cfg.vocab * m->cfg.dim);
+  const int rc = bind_device(m);
+  if (rc) return rc;
+  GLC_CHECK_CUDA(cudaMemcpy(m->embedding.p, table, count * 2, cudaMemcpyHostToDevice));
+  m->emb_loaded = true;
+  return GLACIER_CUDA_OK;
+}
+
+int glacier_cuda_model_finalize(glacier_cuda_model* m) {
+  GLC_REQUIRE(m, "model_finalize: null model");
+  int rc = bind_device(m);
+  if (rc) return rc;
+  for (size_t l = 0; l < m->layers.size(); ++l) {
+    Layer& L = *m->layers[l];
+    GLC_REQUIRE(L.qkv.complete() && L.o.complete() && L.gu.complete() && L.d.complete(),
+                "model_finalize: layer %zu is missing a weight", l);
+    GLC_REQUIRE(L.norm_loaded[0] && L.norm_loaded[1], "model_finalize: layer %zu is missing a norm", l);
+    for (FusedWeight* fw : {&L.qkv, &L.o, &L.gu, &L.d})
+      if ((rc = int4_weight_prepare(fw->w))) return rc;
+  }
+  GLC_REQUIRE(m->lm.complete() && m->emb_loaded && m->final_loaded,
+              "model_finalize: LM head, embedding or final norm missing");
+  if ((rc = int4_weight_prepare(m->lm.w))) return rc;
+  m->finalized = true;
+  return GLACIER_CUDA_OK;
+}
+
+int glacier_cuda_model_reserve(glacier_cuda_model* m, size_t max_lanes, size_t max_pages) {
+  GLC_REQUIRE(m && m->finalized, "model_reserve: model not finalized");
+  GLC_REQUIRE(max_lanes > 0 && max_pages > 0, "model_reserve: empty reservation");
+  GLC_REQUIRE(max_pages * 16 <= m->cfg.max_positions, "model_reserve: %zu pages exceed %u RoPE positions",
+              max_pages, m->cfg.max_positions);
+  int rc = bind_device(m);
+  if (rc) return rc;
+  const auto& c = m->cfg;
+  const size_t L = max_lanes;
+  m->att_chunk = attention_chunk(L, c.num_kv_heads, max_pages * 16);
+  const size_t nsplit = ceil_div(max_pages * 16, (size_t)m->att_chunk);
+  m->att_floats = attention_workspace_floats(L, c.num_heads, c.head_dim, nsplit);
+  m->arg_bytes = argmax_workspace_bytes(L, c.vocab);
+  if ((rc = m->x.alloc(L * c.dim * 4)) || (rc = m->hn.alloc(L * c.dim * 4)) ||
+      (rc = m->qkv.alloc(L * m->qkv_dim * 4)) || (rc = m->q.alloc(L * m->q_dim * 4)) ||
+      (rc = m->attn.alloc(L * m->q_dim * 4)) || (rc = m->proj.alloc(L * c.dim * 4)) ||
+      (rc = m->gu.alloc(L * 2 * (size_t)c.hidden * 4)) || (rc = m->act.alloc(L * (size_t)c.hidden * 4)) ||
+      (rc = m->down.alloc(L * c.dim * 4)) || (rc = m->logits.alloc(L * (size_t)c.vocab * 4)) ||
+      (rc = m->ctx.alloc(L * 4)) || (rc = m->att_ws.alloc(m->att_floats * 4)) ||
+      (rc = m->arg_ws.alloc(m->arg_bytes)) || (rc = m->status.alloc(L * 4)))
+    return rc;
+  m->max_lanes = max_lanes;
+  m->max_pages = max_pages;
+  return GLACIER_CUDA_OK;
+}
+
+glacier_cuda_kv* glacier_cuda_kv_create(const glacier_cuda_model* m, size_t num_pages) {
+  if (!m || num_pages == 0) {
+    set_error(GLACIER_CUDA_EINVAL, "kv_create: null model or zero pages");
+    return nullptr;
+  }
+  if (bind_device(m)) return nullptr;
+  auto kv = std::make_unique<glacier_cuda_kv>();
+  kv->num_pages = num_pages;
+  // One page = 16 positions of K and V for every layer (paged_kv_cache.zig:1-16).
+  kv->page_floats = (size_t)m->cfg.num_layers * 2 * 16 * m->kv_dim;
+  if (kv->pool.alloc(num_pages * kv->page_floats * 4)) return nullptr;
+  if (cudaMemset(kv->pool.p, 0, kv->pool.bytes) != cudaSuccess) {
+    set_error(GLACIER_CUDA_ECUDA, "kv_create: memset failed");
+    return nullptr;
+  }
+  return kv.release();
+}
+
+void glacier_cuda_kv_destroy(glacier_cuda_kv* kv) { delete kv; }
+
+float* glacier_cuda_kv_pages(glacier_cuda_kv* kv) { return kv ? kv->pool.as<float>() : nullptr; }
+
+size_t glacier_cuda_kv_page_floats(const glacier_cuda_kv* kv) { return kv ? kv->page_floats : 0; }
+
+int glacier_cuda_decode_step(glacier_cuda_model* m, glacier_cuda_kv* kv, size_t lanes, const int32_t* tokens,
+                             const int32_t* positions, const int32_t* block_tables, size_t max_pages,
+                             const uint64_t* eligible, size_t eligible_words, int32_t* tokens_out,
+                             int32_t* status_out, float* logits_out, void* stream_ptr) {
+  GLC_REQUIRE(m && kv && m->finalized, "decode_step: model not finalized");
+  GLC_REQUIRE(lanes > 0 && lanes <= m->max_lanes, "decode_step: %zu lanes, %zu reserved", lanes, m->max_lanes);
+  GLC_REQUIRE(max_pages > 0 && max_pages <= m->max_pages, "decode_step: %zu pages per lane, %zu reserved", max_pages,
+              m->max_pages);
+  GLC_REQUIRE(tokens && positions && block_tables && tokens_out, "decode_step: null argument");
+  if (eligible)
+    GLC_REQUIRE(eligible_words == ceil_div(m->cfg.vocab, 64), "decode_step: eligible mask needs %zu words per lane",
+                ceil_div(m->cfg.vocab, 64));
+  cudaStream_t st = (cudaStream_t)stream_ptr;
+  const auto& c = m->cfg;
+  const size_t D = c.dim, F = c.hidden, B = lanes;
+  const size_t max_ctx = max_pages * 16;
+  int rc;
+  float* x = m->x.as<float>();
+  float* hn = m->hn.as<float>();
+  ctx_from_pos_kernel<<<(unsigned)ceil_div(B, 128), 128, 0, st>>>(positions, m->ctx.as<int32_t>(), (int)B);
+  GLC_CHECK_LAUNCH();
+  if ((rc = embed_gather(m->embedding.as<__half>(), c.vocab, D, tokens, B, x, D, st))) return rc;
+  for (size_t l = 0; l < c.num_layers; ++l) {
+    Layer& L = *m->layers[l];
+    // x (+ previous layer's down projection) -> residual x, normed hn
+    if ((rc = add_rmsnorm(x, D, l ? m->down.as<float>() : nullptr, D, 0, l ? 1 : 0, x, D, L.in_norm.as<float>(),
+                          c.rms_eps, hn, D, B, D, st)))
+      return rc;
+    if ((rc = int4_linear(L.qkv.w, hn, D, B, nullptr, m->qkv.as<float>(), m->qkv_dim, st))) return rc;
+    if ((rc = qkv_rope_append(m->qkv.as<float>(), m->qkv_dim, 0, 1, L.bqkv.as<float>(), m->rope_cos.as<float>(),
+                              m->rope_sin.as<float>(), c.max_positions, positions, B, c.num_heads, c.num_kv_heads,
+                              c.head_dim, m->q.as<float>(), m->q_dim, kv->pool.as<float>(), kv->page_floats,
+                              block_tables, max_pages, l, st)))
+      return rc;
+    if ((rc = paged_attention(m->q.as<float>(), m->q_dim, kv->pool.as<float>(), kv->page_floats, block_tables,
+                              max_pages, m->ctx.as<int32_t>(), max_ctx, B, l, c.num_heads, c.num_kv_heads, c.head_dim,
+                              m->attn.as<float>(), m->q_dim, m->att_ws.as<float>(), m->att_floats,
+                              m->att_chunk, st)))
+      return rc;
+    if ((rc = int4_linear(L.o.w, m->attn.as<float>(), m->q_dim, B, nullptr, m->proj.as<float>(), D, st))) return rc;
+    if ((rc = add_rmsnorm(x, D, m->proj.as<float>(), D, 0, 1, x, D, L.post_norm.as<float>(), c.rms_eps, hn, D, B,
+                          D, st)))
+      return rc;
+    if ((rc = int4_linear(L.gu.w, hn, D, B, nullptr, m->gu.as<float>(), 2 * F, st))) return rc;
+    if ((rc = silu_mul(m->gu.as<float>(), m->gu.as<float>() + F, 2 * F, m->act.as<float>(), F, B, F, st))) return rc;
+    if ((rc = int4_linear(L.d.w, m->act.as<float>(), F, B, nullptr, m->down.as<float>(), D, st))) return rc;
+  }
+  if ((rc = add_rmsnorm(x, D, m->down.as<float>(), D, 0, 1, x, D, m->final_norm.as<float>(), c.rms_eps, hn, D, B, D,
+                        st)))
+    return rc;
+  float* logits = logits_out ? logits_out : m->logits.as<float>();
+  if ((rc = int4_linear(m->lm.w, hn, D, B, nullptr, logits, c.vocab, st))) return rc;
+  return argmax_rows(logits, c.vocab, B, c.vocab, eligible, eligible_words, nullptr, tokens_out,
+                     status_out ? status_out : m->status.as<int32_t>(), m->arg_ws.p, m->arg_bytes, st);
+}
+
+}  // extern "C"

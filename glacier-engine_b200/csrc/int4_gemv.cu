@@ -255,49 +255,71 @@ bool gemv_fast_layout(size_t K, size_t group) {
   return (group & (group - 1)) == 0;
 }
 
-bool gemv_tc_supported(size_t K, size_t group, const void* packed, const float* x, size_t ldx, const void* scales,
-                       size_t scale_stride_bytes);
-template <typename ScaleT>
-int gemv_int4_tc(const float* x, size_t ldx, size_t batch, const uint8_t* packed, const ScaleT* scales,
-                 size_t scale_stride, const float* bias, float* y, size_t ldy, size_t M, size_t K, size_t group,
-                 cudaStream_t stream);
+int gemv_int4_tc(const Int4Weight& w, const float* x, size_t ldx, size_t batch, const float* bias, float* y,
+                 size_t ldy, cudaStream_t stream);
+
+int int4_linear(const Int4Weight& w, const float* x, size_t ldx, size_t batch, const float* bias, float* y,
+                size_t ldy, cudaStream_t stream) {
+  GLC_REQUIRE(x && y && batch > 0, "int4 linear: empty or null argument");
+  const size_t M = w.M, K = w.K, group = w.group;
+  const bool xaligned = ((uintptr_t)x % 16 == 0) && (ldx % 4 == 0);
+  if (w.tc && xaligned) {
+    // Tensor-core GEMV: up to four activation rows per launch.
+    for (size_t b = 0; b < batch; b += 4) {
+      const size_t nb = batch - b < 4 ? batch - b : 4;
+      const int rc = gemv_int4_tc(w, x + b * ldx, ldx, nb, bias, y + b * ldy, ldy, stream);
+      if (rc) return rc;
+    }
+    return GLACIER_CUDA_OK;
+  }
+  const size_t scale_stride = w.scale_stride;
+  if (gemv_fast_layout(K, group) && xaligned && (uintptr_t)w.packed % 16 == 0) {
+    const size_t ss = scale_stride ? scale_stride : K / group;
+    for (size_t b = 0; b < batch; b += 2) {
+      const bool two = b + 2 <= batch;
+      cudaError_t e;
+      if (w.f16)
+        e = two ? launch_split<2, __half>(x + b * ldx, ldx, w.packed, (const __half*)w.scales, ss, bias, y + b * ldy,
+                                          ldy, (int)M, (int)K, (int)group, stream)
+                : launch_split<1, __half>(x + b * ldx, ldx, w.packed, (const __half*)w.scales, ss, bias, y + b * ldy,
+                                          ldy, (int)M, (int)K, (int)group, stream);
+      else
+        e = two ? launch_split<2, float>(x + b * ldx, ldx, w.packed, (const float*)w.scales, ss, bias, y + b * ldy,
+                                         ldy, (int)M, (int)K, (int)group, stream)
+                : launch_split<1, float>(x + b * ldx, ldx, w.packed, (const float*)w.scales, ss, bias, y + b * ldy,
+                                         ldy, (int)M, (int)K, (int)group, stream);
+      GLC_CHECK_CUDA(e);
+    }
+    return GLACIER_CUDA_OK;
+  }
+  // Generic layout: flat element index (scale_stride 0 = flat group array).
+  GLC_REQUIRE(scale_stride == 0 || K % group == 0, "int4 gemv: per-row scale stride needs group-aligned rows");
+  const size_t warps = M * batch;
+  if (w.f16)
+    gemv_int4_generic_kernel<__half><<<(unsigned)ceil_div(warps, 8), 256, 0, stream>>>(
+        x, ldx, w.packed, (const __half*)w.scales, scale_stride, bias, y, ldy, (int)M, (int)K, (int)group, (int)batch);
+  else
+    gemv_int4_generic_kernel<float><<<(unsigned)ceil_div(warps, 8), 256, 0, stream>>>(
+        x, ldx, w.packed, (const float*)w.scales, scale_stride, bias, y, ldy, (int)M, (int)K, (int)group, (int)batch);
+  GLC_CHECK_LAUNCH();
+  return GLACIER_CUDA_OK;
+}
 
 template <typename ScaleT>
 int gemv_int4(const float* x, size_t ldx, size_t batch, const uint8_t* packed, const ScaleT* scales,
               size_t scale_stride, const float* bias, float* y, size_t ldy, size_t M, size_t K,
               size_t group, cudaStream_t stream) {
-  GLC_REQUIRE(M > 0 && K > 0 && batch > 0 && group > 0, "int4 gemv: empty shape or zero group");
-  GLC_REQUIRE(M < (1u << 31) && K < (1u << 31), "int4 gemv: dimension too large");
-  if (gemv_tc_supported(K, group, packed, x, ldx, scales, (scale_stride ? scale_stride : K / 32) * sizeof(ScaleT))) {
-    // Tensor-core GEMV: up to four activation rows per launch.
-    for (size_t b = 0; b < batch; b += 4) {
-      const size_t nb = batch - b < 4 ? batch - b : 4;
-      const int rc = gemv_int4_tc<ScaleT>(x + b * ldx, ldx, nb, packed, scales, scale_stride, bias, y + b * ldy,
-                                          ldy, M, K, group, stream);
-      if (rc) return rc;
-    }
-    return GLACIER_CUDA_OK;
-  }
-  const bool aligned16 = ((uintptr_t)packed % 16 == 0) && ((uintptr_t)x % 16 == 0) && (ldx % 4 == 0);
-  if (gemv_fast_layout(K, group) && aligned16) {
-    if (scale_stride == 0) scale_stride = K / group;  // flat array == row-major [M, K/g]
-    size_t b = 0;
-    for (; b + 2 <= batch; b += 2)
-      GLC_CHECK_CUDA((launch_split<2, ScaleT>(x + b * ldx, ldx, packed, scales, scale_stride, bias,
-                                              y + b * ldy, ldy, (int)M, (int)K, (int)group, stream)));
-    if (b < batch)
-      GLC_CHECK_CUDA((launch_split<1, ScaleT>(x + b * ldx, ldx, packed, scales, scale_stride, bias,
-                                              y + b * ldy, ldy, (int)M, (int)K, (int)group, stream)));
-    return GLACIER_CUDA_OK;
-  }
-  // Generic layout: flat element index (scale_stride 0 = flat group array).
-  GLC_REQUIRE(scale_stride == 0 || K % group == 0,
-              "int4 gemv: per-row scale stride needs group-aligned rows");
-  const size_t warps = M * batch;
-  gemv_int4_generic_kernel<ScaleT><<<(unsigned)ceil_div(warps, 8), 256, 0, stream>>>(
-      x, ldx, packed, scales, scale_stride, bias, y, ldy, (int)M, (int)K, (int)group, (int)batch);
-  GLC_CHECK_LAUNCH();
-  return GLACIER_CUDA_OK;
+  Int4Weight w;
+  w.packed = packed;
+  w.scales = scales;
+  w.f16 = sizeof(ScaleT) == 2;
+  w.scale_stride = scale_stride;
+  w.M = M;
+  w.K = K;
+  w.group = group;
+  const int rc = int4_weight_prepare(w);
+  if (rc) return rc;
+  return int4_linear(w, x, ldx, batch, bias, y, ldy, stream);
 }
 
 template int gemv_int4<__half>(const float*, size_t, size_t, const uint8_t*, const __half*, size_t,

@@ -278,17 +278,10 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_tc_kernel(const __grid_const
 }
 
 template <typename ScaleT>
-int launch_gemv_tc(const float* x, size_t ldx, size_t batch, const uint8_t* packed, const ScaleT* scales,
-                   size_t scale_stride, const float* bias, float* y, size_t ldy, size_t M, size_t K,
-                   cudaStream_t stream) {
-  CUtensorMap tmap_w, tmap_s;
-  int rc = encode_tmap_2d(&tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, packed, K / 2, M, K / 2, 128, kRows,
-                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
-  if (rc) return rc;
-  rc = encode_tmap_2d(&tmap_s, sizeof(ScaleT) == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
-                      scales, K / 32, M, scale_stride * sizeof(ScaleT), 8, kRows, CU_TENSOR_MAP_SWIZZLE_NONE,
-                      CU_TENSOR_MAP_L2_PROMOTION_NONE);
-  if (rc) return rc;
+int launch_gemv_tc(const Int4Weight& w, const float* x, size_t ldx, size_t batch, const float* bias, float* y,
+                   size_t ldy, cudaStream_t stream) {
+  const size_t M = w.M, K = w.K;
+  int rc = 0;
   const int tiles = (int)ceil_div(M, kRows);
   const int stages = (int)ceil_div(K, 256);
   // Cluster size: enough CTAs for two per SM, K-slices short enough that the
@@ -327,7 +320,7 @@ int launch_gemv_tc(const float* x, size_t ldx, size_t batch, const uint8_t* pack
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  GLC_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, tmap_w, tmap_s, prm));
+  GLC_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, w.tmap_w, w.tmap_s, prm));
   return GLACIER_CUDA_OK;
 }
 
@@ -335,26 +328,28 @@ int launch_gemv_tc(const float* x, size_t ldx, size_t batch, const uint8_t* pack
 
 // The tensor-core GEMV handles group 32, whole 32-code chunks, 16-byte aligned
 // operands and scale rows whose byte stride is a multiple of 16 (TMA).
-bool gemv_tc_supported(size_t K, size_t group, const void* packed, const float* x, size_t ldx, const void* scales,
-                       size_t scale_stride_bytes) {
-  if (K == 0 || K % 32 || group != 32) return false;
-  return ((uintptr_t)packed % 16 == 0) && ((uintptr_t)x % 16 == 0) && (ldx % 4 == 0) &&
-         ((uintptr_t)scales % 16 == 0) && (scale_stride_bytes % 16 == 0);
+int int4_weight_prepare(Int4Weight& w) {
+  GLC_REQUIRE(w.packed && w.scales && w.M > 0 && w.K > 0 && w.group > 0, "int4 weight: empty or null");
+  GLC_REQUIRE(w.M < (1u << 31) && w.K < (1u << 31), "int4 weight: dimension too large");
+  const size_t esz = w.f16 ? 2 : 4;
+  const size_t stride = w.scale_stride ? w.scale_stride : (w.K % w.group == 0 ? w.K / w.group : 0);
+  w.tc = w.group == 32 && w.K % 32 == 0 && stride != 0 && (stride * esz) % 16 == 0 &&
+         (uintptr_t)w.packed % 16 == 0 && (uintptr_t)w.scales % 16 == 0;
+  if (!w.tc) return GLACIER_CUDA_OK;
+  w.scale_stride = stride;
+  int rc = encode_tmap_2d(&w.tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.packed, w.K / 2, w.M, w.K / 2, 128, kRows,
+                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+  if (rc) return rc;
+  rc = encode_tmap_2d(&w.tmap_s, w.f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, w.scales,
+                      w.K / 32, w.M, stride * esz, 8, kRows, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE);
+  return rc;
 }
 
-template <typename ScaleT>
-int gemv_int4_tc(const float* x, size_t ldx, size_t batch, const uint8_t* packed, const ScaleT* scales,
-                 size_t scale_stride, const float* bias, float* y, size_t ldy, size_t M, size_t K, size_t group,
-                 cudaStream_t stream) {
-  (void)group;
-  return launch_gemv_tc<ScaleT>(x, ldx, batch, packed, scales, scale_stride ? scale_stride : K / 32, bias, y, ldy,
-                                M, K, stream);
+int gemv_int4_tc(const Int4Weight& w, const float* x, size_t ldx, size_t batch, const float* bias, float* y,
+                 size_t ldy, cudaStream_t stream) {
+  return w.f16 ? launch_gemv_tc<__half>(w, x, ldx, batch, bias, y, ldy, stream)
+               : launch_gemv_tc<float>(w, x, ldx, batch, bias, y, ldy, stream);
 }
-
-template int gemv_int4_tc<__half>(const float*, size_t, size_t, const uint8_t*, const __half*, size_t,
-                                  const float*, float*, size_t, size_t, size_t, size_t, cudaStream_t);
-template int gemv_int4_tc<float>(const float*, size_t, size_t, const uint8_t*, const float*, size_t,
-                                 const float*, float*, size_t, size_t, size_t, size_t, cudaStream_t);
 
 int gemv_device_error(int clear) {
   int v = 0;

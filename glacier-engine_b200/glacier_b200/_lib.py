@@ -39,7 +39,41 @@ SIGNATURES = {
     "glacier_cuda_int4_matvec_f32": ([vp, vp, vp, vp, vp, sz, sz, sz, vp], i32),
     "glacier_cuda_int4_matvec_f16scale": ([vp, vp, vp, vp, vp, sz, sz, sz, vp], i32),
     "glacier_cuda_int4_linear": ([vp, sz, vp, vp, i32, vp, vp, sz, sz, sz, vp], i32),
+    "glacier_cuda_rmsnorm_f32": ([vp, vp, f32, vp, sz, sz, vp], i32),
+    "glacier_cuda_add_rmsnorm_f32": ([vp, vp, vp, vp, f32, vp, sz, sz, vp], i32),
+    "glacier_cuda_silu_mul_f32": ([vp, vp, sz, vp, sz, sz, sz, vp], i32),
+    "glacier_cuda_embedding_f16": ([vp, sz, sz, vp, sz, vp, vp], i32),
+    "glacier_cuda_qkv_rope_append_f32": ([vp, sz, vp, vp, vp, sz, vp, sz, sz, sz, sz, vp, sz, vp, sz, vp, sz,
+                                          sz, vp], i32),
+    "glacier_cuda_paged_attention_workspace": ([sz, sz, sz, sz, sz], sz),
+    "glacier_cuda_paged_attention_f32": ([vp, vp, sz, vp, sz, vp, sz, sz, sz, sz, sz, sz, vp, vp, sz, vp], i32),
+    "glacier_cuda_argmax_workspace": ([sz, sz], sz),
+    "glacier_cuda_argmax_eligible_f32": ([vp, sz, sz, vp, sz, vp, vp, vp, vp, sz, vp], i32),
+    "glacier_cuda_model_create": ([vp], vp),
+    "glacier_cuda_model_destroy": ([vp], None),
+    "glacier_cuda_model_load_int4": ([vp, i32, i32, vp, sz, vp, sz], i32),
+    "glacier_cuda_model_load_qio": ([vp, i32, i32, vp, sz], i32),
+    "glacier_cuda_model_load_f32": ([vp, i32, i32, vp, sz], i32),
+    "glacier_cuda_model_load_embedding_f16": ([vp, vp, sz], i32),
+    "glacier_cuda_model_finalize": ([vp], i32),
+    "glacier_cuda_model_reserve": ([vp, sz, sz], i32),
+    "glacier_cuda_kv_create": ([vp, sz], vp),
+    "glacier_cuda_kv_destroy": ([vp], None),
+    "glacier_cuda_kv_pages": ([vp], vp),
+    "glacier_cuda_kv_page_floats": ([vp], sz),
+    "glacier_cuda_decode_step": ([vp, vp, sz, vp, vp, vp, sz, vp, sz, vp, vp, vp, vp], i32),
 }
+
+# enum glacier_cuda_tensor_kind
+W_Q, W_K, W_V, W_O, W_GATE, W_UP, W_DOWN, W_LM_HEAD, B_Q, B_K, B_V, N_INPUT, N_POST_ATTN, N_FINAL = range(14)
+
+
+class ModelConfigC(C.Structure):
+    """glacier_cuda_model_config."""
+    _fields_ = [(n, C.c_uint32) for n in ("num_layers", "dim", "hidden", "num_heads", "num_kv_heads",
+                                          "head_dim", "vocab", "group_size")] + \
+               [("rms_eps", C.c_float), ("rope_theta", C.c_float), ("max_positions", C.c_uint32),
+                ("scales_f16", C.c_uint32)]
 
 
 def lib():
@@ -67,3 +101,11 @@ def check(rc: int) -> int:
 
 def call(name: str, *args) -> int:
     return check(getattr(lib(), name)(*args))
+
+
+def handle(ptr):
+    """Raise with the library's message when a handle-returning call gave NULL."""
+    if not ptr:
+        msg = lib().glacier_cuda_last_error()
+        raise GlacierCudaError(EINVAL, msg.decode() if msg else "NULL handle")
+    return ptr

@@ -89,6 +89,140 @@ int glacier_cuda_int4_linear(const float *x, size_t batch, const uint8_t *packed
                              size_t out_features, size_t in_features, size_t group_size,
                              void *stream);
 
+/* ------------------------------------------------------------------------
+ * (c) fused norm / rotary / activation steps, on device buffers.
+ * ---------------------------------------------------------------------- */
+
+/* rmsNormF32 (src/backends/cpu/kernels.zig:141-220): out[b] = x[b] / sqrt(mean(x[b]^2) + eps) * weight. */
+int glacier_cuda_rmsnorm_f32(const float *x, const float *weight, float eps, float *out, size_t batch,
+                             size_t dim, void *stream);
+
+/* addRmsNormF32 (kernels.zig:322-401): residual = a + b; out = rmsnorm(residual). residual
+ * may alias a (in-place residual update). */
+int glacier_cuda_add_rmsnorm_f32(const float *a, const float *b, float *residual, const float *weight,
+                                 float eps, float *out, size_t batch, size_t dim, void *stream);
+
+/* siluMulF32 (kernels.zig:465-507) over batch rows with row strides:
+ * out[b, i] = silu(gate[b, i]) * up[b, i]. */
+int glacier_cuda_silu_mul_f32(const float *gate, const float *up, size_t ld_in, float *out, size_t ld_out,
+                              size_t batch, size_t n, void *stream);
+
+/* loadEmbeddingRow (src/generate.zig:3653-3663) for a batch of token ids over an fp16 table. */
+int glacier_cuda_embedding_f16(const uint16_t *table, size_t vocab, size_t dim, const int32_t *tokens,
+                               size_t batch, float *out, void *stream);
+
+/* RopeTable.apply (src/generate.zig:816-831) + PagedKVCache.appendRowTxn
+ * (src/paged_kv_cache.zig:1074-1103), fused: qkv[b] = [q | k | v] (+ bias); q and k are
+ * rotated with the cos/sin table rows at pos[b]; q goes to q_out, k and v to the page
+ * block_tables[b][pos/16], row pos%16, of `layer` (payload offset
+ * ((layer*2+kind)*16+row)*kv_dim, paged_kv_cache.zig:1421-1442).  bias may be NULL. */
+int glacier_cuda_qkv_rope_append_f32(const float *qkv, size_t ld, const float *bias, const float *cos_table,
+                                     const float *sin_table, size_t positions, const int32_t *pos,
+                                     size_t batch, size_t num_heads, size_t num_kv_heads, size_t head_dim,
+                                     float *q_out, size_t ldq, float *kv_pages, size_t page_floats,
+                                     const int32_t *block_tables, size_t max_pages, size_t layer,
+                                     void *stream);
+
+/* ------------------------------------------------------------------------
+ * (d) paged-KV decode attention.
+ * ---------------------------------------------------------------------- */
+
+/* attentionMultiHead (src/paged_attention.zig:108-216) for one query row per lane: q [lanes,
+ * num_heads*head_dim]; lane b attends over positions 0..ctx_lens[b]-1 of `layer`.
+ * workspace: glacier_cuda_paged_attention_workspace() floats of device memory. */
+size_t glacier_cuda_paged_attention_workspace(size_t lanes, size_t num_heads, size_t num_kv_heads,
+                                              size_t head_dim, size_t max_ctx);
+int glacier_cuda_paged_attention_f32(const float *q, const float *kv_pages, size_t page_floats,
+                                     const int32_t *block_tables, size_t max_pages, const int32_t *ctx_lens,
+                                     size_t max_ctx, size_t lanes, size_t layer, size_t num_heads,
+                                     size_t num_kv_heads, size_t head_dim, float *out, float *workspace,
+                                     size_t workspace_floats, void *stream);
+
+/* ------------------------------------------------------------------------
+ * (e) on-device greedy selection.
+ * ---------------------------------------------------------------------- */
+
+/* argmaxEligible (src/sampling.zig:55-107) per row of logits [batch, n]; words NULL means
+ * every row is eligible (sampling.zig:194-207 greedy argmax).  words: [batch][ceil(n/64)]
+ * u64 bitsets on device.  Per row: tokens[b] = winner or -1, status[b] = 0,
+ * GLACIER_CUDA_EMASK or GLACIER_CUDA_ENAN; results[b] (may be NULL) gets the 24-byte
+ * record of int4_neon.c:8-19.  workspace: glacier_cuda_argmax_workspace() bytes. */
+size_t glacier_cuda_argmax_workspace(size_t batch, size_t n);
+int glacier_cuda_argmax_eligible_f32(const float *logits, size_t batch, size_t n, const uint64_t *words,
+                                     size_t word_count, int32_t *tokens, int32_t *status,
+                                     glacier_argmax_result *results, void *workspace, size_t workspace_bytes,
+                                     void *stream);
+
+/* ------------------------------------------------------------------------
+ * Persistent model, paged KV pool and the batched decode step.  Replaces the
+ * compute of generate.zig forwardLayerCached (:1511-1967) + the decode loop
+ * (:5366-5450) + projectLmHead (:3665), and decode_lane4.generate's per-wave
+ * compute (src/decode_lane4.zig:4155) for any lane count.  Weight upload
+ * mirrors glacier_metal_int4_weight_create (src/backends/metal/backend.zig:571-595):
+ * host bytes in, device-resident handle out.
+ * ---------------------------------------------------------------------- */
+
+typedef struct glacier_cuda_model_config {
+  uint32_t num_layers, dim, hidden, num_heads, num_kv_heads, head_dim, vocab, group_size;
+  float rms_eps, rope_theta;
+  uint32_t max_positions; /* RoPE table rows (generate.zig:4964) = longest context */
+  uint32_t scales_f16;    /* 1: fp16 scale mirror (int4_weights.zig:348-358), 0: keep fp32 */
+} glacier_cuda_model_config;
+
+enum glacier_cuda_tensor_kind {
+  GLACIER_CUDA_W_Q = 0, GLACIER_CUDA_W_K, GLACIER_CUDA_W_V, GLACIER_CUDA_W_O,
+  GLACIER_CUDA_W_GATE, GLACIER_CUDA_W_UP, GLACIER_CUDA_W_DOWN, GLACIER_CUDA_W_LM_HEAD,
+  GLACIER_CUDA_B_Q, GLACIER_CUDA_B_K, GLACIER_CUDA_B_V,
+  GLACIER_CUDA_N_INPUT, GLACIER_CUDA_N_POST_ATTN, GLACIER_CUDA_N_FINAL
+};
+
+typedef struct glacier_cuda_model glacier_cuda_model;
+typedef struct glacier_cuda_kv glacier_cuda_kv;
+
+/* Creates an empty model on the current device; NULL on error. */
+glacier_cuda_model *glacier_cuda_model_create(const glacier_cuda_model_config *cfg);
+void glacier_cuda_model_destroy(glacier_cuda_model *model);
+
+/* One INT4 matrix in Int4WeightData form (src/int4_weights.zig:79-107): packed row-major
+ * codes and one f32 scale per group.  layer -1 with GLACIER_CUDA_W_LM_HEAD. */
+int glacier_cuda_model_load_int4(glacier_cuda_model *model, int layer, int kind, const uint8_t *packed,
+                                 size_t packed_bytes, const float *scales, size_t scale_count);
+
+/* Same from a quantized page payload (src/model/qio.zig:73-113 encodePage layout). */
+int glacier_cuda_model_load_qio(glacier_cuda_model *model, int layer, int kind, const uint8_t *payload,
+                                size_t payload_bytes);
+
+/* q/k/v biases, input / post-attention norms (layer >= 0) and the final norm (layer -1). */
+int glacier_cuda_model_load_f32(glacier_cuda_model *model, int layer, int kind, const float *data,
+                                size_t count);
+
+/* Token embedding table [vocab, dim] as IEEE binary16 bit patterns. */
+int glacier_cuda_model_load_embedding_f16(glacier_cuda_model *model, const uint16_t *table, size_t count);
+
+/* Checks that every tensor is present and prepares the kernels' descriptors. */
+int glacier_cuda_model_finalize(glacier_cuda_model *model);
+
+/* Reserves the step workspace for up to max_lanes lanes of max_pages pages each; a decode
+ * step then allocates nothing (graph-capturable). */
+int glacier_cuda_model_reserve(glacier_cuda_model *model, size_t max_lanes, size_t max_pages);
+
+/* FP32 paged KV pool: num_pages pages of [num_layers][K|V][16][kv_dim] floats
+ * (src/paged_kv_cache.zig:1421-1442), so host checkpoint / restore copies pages verbatim. */
+glacier_cuda_kv *glacier_cuda_kv_create(const glacier_cuda_model *model, size_t num_pages);
+void glacier_cuda_kv_destroy(glacier_cuda_kv *kv);
+float *glacier_cuda_kv_pages(glacier_cuda_kv *kv);
+size_t glacier_cuda_kv_page_floats(const glacier_cuda_kv *kv);
+
+/* One greedy decode step for `lanes` independent requests (device buffers): lane b feeds
+ * tokens[b] at position positions[b] (its K/V row is written there; context = positions[b]+1)
+ * through block_tables[b][0..max_pages).  eligible (NULL = all tokens) holds
+ * ceil(vocab/64) words per lane.  tokens_out[b] = next token or -1; status_out[b] (may be
+ * NULL) = 0 / GLACIER_CUDA_EMASK / GLACIER_CUDA_ENAN; logits_out [lanes, vocab] may be NULL. */
+int glacier_cuda_decode_step(glacier_cuda_model *model, glacier_cuda_kv *kv, size_t lanes,
+                             const int32_t *tokens, const int32_t *positions, const int32_t *block_tables,
+                             size_t max_pages, const uint64_t *eligible, size_t eligible_words,
+                             int32_t *tokens_out, int32_t *status_out, float *logits_out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
