@@ -1,0 +1,387 @@
+"""Benchmark: INT4 decode of the Qwen2.5-7B-shaped synthetic model on B200.
+
+Workload (the metric's 7B shape at batch 64): 64 decode
+lanes per GPU, contexts drawn uniformly from [256, 4096], greedy decoding.  One
+step = one decode step of every lane (64 new tokens per GPU).  Weights are
+random-initialised in the reference's INT4 g32 packing (no checkpoint exists
+here); KV pages are pre-filled with random values (FP32, the reference's KV
+format) so that each lane starts at its drawn context length.  The working set
+(4.0 GB of weights + KV) is far larger than the 126 MB L2, so no flush is
+needed between steps.
+
+  python bench.py [--gpus N --steps K --warmup W]          this implementation
+  python bench.py --impl reference [...]                     the reference's CPU
+                                                             path (C oracle port)
+Multi-GPU: one process per GPU (torchrun); lanes are partitioned by GPU with a
+full weight replica each and no collective on the data path (weak scaling).
+Rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "glacier-engine_b200"))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+
+METRIC = "INT4 decode tok/s and achieved HBM GB/s (Qwen2.5-7B shape, batch 1 and 64)"
+UNIT = "tok/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["glacier", "reference"], default="glacier")
+    ap.add_argument("--lanes", type=int, default=64)
+    ap.add_argument("--model", default="qwen2.5-7b")
+    ap.add_argument("--ctx-min", type=int, default=256)
+    ap.add_argument("--ctx-max", type=int, default=4096)
+    ap.add_argument("--seed", type=int, default=2024)
+    ap.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the timed CPU baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# helpers
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms while running."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def lane_contexts(args, lanes: int, rank: int) -> np.ndarray:
+    rng = np.random.default_rng(args.seed + 1000 * rank)
+    return rng.integers(args.ctx_min, args.ctx_max + 1, size=lanes).astype(np.int32)
+
+
+def cpu_threads() -> int:
+    try:
+        return max(1, min(16, len(os.sched_getaffinity(0))))
+    except AttributeError:
+        return max(1, min(16, os.cpu_count() or 1))
+
+
+def time_cpu_oracle(model, ctxs, args, budget_s: float, max_tokens: int | None = None) -> dict:
+    """Greedy decode on the C oracle (the reference's portable FP32 path restated),
+    one lane at a time at its drawn context, with the reference's row-split
+    threading over all host cores.  Returns tokens/s over the sample."""
+    import oracle
+    threads = cpu_threads()
+    c = model.cfg
+    kv_dim = c["num_kv_heads"] * c["head_dim"]
+    om = oracle.OracleModel(model, rope_positions=int(max(ctxs)) + 64, threads=threads)
+    pf = om.page_floats()
+    rng = np.random.default_rng(args.seed + 7)
+    tokens = 0
+    t_total = 0.0
+    lane = 0
+    while True:
+        ctx = int(ctxs[lane % len(ctxs)])
+        pages = -(-(ctx + 1) // 16)
+        pool = rng.standard_normal(pages * pf, dtype=np.float32)
+        bt = np.arange(pages, dtype=np.int32)
+        tok = int(rng.integers(0, c["vocab"]))
+        t0 = time.perf_counter()
+        logits, _ = om.decode_token(pool, bt, ctx, tok)
+        oracle.argmax(logits)
+        t_total += time.perf_counter() - t0
+        tokens += 1
+        lane += 1
+        if (max_tokens is not None and tokens >= max_tokens) or (max_tokens is None and t_total >= budget_s):
+            break
+    return {"value": tokens / t_total, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{tokens} greedy tokens of single lanes at their drawn contexts "
+                      f"(mean ctx {int(np.mean(ctxs[:max(1, min(tokens, len(ctxs)))]))}), full "
+                      f"{c['num_layers']}-layer model + LM head, {kv_dim}-float KV rows",
+            "seconds": t_total}
+
+
+def dist_setup():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+# ---------------------------------------------------------------------------
+# reference arm
+# ---------------------------------------------------------------------------
+
+def run_reference(args):
+    ws, rank, _ = dist_setup()
+    if rank != 0:
+        return
+    from glacier_b200.model import PRESETS, SyntheticModel
+    cfg = PRESETS[args.model]
+    model = SyntheticModel(cfg, seed=args.seed)
+    ctxs = lane_contexts(args, args.lanes, 0)
+    # warmup steps (untimed), then K timed steps; a step is one lane-token.
+    time_cpu_oracle(model, ctxs, args, 0, max_tokens=max(1, args.warmup))
+    r = time_cpu_oracle(model, ctxs, args, 0, max_tokens=max(1, args.steps))
+    line = {
+        "impl": "reference", "metric": METRIC, "value": r["value"], "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 / r["value"], "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "7B decode, 64 lanes, ctx U[256,4096], greedy (config 5); reference step = "
+                               "one lane-token on the host cores", "model": args.model, "lanes": args.lanes},
+        "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": r["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# this implementation
+# ---------------------------------------------------------------------------
+
+def run_glacier(args):
+    import torch
+    from glacier_b200 import _lib
+    from glacier_b200.model import PRESETS, DecodeSession, DeviceModel, SyntheticModel
+
+    ws, rank, local = dist_setup()
+    torch.cuda.set_device(local)
+    if ws > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    cfg = PRESETS[args.model]
+    lanes = args.lanes
+    ctxs = lane_contexts(args, lanes, rank)
+    total_steps = args.warmup + 2 * args.steps + 4
+    max_pages = -(-(int(ctxs.max()) + total_steps + 1) // 16)
+
+    t0 = time.time()
+    model = SyntheticModel(cfg, seed=args.seed)
+    dm = DeviceModel(model, max_positions=max_pages * 16)
+    sess = DecodeSession(dm, lanes, max_pages)
+    # KV: every lane's pages filled with random FP32 rows (equivalent to having
+    # prefilled its context; decode cost depends only on the context length).
+    g = torch.Generator(device="cuda")
+    g.manual_seed(args.seed + rank)
+    pages = sess.pages()
+    for i in range(0, pages.shape[0], 256):
+        pages[i:i + 256].normal_(generator=g)
+    setup_s = time.time() - t0
+
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream()
+    tokens = torch.randint(0, cfg.vocab, (lanes,), dtype=torch.int32, device=dev)
+    positions = torch.from_numpy(ctxs).to(dev)
+    sess.tokens.copy_(tokens)
+    sess.positions.copy_(positions)
+
+    def device_step():
+        out = sess.step()
+        sess.tokens.copy_(out)
+        sess.positions.add_(1)
+
+    for _ in range(args.warmup):
+        device_step()
+    torch.cuda.synchronize()
+    if ws > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    launches0 = _lib.lib().glacier_cuda_launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            device_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    launches = _lib.lib().glacier_cuda_launch_count() - launches0
+    dev_ms = e0.elapsed_time(e1)
+    status = sess.status.cpu().numpy()
+    assert (status == 0).all(), f"decode status {status}"
+    assert _lib.lib().glacier_cuda_device_status(0) == 0
+
+    # e2e: host-side runtime loop through the C ABI with pinned host buffers;
+    # each step copies its inputs in and the new token ids out.
+    h_tok = torch.empty(lanes, dtype=torch.int32, pin_memory=True)
+    h_pos = torch.empty(lanes, dtype=torch.int32, pin_memory=True)
+    h_out = torch.empty(lanes, dtype=torch.int32, pin_memory=True)
+    h_tok.copy_(sess.tokens.cpu())
+    h_pos.copy_(sess.positions.cpu())
+    torch.cuda.synchronize()
+    if ws > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    t_e2e0 = time.perf_counter()
+    for _ in range(args.steps):
+        sess.tokens.copy_(h_tok, non_blocking=True)
+        sess.positions.copy_(h_pos, non_blocking=True)
+        out = sess.step()
+        h_out.copy_(out, non_blocking=True)
+        stream.synchronize()
+        h_tok.copy_(h_out)
+        h_pos.add_(1)
+    torch.cuda.synchronize()
+    e2e_s = time.perf_counter() - t_e2e0
+
+    # Dominant-kernel timing pass: the INT4 GEMV of the largest matrix (LM head)
+    # and the attention kernel, each timed with CUDA events on its stream.
+    dom = dominant_kernel_timing(torch, dm, sess, cfg, lanes, stream)
+
+    times = torch.tensor([dev_ms, e2e_s * 1e3], dtype=torch.float64, device=dev)
+    if ws > 1:
+        torch.distributed.all_reduce(times, op=torch.distributed.ReduceOp.MAX)
+    dev_ms, e2e_ms = float(times[0]), float(times[1])
+    tokens_total = lanes * args.steps * ws
+    value = tokens_total / (dev_ms / 1e3)
+    e2e_value = tokens_total / (e2e_ms / 1e3)
+
+    if rank == 0:
+        cpu = None
+        if not args.no_cpu_baseline:
+            r = time_cpu_oracle(model, ctxs, args, args.cpu_seconds)
+            cpu = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        kv_bytes = int(np.sum(ctxs + args.warmup + args.steps // 2)) * cfg.num_layers * 2 * cfg.kv_dim * 4
+        step_bytes = cfg.int4_bytes_per_token() + kv_bytes / 1  # weights once per step + every lane's KV
+        peaks = load_peaks()
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": dev_ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32 activations / int4 g32 weights (fp16 scales) / f32 KV", "data": "synthetic",
+            "config": {"workload": "7B decode, 64 lanes per GPU, ctx U[256,4096], greedy (BASELINE config 5)",
+                       "model": args.model, "lanes_per_gpu": lanes, "mean_ctx": float(np.mean(ctxs)),
+                       "parallelism": f"lane partition x{ws} (weights replicated, no collective)",
+                       "l2": "working set (weights 4.0 GB + KV) >> 126 MB L2; no flush needed",
+                       "setup_seconds": round(setup_s, 1)},
+            "achieved_step_gbs": step_bytes / (dev_ms / args.steps / 1e3) / 1e9,
+            "roofline": dom["roofline"],
+            "kernels": dom["kernels"],
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 2 * lanes * 4,
+                    "d2h_bytes_per_step": lanes * 4},
+            "gpu_launches": int(launches),
+            "clocks": clk.summary(),
+            "peaks_source": peaks.get("_source"),
+        }
+        print(json.dumps(line), flush=True)
+    sess.close()
+    dm.close()
+    if ws > 1:
+        torch.distributed.destroy_process_group()
+
+
+def load_peaks() -> dict:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        d = json.load(open(p))
+        d["_source"] = "measured (MEASURED_PEAKS.json)"
+        return d
+    except (OSError, ValueError):
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "_source": "fallback"}
+
+
+def dominant_kernel_timing(torch, dm, sess, cfg, lanes, stream) -> dict:
+    """Times the step's heaviest kernels in isolation with CUDA events on the launching stream."""
+    from glacier_b200 import ops
+    from glacier_b200.model import random_int4
+    peaks = load_peaks()
+    hbm = float(peaks["hbm_gbs"])
+    out = {"kernels": {}, "roofline": None}
+    # INT4 GEMV of the fused gate+up matrix (the largest per-layer matrix) at
+    # batch 1 and at the step's batch, on rotating weight copies (> L2).
+    rng = np.random.default_rng(5)
+    M, K = 2 * cfg.hidden, cfg.dim
+    packed, scales = random_int4(rng, M, K, 32)
+    copies = 4
+    Ws = [torch.from_numpy(packed).cuda() for _ in range(copies)]
+    Ss = [torch.from_numpy(scales.astype(np.float16)).cuda() for _ in range(copies)]
+    for b in (1, lanes):
+        x = torch.randn(b, K, device="cuda")
+        y = torch.empty(b, M, device="cuda")
+        for i in range(3):
+            ops.linear_int4_on_the_fly(x, Ws[i % copies], Ss[i % copies], M, K, 32, out=y, stream=stream)
+        n = 12
+        e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+        e0.record(stream)
+        for i in range(n):
+            ops.linear_int4_on_the_fly(x, Ws[i % copies], Ss[i % copies], M, K, 32, out=y, stream=stream)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        t = e0.elapsed_time(e1) / n / 1e3
+        byt = M * K // 2 + M * K // 32 * 2 + b * K * 4 + b * M * 4
+        out["kernels"][f"int4_linear_{M}x{K}_b{b}"] = {"us": t * 1e6, "algorithmic_bytes": byt,
+                                                       "gbs": byt / t / 1e9}
+    k1 = out["kernels"][f"int4_linear_{M}x{K}_b1"]
+    out["roofline"] = {"bound": "hbm", "kernel": f"int4 dequant GEMV {M}x{K} g32, batch 1",
+                       "achieved": k1["gbs"], "peak": hbm, "unit": "GB/s", "frac": k1["gbs"] / hbm,
+                       "traffic": None, "peak_source": peaks.get("_source")}
+    return out
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_glacier(args)
+
+
+if __name__ == "__main__":
+    main()

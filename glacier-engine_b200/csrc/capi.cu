@@ -1,6 +1,7 @@
 // extern "C" entry points of libglacier_cuda.so (declared in include/glacier_cuda.h).
 #include <stdarg.h>
 
+#include <atomic>
 #include <mutex>
 #include <vector>
 
@@ -9,6 +10,9 @@
 namespace glacier {
 
 static thread_local char g_last_error[512] = "";
+static std::atomic<unsigned long long> g_launches{0};
+
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 int set_error(int code, const char* fmt, ...) {
   va_list ap;
@@ -105,6 +109,8 @@ extern "C" {
 const char* glacier_cuda_last_error(void) { return g_last_error; }
 
 int glacier_cuda_version(void) { return (0 << 16) | 1; }
+
+unsigned long long glacier_cuda_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 int glacier_cuda_device_status(int clear) {
   GLC_CHECK_CUDA(cudaDeviceSynchronize());

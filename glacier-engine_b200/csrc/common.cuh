@@ -31,8 +31,15 @@ int set_error(int code, const char* fmt, ...);
     if (!(cond)) return ::glacier::set_error(GLACIER_CUDA_EINVAL, __VA_ARGS__);     \
   } while (0)
 
+// Counts every kernel this library launches (process-wide, all devices).
+void note_launch();
+
 // Launch-error check after a kernel launch (no device synchronisation).
-#define GLC_CHECK_LAUNCH() GLC_CHECK_CUDA(cudaGetLastError())
+#define GLC_CHECK_LAUNCH()      \
+  do {                          \
+    ::glacier::note_launch();   \
+    GLC_CHECK_CUDA(cudaGetLastError()); \
+  } while (0)
 
 __host__ __device__ inline size_t ceil_div(size_t a, size_t b) { return (a + b - 1) / b; }
 

@@ -212,6 +212,7 @@ cudaError_t launch_fast(const float* x, size_t ldx, const uint8_t* packed, const
   else
     gemv_int4_kernel<B, R, KS, ScaleT, 4><<<grid, 256, 0, stream>>>(x, ldx, packed, scales, scale_stride,
                                                                      bias, y, ldy, M, K, gs);
+  note_launch();
   return cudaGetLastError();
 }
 

@@ -321,6 +321,7 @@ int launch_gemv_tc(const Int4Weight& w, const float* x, size_t ldx, size_t batch
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   GLC_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, w.tmap_w, w.tmap_s, prm));
+  note_launch();
   return GLACIER_CUDA_OK;
 }
 

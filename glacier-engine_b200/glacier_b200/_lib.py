@@ -36,6 +36,7 @@ SIGNATURES = {
     "glacier_cuda_last_error": ([], C.c_char_p),
     "glacier_cuda_version": ([], i32),
     "glacier_cuda_device_status": ([i32], i32),
+    "glacier_cuda_launch_count": ([], C.c_ulonglong),
     "glacier_cuda_int4_matvec_f32": ([vp, vp, vp, vp, vp, sz, sz, sz, vp], i32),
     "glacier_cuda_int4_matvec_f16scale": ([vp, vp, vp, vp, vp, sz, sz, sz, vp], i32),
     "glacier_cuda_int4_linear": ([vp, sz, vp, vp, i32, vp, vp, sz, sz, sz, vp], i32),

@@ -54,6 +54,9 @@ const char *glacier_cuda_last_error(void);
 /* Library ABI version (major << 16 | minor). */
 int glacier_cuda_version(void);
 
+/* Number of kernels this library has launched in this process (all devices). */
+unsigned long long glacier_cuda_launch_count(void);
+
 /* Device-side status word of the current device: 0 = ok, 1 = a kernel gave up
  * a bounded wait (its outputs are invalid).  Synchronises the device.  clear != 0
  * resets the word.  No reference counterpart: the reference's CPU kernels
