@@ -100,6 +100,17 @@ int argmax_rows(const float* logits, size_t ld, size_t batch, size_t n, const ui
                 glacier_argmax_result* out, int32_t* tokens, int32_t* status, void* workspace, size_t ws_bytes,
                 cudaStream_t stream);
 
+size_t gemm_split_bytes(size_t np, size_t K);
+bool gemm_tc_supported(const Int4Weight& w);
+int split_activation(const float* x, size_t ldx, size_t n, size_t K, size_t np, __half* xs, float* xscale,
+                     cudaStream_t stream);
+int encode_split_map(CUtensorMap* map, const __half* xs, size_t np, size_t K);
+int gemm_int4_tc(const Int4Weight& w, const CUtensorMap& xmap, const float* xscale, size_t n, size_t np, float* y,
+                 size_t ldy, int nsplit, size_t split_stride, const float* bias, cudaStream_t stream);
+int gemm_device_error(int clear);
+int gemm_splits(size_t M, size_t K);
+int reduce_splits(const float* part, size_t split_stride, int nsplit, float* y, size_t n, cudaStream_t stream);
+
 }  // namespace glacier
 
 using namespace glacier;
@@ -114,9 +125,9 @@ unsigned long long glacier_cuda_launch_count(void) { return g_launches.load(std:
 
 int glacier_cuda_device_status(int clear) {
   GLC_CHECK_CUDA(cudaDeviceSynchronize());
-  const int v = gemv_device_error(clear), w = ops_device_error(clear);
-  if (v < 0 || w < 0) return set_error(GLACIER_CUDA_ECUDA, "device status read failed");
-  return v ? v : (w ? 2 : 0);
+  const int v = gemv_device_error(clear), w = ops_device_error(clear), g = gemm_device_error(clear);
+  if (v < 0 || w < 0 || g < 0) return set_error(GLACIER_CUDA_ECUDA, "device status read failed");
+  return (v || g) ? 1 : (w ? 2 : 0);
 }
 
 int glacier_cuda_int4_matvec_f32(const float* x, const uint8_t* packed, const float* scales,
@@ -144,6 +155,51 @@ int glacier_cuda_int4_linear(const float* x, size_t batch, const uint8_t* packed
                              out_features, out_features, in_features, group_size, (cudaStream_t)stream);
   return gemv_int4<float>(x, in_features, batch, packed, static_cast<const float*>(scales), 0, bias, y,
                           out_features, out_features, in_features, group_size, (cudaStream_t)stream);
+}
+
+static size_t matmul_ws_bytes(size_t batch, size_t in_features, size_t out_features) {
+  const size_t np = ceil_div(batch < 16 ? 16 : batch, 16) * 16;
+  const int ns = gemm_splits(out_features, in_features);
+  const size_t part = ns > 1 ? (size_t)ns * batch * out_features * sizeof(float) : 0;
+  return ceil_div(gemm_split_bytes(np, in_features), 256) * 256 + part;
+}
+
+size_t glacier_cuda_int4_matmul_workspace(size_t batch, size_t in_features, size_t out_features) {
+  return matmul_ws_bytes(batch, in_features, out_features);
+}
+
+int glacier_cuda_int4_matmul_f16scale(const float* x, size_t batch, const uint8_t* packed, const uint16_t* scales,
+                                      const float* bias, float* y, size_t out_features, size_t in_features,
+                                      size_t group_size, void* workspace, size_t workspace_bytes, void* stream) {
+  GLC_REQUIRE(x && packed && scales && y && batch > 0, "int4_matmul: null or empty argument");
+  Int4Weight w;
+  w.packed = packed;
+  w.scales = scales;
+  w.f16 = true;
+  w.M = out_features;
+  w.K = in_features;
+  w.group = group_size;
+  int rc = int4_weight_prepare(w);
+  if (rc) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (!gemm_tc_supported(w) || batch > 128)
+    return int4_linear(w, x, in_features, batch, bias, y, out_features, st);
+  const size_t np = ceil_div(batch < 16 ? 16 : batch, 16) * 16;
+  const size_t need = matmul_ws_bytes(batch, in_features, out_features);
+  GLC_REQUIRE(workspace && workspace_bytes >= need, "int4_matmul: workspace of %zu bytes needed", need);
+  __half* xs = static_cast<__half*>(workspace);
+  float* xscale = reinterpret_cast<float*>(xs + 2 * np * in_features);
+  GLC_CHECK_CUDA(cudaMemsetAsync(xs, 0, 2 * np * in_features * sizeof(__half), st));
+  if ((rc = split_activation(x, in_features, batch, in_features, np, xs, xscale, st))) return rc;
+  CUtensorMap map;
+  if ((rc = encode_split_map(&map, xs, np, in_features))) return rc;
+  const int ns = gemm_splits(out_features, in_features);
+  if (ns == 1) return gemm_int4_tc(w, map, xscale, batch, np, y, out_features, 1, 0, bias, st);
+  float* part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) +
+                                         ceil_div(gemm_split_bytes(np, in_features), 256) * 256);
+  const size_t stride = batch * out_features;
+  if ((rc = gemm_int4_tc(w, map, xscale, batch, np, part, out_features, ns, stride, bias, st))) return rc;
+  return reduce_splits(part, stride, ns, y, stride, st);
 }
 
 int glacier_cuda_rmsnorm_f32(const float* x, const float* weight, float eps, float* out, size_t batch, size_t dim,

@@ -52,6 +52,15 @@ int argmax_rows(const float* logits, size_t ld, size_t batch, size_t n, const ui
                 glacier_argmax_result* out, int32_t* tokens, int32_t* status, void* workspace, size_t ws_bytes,
                 cudaStream_t stream);
 
+size_t gemm_split_bytes(size_t np, size_t K);
+bool gemm_tc_supported(const Int4Weight& w);
+int split_activation(const float* x, size_t ldx, size_t n, size_t K, size_t np, __half* xs, float* xscale,
+                     cudaStream_t stream);
+int encode_split_map(CUtensorMap* map, const __half* xs, size_t np, size_t K);
+int gemm_splits(size_t M, size_t K);
+int gemm_int4_tc(const Int4Weight& w, const CUtensorMap& xmap, const float* xscale, size_t n, size_t np, float* y,
+                 size_t ldy, int nsplit, size_t split_stride, const float* bias, cudaStream_t stream);
+
 namespace {
 
 __global__ void ctx_from_pos_kernel(const int32_t* __restrict__ pos, int32_t* __restrict__ ctx, int n) {
@@ -181,6 +190,12 @@ struct glacier_cuda_model {
   DevBuf x, hn, qkv, q, attn, proj, gu, act, down, logits, ctx, att_ws, arg_ws, status;
   size_t att_floats = 0, arg_bytes = 0;
   int att_chunk = 0;
+  // Tensor-core GEMM mode (more than 4 lanes): activations in split fp16 form.
+  bool gemm = false;
+  size_t np = 0;
+  DevBuf xs_d, xs_q, xs_f, xscale;
+  CUtensorMap map_d, map_q, map_f;
+  int split_qkv = 1, split_o = 1, split_d = 1;
 };
 
 struct glacier_cuda_kv {
@@ -437,6 +452,30 @@ int glacier_cuda_model_reserve(glacier_cuda_model* m, size_t max_lanes, size_t m
     return rc;
   m->max_lanes = max_lanes;
   m->max_pages = max_pages;
+  m->gemm = max_lanes > 4 && gemm_tc_supported(m->layers[0]->qkv.w) && gemm_tc_supported(m->layers[0]->o.w) &&
+            gemm_tc_supported(m->layers[0]->d.w) && gemm_tc_supported(m->lm.w);
+  if (m->gemm) {
+    GLC_REQUIRE(max_lanes <= 128, "model_reserve: at most 128 lanes per GPU in tensor-core mode");
+    const size_t np = ceil_div(max_lanes, 16) * 16;
+    m->np = np;
+    m->split_qkv = gemm_splits(m->qkv_dim, c.dim);
+    m->split_o = gemm_splits(c.dim, m->q_dim);
+    m->split_d = gemm_splits(c.dim, c.hidden);
+    if ((rc = m->xs_d.alloc(gemm_split_bytes(np, c.dim))) || (rc = m->xs_q.alloc(gemm_split_bytes(np, m->q_dim))) ||
+        (rc = m->xs_f.alloc(gemm_split_bytes(np, c.hidden))) || (rc = m->xscale.alloc(np * 4)) ||
+        (rc = m->qkv.alloc((size_t)m->split_qkv * L * m->qkv_dim * 4)) ||
+        (rc = m->proj.alloc((size_t)m->split_o * L * c.dim * 4)) ||
+        (rc = m->down.alloc((size_t)m->split_d * L * c.dim * 4)))
+      return rc;
+    // Padding rows of the split activations stay zero.
+    GLC_CHECK_CUDA(cudaMemset(m->xs_d.p, 0, m->xs_d.bytes));
+    GLC_CHECK_CUDA(cudaMemset(m->xs_q.p, 0, m->xs_q.bytes));
+    GLC_CHECK_CUDA(cudaMemset(m->xs_f.p, 0, m->xs_f.bytes));
+    if ((rc = encode_split_map(&m->map_d, m->xs_d.as<__half>(), np, c.dim)) ||
+        (rc = encode_split_map(&m->map_q, m->xs_q.as<__half>(), np, m->q_dim)) ||
+        (rc = encode_split_map(&m->map_f, m->xs_f.as<__half>(), np, c.hidden)))
+      return rc;
+  }
   return GLACIER_CUDA_OK;
 }
 
@@ -486,36 +525,44 @@ int glacier_cuda_decode_step(glacier_cuda_model* m, glacier_cuda_kv* kv, size_t 
   ctx_from_pos_kernel<<<(unsigned)ceil_div(B, 128), 128, 0, st>>>(positions, m->ctx.as<int32_t>(), (int)B);
   GLC_CHECK_LAUNCH();
   if ((rc = embed_gather(m->embedding.as<__half>(), c.vocab, D, tokens, B, x, D, st))) return rc;
+  // One projection: GEMV (up to 4 lanes) or split activation + tensor-core GEMM.
+  auto project = [&](const Int4Weight& w, const float* xin, size_t K, DevBuf& xs, const CUtensorMap& map, float* y,
+                     size_t ldy, int nsplit) -> int {
+    if (!m->gemm) return int4_linear(w, xin, K, B, nullptr, y, ldy, st);
+    int r = split_activation(xin, K, B, K, m->np, xs.as<__half>(), m->xscale.as<float>(), st);
+    if (r) return r;
+    return gemm_int4_tc(w, map, m->xscale.as<float>(), B, m->np, y, ldy, nsplit, B * ldy, nullptr, st);
+  };
+  const int sq = m->gemm ? m->split_qkv : 1, so = m->gemm ? m->split_o : 1, sd = m->gemm ? m->split_d : 1;
   for (size_t l = 0; l < c.num_layers; ++l) {
     Layer& L = *m->layers[l];
-    // x (+ previous layer's down projection) -> residual x, normed hn
-    if ((rc = add_rmsnorm(x, D, l ? m->down.as<float>() : nullptr, D, 0, l ? 1 : 0, x, D, L.in_norm.as<float>(),
+    // x (+ previous layer's down projection, its split-K partials summed in order) -> x, normed hn
+    if ((rc = add_rmsnorm(x, D, l ? m->down.as<float>() : nullptr, D, B * D, l ? sd : 0, x, D, L.in_norm.as<float>(),
                           c.rms_eps, hn, D, B, D, st)))
       return rc;
-    if ((rc = int4_linear(L.qkv.w, hn, D, B, nullptr, m->qkv.as<float>(), m->qkv_dim, st))) return rc;
-    if ((rc = qkv_rope_append(m->qkv.as<float>(), m->qkv_dim, 0, 1, L.bqkv.as<float>(), m->rope_cos.as<float>(),
-                              m->rope_sin.as<float>(), c.max_positions, positions, B, c.num_heads, c.num_kv_heads,
-                              c.head_dim, m->q.as<float>(), m->q_dim, kv->pool.as<float>(), kv->page_floats,
-                              block_tables, max_pages, l, st)))
+    if ((rc = project(L.qkv.w, hn, D, m->xs_d, m->map_d, m->qkv.as<float>(), m->qkv_dim, sq))) return rc;
+    if ((rc = qkv_rope_append(m->qkv.as<float>(), m->qkv_dim, B * m->qkv_dim, sq, L.bqkv.as<float>(),
+                              m->rope_cos.as<float>(), m->rope_sin.as<float>(), c.max_positions, positions, B,
+                              c.num_heads, c.num_kv_heads, c.head_dim, m->q.as<float>(), m->q_dim,
+                              kv->pool.as<float>(), kv->page_floats, block_tables, max_pages, l, st)))
       return rc;
     if ((rc = paged_attention(m->q.as<float>(), m->q_dim, kv->pool.as<float>(), kv->page_floats, block_tables,
                               max_pages, m->ctx.as<int32_t>(), max_ctx, B, l, c.num_heads, c.num_kv_heads, c.head_dim,
-                              m->attn.as<float>(), m->q_dim, m->att_ws.as<float>(), m->att_floats,
-                              m->att_chunk, st)))
+                              m->attn.as<float>(), m->q_dim, m->att_ws.as<float>(), m->att_floats, m->att_chunk, st)))
       return rc;
-    if ((rc = int4_linear(L.o.w, m->attn.as<float>(), m->q_dim, B, nullptr, m->proj.as<float>(), D, st))) return rc;
-    if ((rc = add_rmsnorm(x, D, m->proj.as<float>(), D, 0, 1, x, D, L.post_norm.as<float>(), c.rms_eps, hn, D, B,
+    if ((rc = project(L.o.w, m->attn.as<float>(), m->q_dim, m->xs_q, m->map_q, m->proj.as<float>(), D, so))) return rc;
+    if ((rc = add_rmsnorm(x, D, m->proj.as<float>(), D, B * D, so, x, D, L.post_norm.as<float>(), c.rms_eps, hn, D, B,
                           D, st)))
       return rc;
-    if ((rc = int4_linear(L.gu.w, hn, D, B, nullptr, m->gu.as<float>(), 2 * F, st))) return rc;
+    if ((rc = project(L.gu.w, hn, D, m->xs_d, m->map_d, m->gu.as<float>(), 2 * F, 1))) return rc;
     if ((rc = silu_mul(m->gu.as<float>(), m->gu.as<float>() + F, 2 * F, m->act.as<float>(), F, B, F, st))) return rc;
-    if ((rc = int4_linear(L.d.w, m->act.as<float>(), F, B, nullptr, m->down.as<float>(), D, st))) return rc;
+    if ((rc = project(L.d.w, m->act.as<float>(), F, m->xs_f, m->map_f, m->down.as<float>(), D, sd))) return rc;
   }
-  if ((rc = add_rmsnorm(x, D, m->down.as<float>(), D, 0, 1, x, D, m->final_norm.as<float>(), c.rms_eps, hn, D, B, D,
-                        st)))
+  if ((rc = add_rmsnorm(x, D, m->down.as<float>(), D, B * D, sd, x, D, m->final_norm.as<float>(), c.rms_eps, hn, D,
+                        B, D, st)))
     return rc;
   float* logits = logits_out ? logits_out : m->logits.as<float>();
-  if ((rc = int4_linear(m->lm.w, hn, D, B, nullptr, logits, c.vocab, st))) return rc;
+  if ((rc = project(m->lm.w, hn, D, m->xs_d, m->map_d, logits, c.vocab, 1))) return rc;
   return argmax_rows(logits, c.vocab, B, c.vocab, eligible, eligible_words, nullptr, tokens_out,
                      status_out ? status_out : m->status.as<int32_t>(), m->arg_ws.p, m->arg_bytes, st);
 }

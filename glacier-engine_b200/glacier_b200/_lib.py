@@ -40,6 +40,8 @@ SIGNATURES = {
     "glacier_cuda_int4_matvec_f32": ([vp, vp, vp, vp, vp, sz, sz, sz, vp], i32),
     "glacier_cuda_int4_matvec_f16scale": ([vp, vp, vp, vp, vp, sz, sz, sz, vp], i32),
     "glacier_cuda_int4_linear": ([vp, sz, vp, vp, i32, vp, vp, sz, sz, sz, vp], i32),
+    "glacier_cuda_int4_matmul_workspace": ([sz, sz, sz], sz),
+    "glacier_cuda_int4_matmul_f16scale": ([vp, sz, vp, vp, vp, vp, sz, sz, sz, vp, sz, vp], i32),
     "glacier_cuda_rmsnorm_f32": ([vp, vp, f32, vp, sz, sz, vp], i32),
     "glacier_cuda_add_rmsnorm_f32": ([vp, vp, vp, vp, f32, vp, sz, sz, vp], i32),
     "glacier_cuda_silu_mul_f32": ([vp, vp, sz, vp, sz, sz, sz, vp], i32),

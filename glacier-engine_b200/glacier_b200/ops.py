@@ -38,6 +38,20 @@ def linear_int4_on_the_fly(x: torch.Tensor, packed: torch.Tensor, scales: torch.
     return out
 
 
+def linear_int4_tensor_core(x: torch.Tensor, packed: torch.Tensor, scales_f16: torch.Tensor, out_f: int,
+                            in_f: int, group: int, bias: torch.Tensor | None = None, out=None, stream=None):
+    """Batched linearInt4OnTheFly on the tcgen05 dequant GEMM (int4_neon.c:1439 M4 GEMM role)."""
+    from ._lib import lib
+    x = x.reshape(-1, in_f)
+    b = x.shape[0]
+    out = torch.empty((b, out_f), dtype=torch.float32, device=x.device) if out is None else out
+    ws_n = lib().glacier_cuda_int4_matmul_workspace(b, in_f, out_f)
+    ws = torch.empty(ws_n, dtype=torch.uint8, device=x.device)
+    call("glacier_cuda_int4_matmul_f16scale", x.data_ptr(), b, packed.data_ptr(), scales_f16.data_ptr(), _ptr(bias),
+         out.data_ptr(), out_f, in_f, group, ws.data_ptr(), ws_n, _stream(stream))
+    return out
+
+
 def rms_norm_f32(x: torch.Tensor, weight: torch.Tensor, eps: float, out=None, stream=None):
     """kernels.zig:141 rmsNormF32 over rows of x [batch, dim]."""
     b, d = x.shape

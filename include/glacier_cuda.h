@@ -92,6 +92,19 @@ int glacier_cuda_int4_linear(const float *x, size_t batch, const uint8_t *packed
                              size_t out_features, size_t in_features, size_t group_size,
                              void *stream);
 
+/* (b) Batched form on the tensor cores (tcgen05/TMEM dequant GEMM): x [batch, in_f] fp32,
+ * y [batch, out_f]; the reference's M4 weight-stationary GEMM
+ * (glacier_int4_gemm_neon_q8_prequant_f16scale_rows4_k16_m4, src/decode_lane4.zig:221-264,
+ * int4_neon.c:1439-1621) generalised to batch <= 128 with FP32-activation numerics.
+ * scales: fp16 bit patterns [out_f, in_f/32]; group_size must be 32 and in_f a multiple
+ * of 256 for the tensor-core path (other shapes run the GEMV kernels).
+ * workspace: glacier_cuda_int4_matmul_workspace(batch, in_f, out_f) bytes of device memory. */
+size_t glacier_cuda_int4_matmul_workspace(size_t batch, size_t in_features, size_t out_features);
+int glacier_cuda_int4_matmul_f16scale(const float *x, size_t batch, const uint8_t *packed,
+                                      const uint16_t *scales, const float *bias, float *y,
+                                      size_t out_features, size_t in_features, size_t group_size,
+                                      void *workspace, size_t workspace_bytes, void *stream);
+
 /* ------------------------------------------------------------------------
  * (c) fused norm / rotary / activation steps, on device buffers.
  * ---------------------------------------------------------------------- */

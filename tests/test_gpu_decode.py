@@ -78,3 +78,10 @@ def test_decode_05b_head_geometry_batch5():
     # five lanes: the tensor-core GEMV runs as a 4-row launch plus a 1-row launch
     cfg = ModelConfig(num_layers=1, dim=896, hidden=1024, num_heads=14, num_kv_heads=2, head_dim=64, vocab=1536)
     assert run_parity(cfg, lanes=5, prompt_len=3, new_tokens=3) >= 10
+
+
+def test_decode_tensor_core_mode_16_lanes():
+    from glacier_b200.model import ModelConfig
+    # more than 4 lanes: every projection runs the tcgen05 GEMM with split-K partials
+    cfg = ModelConfig(num_layers=2, dim=512, hidden=1024, num_heads=28, num_kv_heads=4, head_dim=128, vocab=2048)
+    assert run_parity(cfg, lanes=16, prompt_len=4, new_tokens=3) >= 30

@@ -1,0 +1,38 @@
+"""Kernel (b): tcgen05/TMEM INT4 dequant GEMM on the GPU vs the CPU oracle."""
+import numpy as np
+import pytest
+
+import oracle
+from helpers import REL_TOL, max_rel_err, synthetic_int4
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+@pytest.mark.parametrize("out_f,in_f,batch", [
+    (256, 512, 16),      # one tile, single split
+    (1000, 2048, 17),    # row tail, padded batch
+    (512, 1024, 5),
+    (4608, 3584, 64),    # 7B fused QKV at 64 lanes
+    (3584, 18944, 64),   # 7B down projection
+    (256, 512, 128),     # widest batch tile
+])
+def test_gemm_matches_oracle(out_f, in_f, batch):
+    from glacier_b200 import _lib, ops
+    rng = np.random.default_rng(out_f + in_f + batch)
+    packed, s32, s16 = synthetic_int4(rng, out_f, in_f, 32)
+    x = rng.standard_normal((batch, in_f), dtype=np.float32)
+    x[1] *= 1e-3   # per-row scaling of the split activation
+    x[2] *= 300.0
+    bias = rng.standard_normal(out_f, dtype=np.float32) * 0.1
+    y = ops.linear_int4_tensor_core(dev(x), dev(packed), dev(s16.view(np.int16)), out_f, in_f, 32, bias=dev(bias))
+    torch.cuda.synchronize()
+    assert _lib.lib().glacier_cuda_device_status(1) == 0
+    ref = oracle.linear_int4(x, packed, s32, out_f, in_f, 32, bias=bias, threads=8)
+    y = y.cpu().numpy()
+    for b in range(batch):
+        assert max_rel_err(y[b], ref[b]) <= REL_TOL, b
