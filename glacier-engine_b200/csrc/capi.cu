@@ -79,9 +79,9 @@ int gemv_device_error(int clear);
 int ops_device_error(int clear);
 int add_rmsnorm(const float* a, size_t lda, const float* b, size_t ldb, size_t b_split_stride, int nb,
                 float* residual, size_t ldr, const float* w, float eps, float* out, size_t ldo, size_t batch,
-                size_t dim, cudaStream_t stream);
+                size_t dim, cudaStream_t stream, SplitOut so = SplitOut());
 int silu_mul(const float* gate, const float* up, size_t ld_in, float* out, size_t ld_out, size_t batch, size_t n,
-             cudaStream_t stream);
+             cudaStream_t stream, SplitOut so = SplitOut());
 int embed_gather(const __half* table, size_t vocab, size_t dim, const int32_t* tokens, size_t batch, float* out,
                  size_t ldo, cudaStream_t stream);
 int qkv_rope_append(const float* qkv, size_t ld, size_t split_stride, int nsplit, const float* bias,
@@ -94,7 +94,7 @@ int attention_chunk(size_t lanes, size_t num_kv_heads, size_t max_ctx);
 int paged_attention(const float* q, size_t ldq, const float* pool, size_t page_floats, const int32_t* block_tables,
                     size_t max_pages, const int32_t* ctx_lens, size_t max_ctx, size_t lanes, size_t layer,
                     size_t num_heads, size_t num_kv_heads, size_t head_dim, float* out, size_t ldo, float* workspace,
-                    size_t workspace_floats, int chunk, cudaStream_t stream);
+                    size_t workspace_floats, int chunk, cudaStream_t stream, SplitOut so = SplitOut());
 size_t argmax_workspace_bytes(size_t batch, size_t n);
 int argmax_rows(const float* logits, size_t ld, size_t batch, size_t n, const uint64_t* words, size_t word_count,
                 glacier_argmax_result* out, int32_t* tokens, int32_t* status, void* workspace, size_t ws_bytes,

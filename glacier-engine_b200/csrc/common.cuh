@@ -75,8 +75,15 @@ int int4_weight_prepare(Int4Weight& w);
 int int4_linear(const Int4Weight& w, const float* x, size_t ldx, size_t batch, const float* bias, float* y,
                 size_t ldy, cudaStream_t stream);
 
-// Wall-clock limit for every bounded spin-wait in device code (nanoseconds).
-constexpr unsigned long long kSpinLimitNs = 2000000000ull;
+// Destination of an activation block that feeds the tensor-core GEMM: rows of
+// fp16 hi / lo parts ([2*np, K]: hi rows 0..np-1, lo rows np..2np-1) in the
+// per-8 code order (0,4,1,5,2,6,3,7), plus one power-of-two scale per row
+// (x = scale * (hi + lo)).  xs == nullptr selects a plain fp32 destination.
+struct SplitOut {
+  __half* xs = nullptr;
+  float* xscale = nullptr;
+  int np = 0;
+};
 
 // Device-side error words (written by kernels that give up waiting).
 enum DeviceError : int { kErrNone = 0, kErrTimeout = 1 };
@@ -150,25 +157,30 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
+// try_wait with a suspend-time hint: a waiting thread sleeps in hardware until
+// the phase completes (or ~1 ms passes) instead of spinning on the issue port.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
       : "memory");
   return ok != 0;
 }
 // Bounded wait: returns false (and raises *err) when the phase does not
-// complete within kSpinLimitNs.
+// complete within kSpinLimitCycles SM clock cycles (about two seconds); the
+// cycle counter is checked every 8 (hardware-suspended) polls.
+constexpr long long kSpinLimitCycles = 4000000000ll;
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
   if (mbar_try_wait(bar, parity)) return true;
-  const unsigned long long t0 = globaltimer_ns();
-  while (true) {
+  const long long t0 = clock64();
+#pragma unroll 1
+  for (int it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer_ns() - t0 > kSpinLimitNs) {
+    if ((it & 7) == 0 && clock64() - t0 > kSpinLimitCycles) {
       if (err) atomicExch(err, kErrTimeout);
       return false;
     }
@@ -206,6 +218,34 @@ __device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
   float v;
   asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
   return v;
+}
+
+__device__ __forceinline__ uint32_t cluster_nctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
+}
+
+// Power-of-two scale s with max|x| / s in [2^14, 2^15) (1 for an all-zero row).
+__device__ __forceinline__ float split_scale(float m) {
+  if (!(m > 0.f) || !isfinite(m)) return 1.f;
+  int e;
+  frexpf(m, &e);
+  return ldexpf(1.f, e - 15);
+}
+
+// Writes 8 consecutive values (k = base..base+7 of row r) in split form.
+__device__ __forceinline__ void store_split8(const SplitOut& so, int r, size_t K, size_t base, const float (&v)[8],
+                                             float inv_scale) {
+  __half h[8], l[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float x = v[(i & 1) ? 4 + (i >> 1) : (i >> 1)] * inv_scale;  // order (0,4,1,5,2,6,3,7)
+    h[i] = __float2half_rn(x);
+    l[i] = __float2half_rn(x - __half2float(h[i]));
+  }
+  *reinterpret_cast<uint4*>(so.xs + (size_t)r * K + base) = *reinterpret_cast<uint4*>(h);
+  *reinterpret_cast<uint4*>(so.xs + ((size_t)so.np + r) * K + base) = *reinterpret_cast<uint4*>(l);
 }
 
 // Scale loads: the library keeps fp16 scale mirrors (as the reference's

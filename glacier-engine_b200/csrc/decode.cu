@@ -31,9 +31,9 @@ namespace glacier {
 
 int add_rmsnorm(const float* a, size_t lda, const float* b, size_t ldb, size_t b_split_stride, int nb,
                 float* residual, size_t ldr, const float* w, float eps, float* out, size_t ldo, size_t batch,
-                size_t dim, cudaStream_t stream);
+                size_t dim, cudaStream_t stream, SplitOut so = SplitOut());
 int silu_mul(const float* gate, const float* up, size_t ld_in, float* out, size_t ld_out, size_t batch, size_t n,
-             cudaStream_t stream);
+             cudaStream_t stream, SplitOut so = SplitOut());
 int embed_gather(const __half* table, size_t vocab, size_t dim, const int32_t* tokens, size_t batch, float* out,
                  size_t ldo, cudaStream_t stream);
 int qkv_rope_append(const float* qkv, size_t ld, size_t split_stride, int nsplit, const float* bias,
@@ -46,7 +46,7 @@ int attention_chunk(size_t lanes, size_t num_kv_heads, size_t max_ctx);
 int paged_attention(const float* q, size_t ldq, const float* pool, size_t page_floats, const int32_t* block_tables,
                     size_t max_pages, const int32_t* ctx_lens, size_t max_ctx, size_t lanes, size_t layer,
                     size_t num_heads, size_t num_kv_heads, size_t head_dim, float* out, size_t ldo, float* workspace,
-                    size_t workspace_floats, int chunk, cudaStream_t stream);
+                    size_t workspace_floats, int chunk, cudaStream_t stream, SplitOut so = SplitOut());
 size_t argmax_workspace_bytes(size_t batch, size_t n);
 int argmax_rows(const float* logits, size_t ld, size_t batch, size_t n, const uint64_t* words, size_t word_count,
                 glacier_argmax_result* out, int32_t* tokens, int32_t* status, void* workspace, size_t ws_bytes,
@@ -462,7 +462,7 @@ int glacier_cuda_model_reserve(glacier_cuda_model* m, size_t max_lanes, size_t m
     m->split_o = gemm_splits(c.dim, m->q_dim);
     m->split_d = gemm_splits(c.dim, c.hidden);
     if ((rc = m->xs_d.alloc(gemm_split_bytes(np, c.dim))) || (rc = m->xs_q.alloc(gemm_split_bytes(np, m->q_dim))) ||
-        (rc = m->xs_f.alloc(gemm_split_bytes(np, c.hidden))) || (rc = m->xscale.alloc(np * 4)) ||
+        (rc = m->xs_f.alloc(gemm_split_bytes(np, c.hidden))) ||
         (rc = m->qkv.alloc((size_t)m->split_qkv * L * m->qkv_dim * 4)) ||
         (rc = m->proj.alloc((size_t)m->split_o * L * c.dim * 4)) ||
         (rc = m->down.alloc((size_t)m->split_d * L * c.dim * 4)))
@@ -525,22 +525,32 @@ int glacier_cuda_decode_step(glacier_cuda_model* m, glacier_cuda_kv* kv, size_t 
   ctx_from_pos_kernel<<<(unsigned)ceil_div(B, 128), 128, 0, st>>>(positions, m->ctx.as<int32_t>(), (int)B);
   GLC_CHECK_LAUNCH();
   if ((rc = embed_gather(m->embedding.as<__half>(), c.vocab, D, tokens, B, x, D, st))) return rc;
-  // One projection: GEMV (up to 4 lanes) or split activation + tensor-core GEMM.
-  auto project = [&](const Int4Weight& w, const float* xin, size_t K, DevBuf& xs, const CUtensorMap& map, float* y,
-                     size_t ldy, int nsplit) -> int {
-    if (!m->gemm) return int4_linear(w, xin, K, B, nullptr, y, ldy, st);
-    int r = split_activation(xin, K, B, K, m->np, xs.as<__half>(), m->xscale.as<float>(), st);
-    if (r) return r;
-    return gemm_int4_tc(w, map, m->xscale.as<float>(), B, m->np, y, ldy, nsplit, B * ldy, nullptr, st);
+  // Split-form destinations of the GEMM inputs (tensor-core mode only).
+  auto split_of = [&](DevBuf& xs, size_t K) {
+    SplitOut so;
+    if (m->gemm) {
+      so.xs = xs.as<__half>();
+      so.xscale = reinterpret_cast<float*>(so.xs + 2 * m->np * K);
+      so.np = (int)m->np;
+    }
+    return so;
   };
-  const int sq = m->gemm ? m->split_qkv : 1, so = m->gemm ? m->split_o : 1, sd = m->gemm ? m->split_d : 1;
+  const SplitOut so_d = split_of(m->xs_d, D), so_q = split_of(m->xs_q, m->q_dim), so_f = split_of(m->xs_f, F);
+  // One projection: GEMV on fp32 activations (up to 4 lanes) or the tensor-core
+  // GEMM on the split activations its producer wrote.
+  auto project = [&](const Int4Weight& w, const float* xin, size_t K, const SplitOut& so, const CUtensorMap& map,
+                     float* y, size_t ldy, int nsplit) -> int {
+    if (!m->gemm) return int4_linear(w, xin, K, B, nullptr, y, ldy, st);
+    return gemm_int4_tc(w, map, so.xscale, B, m->np, y, ldy, nsplit, B * ldy, nullptr, st);
+  };
+  const int sq = m->gemm ? m->split_qkv : 1, so_ = m->gemm ? m->split_o : 1, sd = m->gemm ? m->split_d : 1;
   for (size_t l = 0; l < c.num_layers; ++l) {
     Layer& L = *m->layers[l];
     // x (+ previous layer's down projection, its split-K partials summed in order) -> x, normed hn
     if ((rc = add_rmsnorm(x, D, l ? m->down.as<float>() : nullptr, D, B * D, l ? sd : 0, x, D, L.in_norm.as<float>(),
-                          c.rms_eps, hn, D, B, D, st)))
+                          c.rms_eps, m->gemm ? nullptr : hn, D, B, D, st, so_d)))
       return rc;
-    if ((rc = project(L.qkv.w, hn, D, m->xs_d, m->map_d, m->qkv.as<float>(), m->qkv_dim, sq))) return rc;
+    if ((rc = project(L.qkv.w, hn, D, so_d, m->map_d, m->qkv.as<float>(), m->qkv_dim, sq))) return rc;
     if ((rc = qkv_rope_append(m->qkv.as<float>(), m->qkv_dim, B * m->qkv_dim, sq, L.bqkv.as<float>(),
                               m->rope_cos.as<float>(), m->rope_sin.as<float>(), c.max_positions, positions, B,
                               c.num_heads, c.num_kv_heads, c.head_dim, m->q.as<float>(), m->q_dim,
@@ -548,21 +558,24 @@ int glacier_cuda_decode_step(glacier_cuda_model* m, glacier_cuda_kv* kv, size_t 
       return rc;
     if ((rc = paged_attention(m->q.as<float>(), m->q_dim, kv->pool.as<float>(), kv->page_floats, block_tables,
                               max_pages, m->ctx.as<int32_t>(), max_ctx, B, l, c.num_heads, c.num_kv_heads, c.head_dim,
-                              m->attn.as<float>(), m->q_dim, m->att_ws.as<float>(), m->att_floats, m->att_chunk, st)))
+                              m->gemm ? nullptr : m->attn.as<float>(), m->q_dim, m->att_ws.as<float>(), m->att_floats,
+                              m->att_chunk, st, so_q)))
       return rc;
-    if ((rc = project(L.o.w, m->attn.as<float>(), m->q_dim, m->xs_q, m->map_q, m->proj.as<float>(), D, so))) return rc;
-    if ((rc = add_rmsnorm(x, D, m->proj.as<float>(), D, B * D, so, x, D, L.post_norm.as<float>(), c.rms_eps, hn, D, B,
-                          D, st)))
+    if ((rc = project(L.o.w, m->attn.as<float>(), m->q_dim, so_q, m->map_q, m->proj.as<float>(), D, so_))) return rc;
+    if ((rc = add_rmsnorm(x, D, m->proj.as<float>(), D, B * D, so_, x, D, L.post_norm.as<float>(), c.rms_eps,
+                          m->gemm ? nullptr : hn, D, B, D, st, so_d)))
       return rc;
-    if ((rc = project(L.gu.w, hn, D, m->xs_d, m->map_d, m->gu.as<float>(), 2 * F, 1))) return rc;
-    if ((rc = silu_mul(m->gu.as<float>(), m->gu.as<float>() + F, 2 * F, m->act.as<float>(), F, B, F, st))) return rc;
-    if ((rc = project(L.d.w, m->act.as<float>(), F, m->xs_f, m->map_f, m->down.as<float>(), D, sd))) return rc;
+    if ((rc = project(L.gu.w, hn, D, so_d, m->map_d, m->gu.as<float>(), 2 * F, 1))) return rc;
+    if ((rc = silu_mul(m->gu.as<float>(), m->gu.as<float>() + F, 2 * F, m->gemm ? nullptr : m->act.as<float>(), F, B,
+                       F, st, so_f)))
+      return rc;
+    if ((rc = project(L.d.w, m->act.as<float>(), F, so_f, m->map_f, m->down.as<float>(), D, sd))) return rc;
   }
-  if ((rc = add_rmsnorm(x, D, m->down.as<float>(), D, B * D, sd, x, D, m->final_norm.as<float>(), c.rms_eps, hn, D,
-                        B, D, st)))
+  if ((rc = add_rmsnorm(x, D, m->down.as<float>(), D, B * D, sd, x, D, m->final_norm.as<float>(), c.rms_eps,
+                        m->gemm ? nullptr : hn, D, B, D, st, so_d)))
     return rc;
   float* logits = logits_out ? logits_out : m->logits.as<float>();
-  if ((rc = project(m->lm.w, hn, D, m->xs_d, m->map_d, logits, c.vocab, 1))) return rc;
+  if ((rc = project(m->lm.w, hn, D, so_d, m->map_d, logits, c.vocab, 1))) return rc;
   return argmax_rows(logits, c.vocab, B, c.vocab, eligible, eligible_words, nullptr, tokens_out,
                      status_out ? status_out : m->status.as<int32_t>(), m->arg_ws.p, m->arg_bytes, st);
 }

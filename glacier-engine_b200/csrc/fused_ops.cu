@@ -32,37 +32,138 @@ __device__ __forceinline__ float block_sum(float v, float* sh) {
   return sh[0];
 }
 
-// One CTA per row.  x = a (+ sum of nb partial rows of b, in order) ; the sum
-// is written to `residual` when given; out = x * (1/sqrt(mean(x^2)+eps)) * w.
-// The rows are held in shared memory between the two passes.
+// Reduces one float per CTA across the cluster (in rank order) through
+// distributed shared memory.  `slot` is this CTA's shared word.
+__device__ __forceinline__ float cluster_sum(float* slot, float v) {
+  if (threadIdx.x == 0) *slot = v;
+  cluster_sync_all();
+  const uint32_t n = cluster_nctarank();
+  const uint32_t a = smem_u32(slot);
+  float t = 0.f;
+  for (uint32_t q = 0; q < n; ++q) t += ld_dsmem_f32(mapa_shared(a, q));
+  return t;
+}
+__device__ __forceinline__ float cluster_max(float* slot, float v) {
+  if (threadIdx.x == 0) *slot = v;
+  cluster_sync_all();
+  const uint32_t n = cluster_nctarank();
+  const uint32_t a = smem_u32(slot);
+  float t = 0.f;
+  for (uint32_t q = 0; q < n; ++q) t = fmaxf(t, ld_dsmem_f32(mapa_shared(a, q)));
+  return t;
+}
+
+__device__ __forceinline__ float block_max(float v, float* sh) {
+  v = warp_max(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) sh[w] = v;
+  __syncthreads();
+  const int nw = blockDim.x >> 5;
+  float t = (threadIdx.x < nw) ? sh[threadIdx.x] : 0.f;
+  if (w == 0) t = warp_max(t);
+  if (threadIdx.x == 0) sh[0] = t;
+  __syncthreads();
+  return sh[0];
+}
+
+// A cluster of CTAs per row (blockIdx.y = row, cluster rank = slice of the row):
+// x = a (+ the nb split-K partial rows of b, summed in split order); the sum
+// goes to `residual` when given; out = x * (1/sqrt(mean(x^2)+eps)) * w, written
+// as fp32 or in split form.  The sum of squares (and for split outputs the row
+// max) is combined across the cluster through distributed shared memory.
 __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(
     const float* __restrict__ a, size_t lda, const float* __restrict__ b, size_t ldb, size_t b_split_stride,
     int nb, float* __restrict__ residual, size_t ldr, const float* __restrict__ w, float eps, float* __restrict__ out,
-    size_t ldo, int dim) {
+    size_t ldo, SplitOut so, int dim) {
   extern __shared__ float row[];
   __shared__ float sh[32];
-  const int r = blockIdx.x;
+  __shared__ float xch[2];
+  const int r = blockIdx.y;
+  const int cr = (int)cluster_ctarank(), cn = (int)cluster_nctarank();
+  const int slice = ((dim + cn - 1) / cn + 7) & ~7;
+  const int k0 = min(dim, cr * slice), k1 = min(dim, k0 + slice);
   const float* ar = a + r * lda;
   float ss = 0.f;
-  for (int k = threadIdx.x; k < dim; k += blockDim.x) {
+  for (int k = k0 + threadIdx.x; k < k1; k += blockDim.x) {
     float v = ar[k];
-    // addInto (generate.zig:3642): dst = a + b; split-K partial rows of b are
-    // summed first, in split order.
+    // addInto (generate.zig:3642): dst = a + b, split-K partials summed first.
     if (nb > 0) {
       float bv = b[r * ldb + k];
       for (int s = 1; s < nb; ++s) bv += b[s * b_split_stride + r * ldb + k];
       v = v + bv;
     }
-    row[k] = v;
+    row[k - k0] = v;
     ss = fmaf(v, v, ss);
   }
   ss = block_sum(ss, sh);
-  const float rms = sqrtf(ss / (float)dim + eps);
+  const float total = cluster_sum(&xch[0], ss);
+  const float rms = sqrtf(total / (float)dim + eps);
   const float inv = 1.0f / rms;
-  for (int k = threadIdx.x; k < dim; k += blockDim.x) {
-    const float v = row[k];
+  float m = 0.f;
+  for (int k = k0 + threadIdx.x; k < k1; k += blockDim.x) {
+    const float v = row[k - k0];
     if (residual) residual[r * ldr + k] = v;
-    out[r * ldo + k] = v * inv * w[k];
+    const float o = v * inv * w[k];
+    if (so.xs) {
+      row[k - k0] = o;
+      m = fmaxf(m, fabsf(o));
+    } else {
+      out[r * ldo + k] = o;
+    }
+  }
+  if (so.xs) {
+    m = block_max(m, sh);
+    const float scale = split_scale(cluster_max(&xch[1], m));
+    const float iscale = 1.0f / scale;
+    for (int k8 = k0 / 8 + threadIdx.x; k8 < k1 / 8; k8 += blockDim.x) {
+      float v[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = row[k8 * 8 - k0 + i];
+      store_split8(so, r, dim, (size_t)k8 * 8, v, iscale);
+    }
+    if (cr == 0 && threadIdx.x == 0) so.xscale[r] = scale;
+  }
+  cluster_sync_all();  // peers may still read this CTA's exchange words
+}
+
+// One cluster per row: out = silu(gate) * up (kernels.zig:465-507), as fp32
+// or in split form with the row max combined across the cluster.
+__global__ void __launch_bounds__(kNormThreads) silu_mul_split_kernel(const float* __restrict__ gate,
+                                                                        const float* __restrict__ up, size_t ld_in,
+                                                                        float* __restrict__ out, size_t ld_out,
+                                                                        SplitOut so, int n) {
+  extern __shared__ float row[];
+  __shared__ float sh[32];
+  __shared__ float xch;
+  const int r = blockIdx.y;
+  const int cr = (int)cluster_ctarank(), cn = (int)cluster_nctarank();
+  const int slice = ((n + cn - 1) / cn + 7) & ~7;
+  const int k0 = min(n, cr * slice), k1 = min(n, k0 + slice);
+  float m = 0.f;
+  for (int k = k0 + threadIdx.x; k < k1; k += blockDim.x) {
+    const float g = gate[r * ld_in + k];
+    const float sig = 1.0f / (1.0f + expf(-g));
+    const float h = g * sig * up[r * ld_in + k];
+    if (so.xs) {
+      row[k - k0] = h;
+      m = fmaxf(m, fabsf(h));
+    } else {
+      out[r * ld_out + k] = h;
+    }
+  }
+  if (so.xs) {
+    m = block_max(m, sh);
+    const float scale = split_scale(cluster_max(&xch, m));
+    const float iscale = 1.0f / scale;
+    for (int k8 = k0 / 8 + threadIdx.x; k8 < k1 / 8; k8 += blockDim.x) {
+      float v[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = row[k8 * 8 - k0 + i];
+      store_split8(so, r, n, (size_t)k8 * 8, v, iscale);
+    }
+    if (cr == 0 && threadIdx.x == 0) so.xscale[r] = scale;
+    cluster_sync_all();
   }
 }
 
@@ -106,10 +207,13 @@ __global__ void qkv_rope_append_kernel(const float* __restrict__ qkv, size_t ld,
   const int b = blockIdx.x;
   const int p = pos[b];
   const int half = head_dim >> 1;
+  // blockIdx.y / gridDim.y: this CTA's share of the lane's pairs and v values.
+  const int part = blockIdx.y, nparts = gridDim.y;
+  const int tid = part * blockDim.x + threadIdx.x, nthreads = nparts * blockDim.x;
   const int q_dim = num_heads * head_dim, kv_dim = num_kv_heads * head_dim;
   const int page_idx = p >> 4;
   if (p < 0 || p >= positions || page_idx >= max_pages) {
-    if (threadIdx.x == 0) atomicExch(bad, 1);
+    if (threadIdx.x == 0 && part == 0) atomicExch(bad, 1);
     return;
   }
   const int32_t page = block_tables[b * max_pages + page_idx];
@@ -125,7 +229,7 @@ __global__ void qkv_rope_append_kernel(const float* __restrict__ qkv, size_t ld,
   const float* st = sin_t + (size_t)p * half;
   // Rotated pairs: (head, j) and (head, j + half) for q and k heads.
   const int pairs = (num_heads + num_kv_heads) * half;
-  for (int i = threadIdx.x; i < pairs; i += blockDim.x) {
+  for (int i = tid; i < pairs; i += nthreads) {
     const int hh = i / half, j = i % half;
     const float c = ct[j], s = st[j];
     if (hh < num_heads) {
@@ -141,7 +245,7 @@ __global__ void qkv_rope_append_kernel(const float* __restrict__ qkv, size_t ld,
       kdst[i0 + half] = x0 * s + x1 * c;
     }
   }
-  for (int i = threadIdx.x; i < kv_dim; i += blockDim.x) vdst[i] = val(q_dim + kv_dim + i);
+  for (int i = tid; i < kv_dim; i += nthreads) vdst[i] = val(q_dim + kv_dim + i);
 }
 
 }  // namespace
@@ -164,32 +268,76 @@ static int* ops_err_ptr() {
   return p;
 }
 
+// Cluster size for a row of `dim` values: about 1024 values per CTA, at most 8.
+static int row_cluster(size_t dim) {
+  int c = 1;
+  while (c < 8 && dim / (size_t)(2 * c) >= 1024) c *= 2;
+  return c;
+}
+
+static int launch_row_cluster(const void* kern, void** args, size_t rows, int cl, size_t smem, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)cl, (unsigned)rows);
+  cfg.blockDim = dim3(kNormThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cl;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  GLC_CHECK_CUDA(cudaLaunchKernelExC(&cfg, kern, args));
+  note_launch();
+  return GLACIER_CUDA_OK;
+}
+
 int add_rmsnorm(const float* a, size_t lda, const float* b, size_t ldb, size_t b_split_stride, int nb,
                 float* residual, size_t ldr, const float* w, float eps, float* out, size_t ldo, size_t batch,
-                size_t dim, cudaStream_t stream) {
-  GLC_REQUIRE(a && w && out && batch > 0 && dim > 0, "rmsnorm: empty or null argument");
-  GLC_REQUIRE(dim * sizeof(float) <= 160 * 1024, "rmsnorm: dim %zu too large", dim);
-  const size_t smem = dim * sizeof(float);
+                size_t dim, cudaStream_t stream, SplitOut so) {
+  GLC_REQUIRE(a && w && (out || so.xs) && batch > 0 && dim > 0, "rmsnorm: empty or null argument");
+  GLC_REQUIRE(!so.xs || dim % 8 == 0, "rmsnorm: split output needs dim %% 8 == 0");
+  const int cl = row_cluster(dim);
+  const size_t slice = ((ceil_div(dim, (size_t)cl)) + 7) & ~(size_t)7;
+  const size_t smem = slice * sizeof(float);
+  GLC_REQUIRE(smem <= 160 * 1024, "rmsnorm: dim %zu too large", dim);
   static size_t attr = 0;
   if (smem > 48 * 1024 && attr < smem) {
     const int rc = allow_dynamic_smem((const void*)add_rmsnorm_kernel, (int)smem);
     if (rc) return rc;
     attr = smem;
   }
-  add_rmsnorm_kernel<<<(unsigned)batch, kNormThreads, smem, stream>>>(a, lda, b, ldb, b_split_stride, nb, residual,
-                                                                      ldr, w, eps, out, ldo, (int)dim);
-  GLC_CHECK_LAUNCH();
-  return GLACIER_CUDA_OK;
+  int d = (int)dim;
+  void* args[] = {(void*)&a, &lda, (void*)&b, &ldb, &b_split_stride, &nb, &residual, &ldr, (void*)&w, &eps, &out,
+                  &ldo, &so, &d};
+  return launch_row_cluster((const void*)add_rmsnorm_kernel, args, batch, cl, smem, stream);
 }
 
 int silu_mul(const float* gate, const float* up, size_t ld_in, float* out, size_t ld_out, size_t batch, size_t n,
-             cudaStream_t stream) {
-  GLC_REQUIRE(gate && up && out && batch > 0 && n > 0, "silu_mul: empty or null argument");
-  const size_t total = batch * n;
-  const unsigned grid = (unsigned)std::min<size_t>(ceil_div(total, 256), (size_t)sm_count() * 8);
-  silu_mul_kernel<<<grid, 256, 0, stream>>>(gate, up, ld_in, out, ld_out, (int)n, (int)batch);
-  GLC_CHECK_LAUNCH();
-  return GLACIER_CUDA_OK;
+             cudaStream_t stream, SplitOut so) {
+  GLC_REQUIRE(gate && up && (out || so.xs) && batch > 0 && n > 0, "silu_mul: empty or null argument");
+  GLC_REQUIRE(!so.xs || n % 8 == 0, "silu_mul: split output needs n %% 8 == 0");
+  if (!so.xs) {
+    const size_t total = batch * n;
+    const unsigned grid = (unsigned)std::min<size_t>(ceil_div(total, 256), (size_t)sm_count() * 8);
+    silu_mul_kernel<<<grid, 256, 0, stream>>>(gate, up, ld_in, out, ld_out, (int)n, (int)batch);
+    GLC_CHECK_LAUNCH();
+    return GLACIER_CUDA_OK;
+  }
+  const int cl = row_cluster(n);
+  const size_t slice = ((ceil_div(n, (size_t)cl)) + 7) & ~(size_t)7;
+  const size_t smem = slice * sizeof(float);
+  GLC_REQUIRE(smem <= 160 * 1024, "silu_mul: row %zu too long", n);
+  static size_t attr = 0;
+  if (smem > 48 * 1024 && attr < smem) {
+    const int rc = allow_dynamic_smem((const void*)silu_mul_split_kernel, (int)smem);
+    if (rc) return rc;
+    attr = smem;
+  }
+  int nn = (int)n;
+  void* args[] = {(void*)&gate, (void*)&up, &ld_in, &out, &ld_out, &so, &nn};
+  return launch_row_cluster((const void*)silu_mul_split_kernel, args, batch, cl, smem, stream);
 }
 
 int embed_gather(const __half* table, size_t vocab, size_t dim, const int32_t* tokens, size_t batch, float* out,
@@ -210,7 +358,7 @@ int qkv_rope_append(const float* qkv, size_t ld, size_t split_stride, int nsplit
               "qkv_rope_append: null argument");
   GLC_REQUIRE(head_dim % 2 == 0 && num_kv_heads > 0 && num_heads % num_kv_heads == 0,
               "qkv_rope_append: bad head geometry");
-  qkv_rope_append_kernel<<<(unsigned)batch, 256, 0, stream>>>(
+  qkv_rope_append_kernel<<<dim3((unsigned)batch, 4), 256, 0, stream>>>(
       qkv, ld, split_stride, nsplit, bias, cos_t, sin_t, (int)positions, pos, (int)num_heads, (int)num_kv_heads,
       (int)head_dim, q_out, ldq, pool, page_floats, block_tables, (int)max_pages, (int)layer, ops_err_ptr());
   GLC_CHECK_LAUNCH();

@@ -23,9 +23,10 @@
 //           128 x 8 scale tiles into a 3-slot ring
 //   warp 1  TMA producer: 64-K activation tiles [Xhi | Xlo] (SWIZZLE_128B)
 //   warp 2  allocates TMEM and issues tcgen05.mma from one thread
-//   warps 3-6 (128 threads, one weight row each) convert nibbles + scales to
-//           the Whi / Wlo tiles in the canonical K-major SWIZZLE_128B layout,
-//           then run the epilogue (tcgen05.ld, xs scaling, coalesced stores).
+//   warps 3-10 (256 threads, two per weight row) convert nibbles + scales to
+//           the -Whi / Wlo tiles in the canonical K-major SWIZZLE_128B layout
+//           (the MMA descriptor negates A back), then run the epilogue
+//           (tcgen05.ld, xs scaling, coalesced stores).
 // Code order inside each 8-code word is permuted to (0,4,1,5,2,6,3,7) by the
 // unpack; the activation split kernel stores X in the same order, so the
 // contraction is unchanged.  Every wait is bounded; no multicast is used.
@@ -40,13 +41,12 @@ namespace {
 constexpr int kRowsTile = 128;
 constexpr int kChunkK = 64;                     // K per MMA stage (one 128-byte swizzle row of fp16)
 constexpr int kSuperK = 256;                    // K per nibble/scale TMA stage
-constexpr int kNibSlots = 3;
-constexpr int kASlots = 2;
-constexpr int kBSlots = 3;
+constexpr int kMaxSlots = 8;                    // ring slots (runtime counts below this)
+constexpr int kConvWarps = 8;                   // two converter threads per weight row
 constexpr int kNibBytes = kRowsTile * 128;      // 128 rows x 256 codes
 constexpr int kSclBytes = kRowsTile * 16;       // 128 rows x 8 fp16 scales
 constexpr int kATileBytes = kRowsTile * 128;    // 128 rows x 64 fp16
-constexpr int kThreads = 7 * 32;
+constexpr int kThreads = (3 + kConvWarps) * 32;
 
 __device__ __forceinline__ uint32_t hfma2_u32(uint32_t a, uint32_t b, uint32_t c) {
   uint32_t d;
@@ -83,9 +83,10 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
   return d;
 }
 
-// Instruction descriptor: kind::f16, A = B = f16, D = f32, both K-major, M = 128.
-__host__ __device__ constexpr uint32_t idesc_f16(int n) {
-  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+// Instruction descriptor: kind::f16, A = B = f16, D = f32, both K-major, M = 128;
+// negate_a flips the sign of A (bit 13).
+__host__ __device__ constexpr uint32_t idesc_f16(int n, bool negate_a = false) {
+  return (1u << 4) | ((negate_a ? 1u : 0u) << 13) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 }
 
 __device__ __forceinline__ void umma_f16(uint32_t dtmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
@@ -123,6 +124,7 @@ struct GemmParams {
   int M, K, n, np;      // weight rows, K, live activation rows, padded rows (multiple of 16)
   int chunks_total;     // ceil(K / 64)
   int chunks_per_split; // multiple of 4
+  int nib_slots, a_slots, b_slots;
   int* err;
 };
 
@@ -133,17 +135,18 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int bbytes = 2 * p.np * 128;  // [Xhi | Xlo] tile: 2*Np rows x 64 fp16
+  const int kNibSlots = p.nib_slots, kASlots = p.a_slots, kBSlots = p.b_slots;
   uint8_t* nib = smem;                                        // kNibSlots x (nibbles + scales)
-  uint8_t* atile = nib + kNibSlots * (kNibBytes + kSclBytes); // kASlots x (Whi + Wlo)
+  uint8_t* atile = nib + kNibSlots * (kNibBytes + kSclBytes); // kASlots x (-Whi, Wlo)
   uint8_t* btile = atile + kASlots * 2 * kATileBytes;         // kBSlots x bbytes
   uint64_t* bars = reinterpret_cast<uint64_t*>(btile + kBSlots * bbytes);
   uint64_t* nib_full = bars;
-  uint64_t* nib_empty = nib_full + kNibSlots;
-  uint64_t* a_full = nib_empty + kNibSlots;
-  uint64_t* a_empty = a_full + kASlots;
-  uint64_t* b_full = a_empty + kASlots;
-  uint64_t* b_empty = b_full + kBSlots;
-  uint64_t* acc_full = b_empty + kBSlots;
+  uint64_t* nib_empty = nib_full + kMaxSlots;
+  uint64_t* a_full = nib_empty + kMaxSlots;
+  uint64_t* a_empty = a_full + kMaxSlots;
+  uint64_t* b_full = a_empty + kMaxSlots;
+  uint64_t* b_empty = b_full + kMaxSlots;
+  uint64_t* acc_full = b_empty + kMaxSlots;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
   __shared__ int s_abort;
 
@@ -159,10 +162,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     s_abort = 0;
     for (int i = 0; i < kNibSlots; ++i) {
       mbar_init(&nib_full[i], 1);
-      mbar_init(&nib_empty[i], 4);
+      mbar_init(&nib_empty[i], kConvWarps);
     }
     for (int i = 0; i < kASlots; ++i) {
-      mbar_init(&a_full[i], 4);
+      mbar_init(&a_full[i], kConvWarps);
       mbar_init(&a_empty[i], 1);
     }
     for (int i = 0; i < kBSlots; ++i) {
@@ -224,7 +227,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
   } else if (warp == 2) {
     // ---- MMA issuer ----
     if (lane == 0 && nch > 0) {
-      const uint32_t id_hl = idesc_f16(2 * p.np), id_h = idesc_f16(p.np);
+      // A holds -Whi (negated back by the descriptor) and Wlo.
+      const uint32_t id_hl = idesc_f16(2 * p.np, true), id_h = idesc_f16(p.np);
       int done = 0;
       for (int i = 0; i < nch; ++i) {
         const int as = i % kASlots, bs = i % kBSlots;
@@ -248,36 +252,37 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
       (void)done;
     }
   } else {
-    // ---- converters (128 threads, one weight row each), then the epilogue ----
-    const int t = threadIdx.x - 3 * 32;  // 0..127 = row within the tile
-    const uint32_t swz = (uint32_t)(t & 7);
-    const int cw = warp - 3;
+    // ---- converters (256 threads: two per weight row, 32 codes each), then the epilogue ----
+    const int t = threadIdx.x - 3 * 32;   // 0..255
+    const int rrow = t & (kRowsTile - 1);  // row within the tile
+    const int hf = t >> 7;                 // which 32-code half of the 64-code chunk
+    const uint32_t swz = (uint32_t)(rrow & 7);
     for (int i = 0; i < nch && !s_abort; ++i) {
       const int sup = i / 4, sub = i % 4;
       const int ns = sup % kNibSlots;
       if (sub == 0 && !mbar_wait(&nib_full[ns], (sup / kNibSlots) & 1, p.err)) { s_abort = 1; break; }
       const int as = i % kASlots;
       if (!mbar_wait(&a_empty[as], ((i / kASlots) & 1) ^ 1, p.err)) { s_abort = 1; break; }
-      const uint8_t* nrow = nib + ns * (kNibBytes + kSclBytes) + t * 128;
-      const uint8_t* srow = nib + ns * (kNibBytes + kSclBytes) + kNibBytes + t * 16;
-      const uint4 g0 = *reinterpret_cast<const uint4*>(nrow + (((uint32_t)(2 * sub) ^ swz) << 4));
-      const uint4 g1 = *reinterpret_cast<const uint4*>(nrow + (((uint32_t)(2 * sub + 1) ^ swz) << 4));
-      const uint32_t sc2 = *reinterpret_cast<const uint32_t*>(srow + 4 * sub);  // {s(2sub), s(2sub+1)}
-      const uint32_t s0 = (sc2 & 0xFFFFu) * 0x10001u, s1 = (sc2 >> 16) * 0x10001u;
-      uint8_t* ahi = atile + as * 2 * kATileBytes + t * 128;
+      const uint8_t* nrow = nib + ns * (kNibBytes + kSclBytes) + rrow * 128;
+      const uint8_t* srow = nib + ns * (kNibBytes + kSclBytes) + kNibBytes + rrow * 16;
+      const int grp = 2 * sub + hf;  // 32-code group within the 256-code super stage
+      const uint4 g = *reinterpret_cast<const uint4*>(nrow + (((uint32_t)grp ^ swz) << 4));
+      const uint32_t sh = *reinterpret_cast<const uint16_t*>(srow + 2 * grp);
+      const uint32_t s2 = sh * 0x10001u;           // {s, s}
+      const uint32_t ns2 = s2 ^ 0x80008000u;       // {-s, -s}
+      uint8_t* ahi = atile + as * 2 * kATileBytes + rrow * 128;
       uint8_t* alo = ahi + kATileBytes;
-      const uint32_t words[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+      const uint32_t words[4] = {g.x, g.y, g.z, g.w};
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < 4; ++j) {
         uint32_t q[4], h[4], l[4];
         unpack8(words[j], q);
-        const uint32_t s = j < 4 ? s0 : s1;
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          h[e] = hmul2_u32(q[e], s);                 // RN(q*s)
-          l[e] = hfma2_u32(q[e], s, neg_half2(h[e]));  // q*s - RN(q*s), exact
+          h[e] = hmul2_u32(q[e], ns2);        // -RN(q*s)
+          l[e] = hfma2_u32(q[e], s2, h[e]);   // q*s - RN(q*s), exact
         }
-        const uint32_t off = ((uint32_t)j ^ swz) << 4;
+        const uint32_t off = ((uint32_t)(4 * hf + j) ^ swz) << 4;
         *reinterpret_cast<uint4*>(ahi + off) = make_uint4(h[0], h[1], h[2], h[3]);
         *reinterpret_cast<uint4*>(alo + off) = make_uint4(l[0], l[1], l[2], l[3]);
       }
@@ -288,14 +293,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
         if (sub == 3 || i == nch - 1) mbar_arrive(&nib_empty[ns]);
       }
     }
-    // Epilogue: TMEM lane = row (this warp's quarter), columns b (hi) and Np + b (lo).
+    // Epilogue: TMEM lane = row (this warp's quarter), columns b (hi) and Np + b (lo);
+    // the two converter warps of a quarter split the column blocks.
+    const int quarter = warp & 3;
+    const int row = row0 + quarter * 32 + lane;
+    float* ybase = p.y + (size_t)split * p.split_stride;
     if (nch > 0 && !s_abort && mbar_wait(acc_full, 0, p.err)) {
       tc_fence_after();
-      const int quarter = warp & 3;
-      const int row = row0 + quarter * 32 + lane;
       const uint32_t tq = tmem + ((uint32_t)(quarter * 32) << 16);
-      float* ybase = p.y + (size_t)split * p.split_stride;
-      for (int b0 = 0; b0 < p.np; b0 += 16) {
+      const int nblk16 = p.np / 16;
+      for (int bi = hf; bi < nblk16; bi += 2) {
+        const int b0 = bi * 16;
         float vh[16], vl[16];
         tmem_ld16(tq + (uint32_t)b0, vh);
         tmem_ld16(tq + (uint32_t)(p.np + b0), vl);
@@ -304,14 +312,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
           for (int j = 0; j < 16; ++j) {
             const int b = b0 + j;
             if (b < p.n)
-              ybase[(size_t)b * p.ldy + row] = (vh[j] + vl[j]) * p.xscale[b] + ((p.bias && split == 0) ? p.bias[row] : 0.f);
+              ybase[(size_t)b * p.ldy + row] =
+                  (vh[j] + vl[j]) * p.xscale[b] + ((p.bias && split == 0) ? p.bias[row] : 0.f);
           }
         }
       }
-    } else if (nch == 0 && cw >= 0) {
-      // Empty K-range: this split contributes zeros.
-      const int row = row0 + t;
-      float* ybase = p.y + (size_t)split * p.split_stride;
+    } else if (nch == 0 && hf == 0) {
+      // Empty K-range: this split contributes zeros (plus the bias on split 0).
       if (row < p.M)
         for (int b = 0; b < p.n; ++b) ybase[(size_t)b * p.ldy + row] = (p.bias && split == 0) ? p.bias[row] : 0.f;
     }
@@ -391,9 +398,29 @@ int encode_split_map(CUtensorMap* map, const __half* xs, size_t np, size_t K) {
                         (uint32_t)(2 * np), CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
 }
 
+// Ring depths for a padded activation width.  The activation ring is the
+// deepest: its tiles come from L2 with ~1 us of TMA latency and each covers only
+// 64 K, so six of them keep the MMA fed; then three nibble stages (768 K of
+// HBM reads in flight) and two converted weight tiles; all within 227 KB.
+static void gemm_slots(size_t np, int* nib, int* a, int* b) {
+  *nib = 3;
+  *a = 4;
+  *b = 6;
+  auto bytes = [&]() {
+    return 1024 + (size_t)*nib * (kNibBytes + kSclBytes) + (size_t)*a * 2 * kATileBytes + (size_t)*b * 2 * np * 128 +
+           (6 * kMaxSlots + 1) * 8 + 16;
+  };
+  while (bytes() > 227 * 1024 && *b > 3) --*b;
+  if (bytes() > 227 * 1024) *nib = 2;
+  while (bytes() > 227 * 1024 && *a > 2) --*a;
+  while (bytes() > 227 * 1024 && *b > 2) --*b;
+}
+
 size_t gemm_smem_bytes(size_t np) {
-  return 1024 + kNibSlots * (kNibBytes + kSclBytes) + kASlots * 2 * kATileBytes + kBSlots * 2 * np * 128 +
-         (2 * kNibSlots + 2 * kASlots + 2 * kBSlots + 1) * 8 + 16;
+  int nib, a, b;
+  gemm_slots(np, &nib, &a, &b);
+  return 1024 + (size_t)nib * (kNibBytes + kSclBytes) + (size_t)a * 2 * kATileBytes + (size_t)b * 2 * np * 128 +
+         (6 * kMaxSlots + 1) * 8 + 16;
 }
 
 // The tensor core's fp32 accumulation does not round every addition, so an
@@ -450,7 +477,10 @@ int gemm_int4_tc(const Int4Weight& w, const CUtensorMap& xmap, const float* xsca
   }
   int* err = nullptr;
   GLC_CHECK_CUDA(cudaGetSymbolAddress((void**)&err, g_gemm_error));
-  GemmParams prm{xscale, bias, y, ldy, split_stride, (int)w.M, (int)w.K, (int)n, (int)np, chunks, per, err};
+  int nib_slots, a_slots, b_slots;
+  gemm_slots(np, &nib_slots, &a_slots, &b_slots);
+  GemmParams prm{xscale, bias, y, ldy, split_stride, (int)w.M, (int)w.K, (int)n, (int)np, chunks, per,
+                 nib_slots, a_slots, b_slots, err};
   dim3 grid((unsigned)ceil_div(w.M, kRowsTile), (unsigned)nsplit);
   gemm_tc_kernel<<<grid, kThreads, smem, stream>>>(w.tmap_w, w.tmap_s, xmap, prm);
   GLC_CHECK_LAUNCH();

@@ -63,7 +63,7 @@ def run_parity(cfg, lanes, prompt_len, new_tokens, seed=7):
 
 def test_decode_small_gqa_model():
     from glacier_b200.model import ModelConfig
-    cfg = ModelConfig(num_layers=2, dim=256, hidden=512, num_heads=8, num_kv_heads=2, head_dim=32, vocab=1000)
+    cfg = ModelConfig(num_layers=2, dim=256, hidden=512, num_heads=8, num_kv_heads=2, head_dim=64, vocab=1000)
     assert run_parity(cfg, lanes=3, prompt_len=20, new_tokens=6) >= 12
 
 

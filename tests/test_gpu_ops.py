@@ -86,7 +86,7 @@ def test_qkv_rope_append_matches_oracle(heads, kv_heads, hd):
     (28, 4, 128, [1, 17, 300, 1100]),   # 7B geometry, ragged lanes across page boundaries
     (14, 2, 64, [512, 513]),            # 0.5B geometry
     (12, 2, 128, [2048]),
-    (4, 4, 32, [33]),                   # no GQA sharing
+    (4, 4, 64, [33]),                   # no GQA sharing
 ])
 def test_paged_attention_matches_oracle(heads, kv_heads, hd, ctxs):
     from glacier_b200 import ops
