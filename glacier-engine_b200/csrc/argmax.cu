@@ -12,6 +12,8 @@
 //
 // Two deterministic passes: per-(row, chunk) partial winners, then a per-row
 // reduction in chunk order.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace glacier {
@@ -158,3 +160,79 @@ int argmax_rows(const float* logits, size_t ld, size_t batch, size_t n, const ui
 }
 
 }  // namespace glacier
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant: glacier_cuda_argmax_eligible_f32_noalloc.
+//
+// Some callers cannot allocate device memory at the point where they pick the
+// next token: a host runtime that budgets every byte of GPU memory when it
+// admits a request, or a plugin that is handed buffers but no allocator.
+// cudaMalloc can also synchronise the device and fail under memory pressure.
+// This entry point therefore takes no workspace. Its partial winners live in
+// one fixed array of device memory that is part of the library image.
+//
+// Limits and sharing:
+//  * the array holds GLACIER_CUDA_ARGMAX_NOALLOC_SCRATCH_BYTES (64 KiB); calls
+//    whose batch and vocabulary need more are rejected before any launch;
+//  * every GPU that loads the library keeps its copy of the array until the
+//    process exits;
+//  * all calls on a device share the one array, so calls that overlap on the
+//    GPU (different streams, or host threads racing) corrupt each other's
+//    partial results. Order them on one stream or serialise them;
+//  * the array keeps the previous call's contents. Nothing needs clearing:
+//    the first pass writes every partial slot that the second pass reads;
+//  * the first call on each device looks up the array's device address
+//    (cudaGetSymbolAddress) with that device current and caches it. Make that
+//    first call before any stream capture begins on the device.
+// ---------------------------------------------------------------------------
+
+static_assert(GLACIER_CUDA_ARGMAX_NOALLOC_SCRATCH_BYTES % 256 == 0, "scratch size must keep 256-byte alignment");
+static __device__ __align__(256) unsigned char g_argmax_scratch[GLACIER_CUDA_ARGMAX_NOALLOC_SCRATCH_BYTES];
+
+namespace glacier {
+namespace {
+
+constexpr int kMaxScratchDevices = 64;
+std::mutex g_scratch_mutex;
+void* g_scratch_address[kMaxScratchDevices];  // device address of g_argmax_scratch, per device
+
+// Host code cannot use g_argmax_scratch's name as a device address: on the
+// host it names a shadow variable. Ask the runtime once per device, with that
+// device current, and cache the answer.
+int scratch_for_current_device(void** out) {
+  int dev = -1;
+  GLC_CHECK_CUDA(cudaGetDevice(&dev));
+  GLC_REQUIRE(dev >= 0 && dev < kMaxScratchDevices, "argmax_noalloc: device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (!g_scratch_address[dev]) {
+    void* p = nullptr;
+    GLC_CHECK_CUDA(cudaGetSymbolAddress(&p, g_argmax_scratch));
+    GLC_REQUIRE(p != nullptr && (reinterpret_cast<uintptr_t>(p) & 255) == 0,
+                "argmax_noalloc: scratch address is not 256-byte aligned");
+    g_scratch_address[dev] = p;
+  }
+  *out = g_scratch_address[dev];
+  return GLACIER_CUDA_OK;
+}
+
+}  // namespace
+
+}  // namespace glacier
+
+extern "C" int glacier_cuda_argmax_eligible_f32_noalloc(const float* logits, size_t batch, size_t n,
+                                                        const uint64_t* words, size_t word_count, int32_t* tokens,
+                                                        int32_t* status, glacier_argmax_result* results,
+                                                        void* stream) {
+  using namespace glacier;
+  GLC_REQUIRE(logits && batch > 0 && n > 0 && n < (1u << 31), "argmax_noalloc: empty or null argument");
+  const size_t need = argmax_workspace_bytes(batch, n);
+  GLC_REQUIRE(need <= GLACIER_CUDA_ARGMAX_NOALLOC_SCRATCH_BYTES,
+              "argmax_noalloc: batch %zu x %zu logits needs %zu bytes of scratch, the fixed scratch holds %d; "
+              "use glacier_cuda_argmax_eligible_f32 with a workspace",
+              batch, n, need, GLACIER_CUDA_ARGMAX_NOALLOC_SCRATCH_BYTES);
+  void* scratch = nullptr;
+  const int rc = scratch_for_current_device(&scratch);
+  if (rc != GLACIER_CUDA_OK) return rc;
+  return argmax_rows(logits, n, batch, n, words, word_count, results, tokens, status, scratch,
+                     GLACIER_CUDA_ARGMAX_NOALLOC_SCRATCH_BYTES, (cudaStream_t)stream);
+}

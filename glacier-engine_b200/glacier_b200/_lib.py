@@ -52,6 +52,7 @@ SIGNATURES = {
     "glacier_cuda_paged_attention_f32": ([vp, vp, sz, vp, sz, vp, sz, sz, sz, sz, sz, sz, vp, vp, sz, vp], i32),
     "glacier_cuda_argmax_workspace": ([sz, sz], sz),
     "glacier_cuda_argmax_eligible_f32": ([vp, sz, sz, vp, sz, vp, vp, vp, vp, sz, vp], i32),
+    "glacier_cuda_argmax_eligible_f32_noalloc": ([vp, sz, sz, vp, sz, vp, vp, vp, vp], i32),
     "glacier_cuda_model_create": ([vp], vp),
     "glacier_cuda_model_destroy": ([vp], None),
     "glacier_cuda_model_load_int4": ([vp, i32, i32, vp, sz, vp, sz], i32),

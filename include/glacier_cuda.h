@@ -169,6 +169,21 @@ int glacier_cuda_argmax_eligible_f32(const float *logits, size_t batch, size_t n
                                      glacier_argmax_result *results, void *workspace, size_t workspace_bytes,
                                      void *stream);
 
+/* Allocation-free form of glacier_cuda_argmax_eligible_f32, for callers that cannot allocate
+ * device memory when they select tokens (a runtime that budgets all GPU memory at admission, a
+ * plugin given buffers but no allocator).  No counterpart in the reference.  Same arguments and
+ * results minus the workspace: partial winners go to a fixed 64 KiB array of device memory inside
+ * the library, so batch * ceil(n/8192) * 16 + 64 must not exceed
+ * GLACIER_CUDA_ARGMAX_NOALLOC_SCRATCH_BYTES (e.g. up to 215 rows of a 152064-token vocabulary);
+ * larger calls return GLACIER_CUDA_EINVAL before any launch.  All calls on a device share the
+ * array: calls that overlap on the GPU race and must be ordered by the caller.  The first call on
+ * a device looks up the array's address with that device current; make it before any stream
+ * capture starts. */
+#define GLACIER_CUDA_ARGMAX_NOALLOC_SCRATCH_BYTES 65536
+int glacier_cuda_argmax_eligible_f32_noalloc(const float *logits, size_t batch, size_t n,
+                                             const uint64_t *words, size_t word_count, int32_t *tokens,
+                                             int32_t *status, glacier_argmax_result *results, void *stream);
+
 /* ------------------------------------------------------------------------
  * Persistent model, paged KV pool and the batched decode step.  Replaces the
  * compute of generate.zig forwardLayerCached (:1511-1967) + the decode loop
