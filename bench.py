@@ -50,6 +50,10 @@ def parse():
     ap.add_argument("--seed", type=int, default=2024)
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the timed CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="build only this many decoder layers (small cases for ncu captures; not a bench number)")
+    ap.add_argument("--profile-steps", type=int, default=10,
+                    help="decode steps of the per-kernel-class event pass that follows the timed region")
     return ap.parse_args()
 
 
@@ -175,7 +179,7 @@ def run_reference(args):
         return
     from glacier_b200.model import PRESETS, SyntheticModel
     cfg = PRESETS[args.model]
-    model = SyntheticModel(cfg, seed=args.seed)
+    model = SyntheticModel(cfg, seed=args.seed, layers=args.layers)
     ctxs = lane_contexts(args, args.lanes, 0)
     # warmup steps (untimed), then K timed steps; a step is one lane-token.
     time_cpu_oracle(model, ctxs, args, 0, max_tokens=max(1, args.warmup))
@@ -210,11 +214,11 @@ def run_glacier(args):
     cfg = PRESETS[args.model]
     lanes = args.lanes
     ctxs = lane_contexts(args, lanes, rank)
-    total_steps = args.warmup + 2 * args.steps + 4
+    total_steps = args.warmup + 2 * args.steps + args.profile_steps + 4
     max_pages = -(-(int(ctxs.max()) + total_steps + 1) // 16)
 
     t0 = time.time()
-    model = SyntheticModel(cfg, seed=args.seed)
+    model = SyntheticModel(cfg, seed=args.seed, layers=args.layers)
     dm = DeviceModel(model, max_positions=max_pages * 16)
     sess = DecodeSession(dm, lanes, max_pages)
     # KV: every lane's pages filled with random FP32 rows (equivalent to having
@@ -247,11 +251,13 @@ def run_glacier(args):
     launches0 = _lib.lib().glacier_cuda_launch_count()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
+        torch.cuda.nvtx.range_push("timed_steps")  # lets a profiler select the timed launches
         e0.record(stream)
         for _ in range(args.steps):
             device_step()
         e1.record(stream)
         torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
     launches = _lib.lib().glacier_cuda_launch_count() - launches0
     dev_ms = e0.elapsed_time(e1)
     status = sess.status.cpu().numpy()
@@ -281,9 +287,10 @@ def run_glacier(args):
     torch.cuda.synchronize()
     e2e_s = time.perf_counter() - t_e2e0
 
-    # Dominant-kernel timing pass: the INT4 GEMV of the largest matrix (LM head)
-    # and the attention kernel, each timed with CUDA events on its stream.
-    dom = dominant_kernel_timing(torch, dm, sess, cfg, lanes, stream)
+    # Per-kernel-class pass: the library records CUDA events on the step's stream
+    # between its kernel classes for a few more steps of the same decode.
+    dom = step_kernel_timing(torch, dm, sess, cfg, lanes, stream, args.profile_steps, device_step)
+    dom["kernels"].update(gemv_batch1_timing(torch, cfg, stream))
 
     times = torch.tensor([dev_ms, e2e_s * 1e3], dtype=torch.float64, device=dev)
     if ws > 1:
@@ -337,42 +344,106 @@ def load_peaks() -> dict:
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "_source": "fallback"}
 
 
-def dominant_kernel_timing(torch, dm, sess, cfg, lanes, stream) -> dict:
-    """Times the step's heaviest kernels in isolation with CUDA events on the launching stream."""
-    from glacier_b200 import ops
-    from glacier_b200.model import random_int4
+# DRAM bytes (dram__bytes_read + write) per algorithmic byte, from one ncu capture of a smaller
+# case of the same kernel (profiles/); traffic scales with the K/V rows a launch reads.
+DRAM_TRAFFIC_RATIO = {
+    "attention": (269.3e6 / 266.1e6, "ncu: 269.3 MB DRAM for 266.1 MB algorithmic (1 layer, 32 lanes, mean ctx "
+                                     "2015), scaled to this launch's K/V bytes; profiles/attn_chunk_128_32lanes.md"),
+}
+
+STEP_KINDS = ("embed", "norm", "proj_qkv", "rope_append", "attention", "attn_combine", "proj_o", "proj_gate_up",
+              "silu", "proj_down", "lm_head", "argmax")  # glacier_cuda_step_kind order
+
+
+def step_kernel_timing(torch, dm, sess, cfg, lanes, stream, steps, device_step) -> dict:
+    """Per-kernel-class device time of `steps` decode steps, from CUDA events that the library
+    records on the step's stream between its kernel classes, plus the roofline of the
+    dominant class.  Algorithmic bytes per launch: INT4 codes (0.5 B) + fp16 scales (2 B per
+    32 weights) + fp32 activations in and out for a projection; every lane's K and V rows
+    (2 * kv_dim * 4 B per context position) + its query for attention; the logits for argmax."""
+    import ctypes as C
+    from glacier_b200 import _lib
+    L = _lib.lib()
     peaks = load_peaks()
     hbm = float(peaks["hbm_gbs"])
-    out = {"kernels": {}, "roofline": None}
-    # INT4 GEMV of the fused gate+up matrix (the largest per-layer matrix) at
-    # batch 1 and at the step's batch, on rotating weight copies (> L2).
+    n = len(STEP_KINDS)
+    ctx_sum = 0
+    _lib.call("glacier_cuda_model_profile", dm.h, 1)
+    for _ in range(steps):
+        ctx_sum += int(sess.positions.sum().item()) + lanes  # context of this step = position + 1
+        device_step()
+    _lib.call("glacier_cuda_model_profile", dm.h, 0)
+    ms = (C.c_double * n)()
+    regions = (C.c_uint64 * n)()
+    _lib.call("glacier_cuda_model_profile_read", dm.h, ms, regions, n)
+    assert L.glacier_cuda_device_status(0) == 0
+    D, F, V = cfg.dim, cfg.hidden, cfg.vocab
+    nl = dm.cfg["num_layers"]
+
+    def proj(M, K):
+        return M * K // 2 + M * (K // 32) * 2 + lanes * K * 4 + lanes * M * 4
+
+    per_launch = {
+        "proj_qkv": proj(cfg.q_dim + 2 * cfg.kv_dim, D), "proj_o": proj(D, cfg.q_dim),
+        "proj_gate_up": proj(2 * F, D), "proj_down": proj(D, F), "lm_head": proj(V, D),
+        "attention": (ctx_sum / steps) * 2 * cfg.kv_dim * 4 + lanes * cfg.q_dim * 4,
+        "argmax": lanes * V * 4,
+    }
+    total_ms = sum(ms[k] for k in range(n))
+    kernels = {}
+    for k, name in enumerate(STEP_KINDS):
+        if regions[k] == 0:
+            continue
+        us = ms[k] / regions[k] * 1e3
+        e = {"us_per_launch": us, "launches_per_step": regions[k] / steps, "share": ms[k] / total_ms}
+        if name in per_launch:
+            e["algorithmic_bytes"] = int(per_launch[name])
+            e["gbs"] = per_launch[name] / (us * 1e-6) / 1e9
+        kernels[name] = e
+    dom_name = max((k for k in kernels if "gbs" in kernels[k]), key=lambda k: kernels[k]["share"])
+    d = kernels[dom_name]
+    what = {"attention": f"paged decode attention (attn_chunk_kernel), one layer, {lanes} lanes, mean ctx "
+                         f"{ctx_sum / steps / lanes:.0f}, {nl} launches per step"}.get(
+        dom_name, f"{dom_name} ({nl} launches per step)")
+    traffic, tsrc = None, None
+    if dom_name in DRAM_TRAFFIC_RATIO:
+        ratio, tsrc = DRAM_TRAFFIC_RATIO[dom_name]
+        traffic = int(d["algorithmic_bytes"] * ratio)
+    roof = {"bound": "hbm", "kernel": what, "achieved": d["gbs"], "peak": hbm, "unit": "GB/s",
+            "frac": d["gbs"] / hbm, "traffic": traffic, "traffic_source": tsrc,
+            "algorithmic_bytes": d["algorithmic_bytes"],
+            "us_per_launch": d["us_per_launch"], "share_of_step": d["share"],
+            "timing": "CUDA events on the decode stream around each launch, inside the library's decode step",
+            "peak_source": peaks.get("_source")}
+    return {"kernels": kernels, "roofline": roof}
+
+
+def gemv_batch1_timing(torch, cfg, stream) -> dict:
+    """The batch-1 INT4 GEMV (row (a)) on the fused gate+up matrix, timed in isolation with CUDA
+    events on rotating weight copies larger than L2."""
+    from glacier_b200 import ops
+    from glacier_b200.model import random_int4
     rng = np.random.default_rng(5)
     M, K = 2 * cfg.hidden, cfg.dim
     packed, scales = random_int4(rng, M, K, 32)
     copies = 4
     Ws = [torch.from_numpy(packed).cuda() for _ in range(copies)]
     Ss = [torch.from_numpy(scales.astype(np.float16)).cuda() for _ in range(copies)]
-    for b in (1, lanes):
-        x = torch.randn(b, K, device="cuda")
-        y = torch.empty(b, M, device="cuda")
-        for i in range(3):
-            ops.linear_int4_on_the_fly(x, Ws[i % copies], Ss[i % copies], M, K, 32, out=y, stream=stream)
-        n = 12
-        e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
-        e0.record(stream)
-        for i in range(n):
-            ops.linear_int4_on_the_fly(x, Ws[i % copies], Ss[i % copies], M, K, 32, out=y, stream=stream)
-        e1.record(stream)
-        torch.cuda.synchronize()
-        t = e0.elapsed_time(e1) / n / 1e3
-        byt = M * K // 2 + M * K // 32 * 2 + b * K * 4 + b * M * 4
-        out["kernels"][f"int4_linear_{M}x{K}_b{b}"] = {"us": t * 1e6, "algorithmic_bytes": byt,
-                                                       "gbs": byt / t / 1e9}
-    k1 = out["kernels"][f"int4_linear_{M}x{K}_b1"]
-    out["roofline"] = {"bound": "hbm", "kernel": f"int4 dequant GEMV {M}x{K} g32, batch 1",
-                       "achieved": k1["gbs"], "peak": hbm, "unit": "GB/s", "frac": k1["gbs"] / hbm,
-                       "traffic": None, "peak_source": peaks.get("_source")}
-    return out
+    x = torch.randn(1, K, device="cuda")
+    y = torch.empty(1, M, device="cuda")
+    for i in range(3):
+        ops.linear_int4_on_the_fly(x, Ws[i % copies], Ss[i % copies], M, K, 32, out=y, stream=stream)
+    n = 12
+    e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+    e0.record(stream)
+    for i in range(n):
+        ops.linear_int4_on_the_fly(x, Ws[i % copies], Ss[i % copies], M, K, 32, out=y, stream=stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    t = e0.elapsed_time(e1) / n / 1e3
+    byt = M * K // 2 + M * K // 32 * 2 + K * 4 + M * 4
+    return {f"int4_gemv_{M}x{K}_b1_isolated": {"us_per_launch": t * 1e6, "algorithmic_bytes": byt,
+                                               "gbs": byt / t / 1e9}}
 
 
 def main():

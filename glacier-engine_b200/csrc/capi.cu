@@ -94,7 +94,8 @@ int attention_chunk(size_t lanes, size_t num_kv_heads, size_t max_ctx);
 int paged_attention(const float* q, size_t ldq, const float* pool, size_t page_floats, const int32_t* block_tables,
                     size_t max_pages, const int32_t* ctx_lens, size_t max_ctx, size_t lanes, size_t layer,
                     size_t num_heads, size_t num_kv_heads, size_t head_dim, float* out, size_t ldo, float* workspace,
-                    size_t workspace_floats, int chunk, cudaStream_t stream, SplitOut so = SplitOut());
+                    size_t workspace_floats, int chunk, cudaStream_t stream, SplitOut so = SplitOut(),
+                    StepProfiler* prof = nullptr, int combine_kind = -1);
 size_t argmax_workspace_bytes(size_t batch, size_t n);
 int argmax_rows(const float* logits, size_t ld, size_t batch, size_t n, const uint64_t* words, size_t word_count,
                 glacier_argmax_result* out, int32_t* tokens, int32_t* status, void* workspace, size_t ws_bytes,

@@ -7,6 +7,8 @@
 #include <stdint.h>
 #include <stdio.h>
 
+#include <vector>
+
 #include "glacier_cuda.h"
 
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
@@ -54,6 +56,24 @@ int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base
 
 // Allows `bytes` of dynamic shared memory for `kernel` (once per kernel).
 int allow_dynamic_smem(const void* kernel, int bytes);
+
+// Optional per-kernel-class timing of a multi-kernel step: while `on`, mark()
+// records a CUDA event on the launching stream that closes the open region and
+// opens one of `kind` (kind < 0 only closes).  The events are read back later,
+// so the step is never synchronised.  Host-side only; one owner per instance.
+struct StepProfiler {
+  static constexpr size_t kMaxEvents = 1 << 16;
+  bool on = false;
+  bool overflow = false;
+  size_t used = 0;
+  std::vector<cudaEvent_t> events;
+  std::vector<int> kinds;
+  void mark(int kind, cudaStream_t stream);
+  // Sums region times per kind into ms[kind] / regions[kind] (kind < kinds_n),
+  // waiting for the last event; then forgets the records.
+  int read(double* ms, uint64_t* regions, size_t kinds_n);
+  ~StepProfiler();
+};
 
 // A device-resident INT4 weight: the reference's exact nibble packing plus one
 // scale row per output row (fp16 mirror or the original fp32), with the TMA

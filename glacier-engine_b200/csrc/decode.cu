@@ -46,7 +46,8 @@ int attention_chunk(size_t lanes, size_t num_kv_heads, size_t max_ctx);
 int paged_attention(const float* q, size_t ldq, const float* pool, size_t page_floats, const int32_t* block_tables,
                     size_t max_pages, const int32_t* ctx_lens, size_t max_ctx, size_t lanes, size_t layer,
                     size_t num_heads, size_t num_kv_heads, size_t head_dim, float* out, size_t ldo, float* workspace,
-                    size_t workspace_floats, int chunk, cudaStream_t stream, SplitOut so = SplitOut());
+                    size_t workspace_floats, int chunk, cudaStream_t stream, SplitOut so = SplitOut(),
+                    StepProfiler* prof = nullptr, int combine_kind = -1);
 size_t argmax_workspace_bytes(size_t batch, size_t n);
 int argmax_rows(const float* logits, size_t ld, size_t batch, size_t n, const uint64_t* words, size_t word_count,
                 glacier_argmax_result* out, int32_t* tokens, int32_t* status, void* workspace, size_t ws_bytes,
@@ -60,6 +61,49 @@ int encode_split_map(CUtensorMap* map, const __half* xs, size_t np, size_t K);
 int gemm_splits(size_t M, size_t K);
 int gemm_int4_tc(const Int4Weight& w, const CUtensorMap& xmap, const float* xscale, size_t n, size_t np, float* y,
                  size_t ldy, int nsplit, size_t split_stride, const float* bias, cudaStream_t stream);
+
+void StepProfiler::mark(int kind, cudaStream_t stream) {
+  if (!on) return;
+  if (used == events.size()) {
+    cudaEvent_t e = nullptr;
+    if (events.size() >= kMaxEvents || cudaEventCreate(&e) != cudaSuccess) {
+      overflow = true;
+      return;
+    }
+    events.push_back(e);
+    kinds.push_back(-1);
+  }
+  if (cudaEventRecord(events[used], stream) != cudaSuccess) {
+    overflow = true;
+    return;
+  }
+  kinds[used++] = kind;
+}
+
+int StepProfiler::read(double* ms, uint64_t* regions, size_t kinds_n) {
+  for (size_t k = 0; k < kinds_n; ++k) {
+    ms[k] = 0.0;
+    regions[k] = 0;
+  }
+  const bool lost = overflow;
+  overflow = false;
+  if (used > 0) GLC_CHECK_CUDA(cudaEventSynchronize(events[used - 1]));
+  for (size_t i = 0; i + 1 < used; ++i) {
+    const int k = kinds[i];
+    if (k < 0 || (size_t)k >= kinds_n) continue;
+    float t = 0.f;
+    GLC_CHECK_CUDA(cudaEventElapsedTime(&t, events[i], events[i + 1]));
+    ms[k] += t;
+    regions[k] += 1;
+  }
+  used = 0;
+  GLC_REQUIRE(!lost, "profile: more than %zu regions recorded between reads; some were dropped", kMaxEvents);
+  return GLACIER_CUDA_OK;
+}
+
+StepProfiler::~StepProfiler() {
+  for (cudaEvent_t e : events) cudaEventDestroy(e);
+}
 
 namespace {
 
@@ -196,6 +240,7 @@ struct glacier_cuda_model {
   DevBuf xs_d, xs_q, xs_f, xscale;
   CUtensorMap map_d, map_q, map_f;
   int split_qkv = 1, split_o = 1, split_d = 1;
+  StepProfiler prof;  // optional per-kernel-class timing of decode steps
 };
 
 struct glacier_cuda_kv {
@@ -522,6 +567,11 @@ int glacier_cuda_decode_step(glacier_cuda_model* m, glacier_cuda_kv* kv, size_t 
   int rc;
   float* x = m->x.as<float>();
   float* hn = m->hn.as<float>();
+  StepProfiler* prof = m->prof.on ? &m->prof : nullptr;
+  auto mark = [&](int kind) {
+    if (prof) prof->mark(kind, st);
+  };
+  mark(GLACIER_CUDA_STEP_EMBED);
   ctx_from_pos_kernel<<<(unsigned)ceil_div(B, 128), 128, 0, st>>>(positions, m->ctx.as<int32_t>(), (int)B);
   GLC_CHECK_LAUNCH();
   if ((rc = embed_gather(m->embedding.as<__half>(), c.vocab, D, tokens, B, x, D, st))) return rc;
@@ -547,37 +597,64 @@ int glacier_cuda_decode_step(glacier_cuda_model* m, glacier_cuda_kv* kv, size_t 
   for (size_t l = 0; l < c.num_layers; ++l) {
     Layer& L = *m->layers[l];
     // x (+ previous layer's down projection, its split-K partials summed in order) -> x, normed hn
+    mark(GLACIER_CUDA_STEP_NORM);
     if ((rc = add_rmsnorm(x, D, l ? m->down.as<float>() : nullptr, D, B * D, l ? sd : 0, x, D, L.in_norm.as<float>(),
                           c.rms_eps, m->gemm ? nullptr : hn, D, B, D, st, so_d)))
       return rc;
+    mark(GLACIER_CUDA_STEP_PROJ_QKV);
     if ((rc = project(L.qkv.w, hn, D, so_d, m->map_d, m->qkv.as<float>(), m->qkv_dim, sq))) return rc;
+    mark(GLACIER_CUDA_STEP_ROPE_APPEND);
     if ((rc = qkv_rope_append(m->qkv.as<float>(), m->qkv_dim, B * m->qkv_dim, sq, L.bqkv.as<float>(),
                               m->rope_cos.as<float>(), m->rope_sin.as<float>(), c.max_positions, positions, B,
                               c.num_heads, c.num_kv_heads, c.head_dim, m->q.as<float>(), m->q_dim,
                               kv->pool.as<float>(), kv->page_floats, block_tables, max_pages, l, st)))
       return rc;
+    mark(GLACIER_CUDA_STEP_ATTENTION);
     if ((rc = paged_attention(m->q.as<float>(), m->q_dim, kv->pool.as<float>(), kv->page_floats, block_tables,
                               max_pages, m->ctx.as<int32_t>(), max_ctx, B, l, c.num_heads, c.num_kv_heads, c.head_dim,
                               m->gemm ? nullptr : m->attn.as<float>(), m->q_dim, m->att_ws.as<float>(), m->att_floats,
-                              m->att_chunk, st, so_q)))
+                              m->att_chunk, st, so_q, prof, GLACIER_CUDA_STEP_ATTN_COMBINE)))
       return rc;
+    mark(GLACIER_CUDA_STEP_PROJ_O);
     if ((rc = project(L.o.w, m->attn.as<float>(), m->q_dim, so_q, m->map_q, m->proj.as<float>(), D, so_))) return rc;
+    mark(GLACIER_CUDA_STEP_NORM);
     if ((rc = add_rmsnorm(x, D, m->proj.as<float>(), D, B * D, so_, x, D, L.post_norm.as<float>(), c.rms_eps,
                           m->gemm ? nullptr : hn, D, B, D, st, so_d)))
       return rc;
+    mark(GLACIER_CUDA_STEP_PROJ_GATE_UP);
     if ((rc = project(L.gu.w, hn, D, so_d, m->map_d, m->gu.as<float>(), 2 * F, 1))) return rc;
+    mark(GLACIER_CUDA_STEP_SILU);
     if ((rc = silu_mul(m->gu.as<float>(), m->gu.as<float>() + F, 2 * F, m->gemm ? nullptr : m->act.as<float>(), F, B,
                        F, st, so_f)))
       return rc;
+    mark(GLACIER_CUDA_STEP_PROJ_DOWN);
     if ((rc = project(L.d.w, m->act.as<float>(), F, so_f, m->map_f, m->down.as<float>(), D, sd))) return rc;
   }
+  mark(GLACIER_CUDA_STEP_NORM);
   if ((rc = add_rmsnorm(x, D, m->down.as<float>(), D, B * D, sd, x, D, m->final_norm.as<float>(), c.rms_eps,
                         m->gemm ? nullptr : hn, D, B, D, st, so_d)))
     return rc;
   float* logits = logits_out ? logits_out : m->logits.as<float>();
+  mark(GLACIER_CUDA_STEP_LM_HEAD);
   if ((rc = project(m->lm.w, hn, D, so_d, m->map_d, logits, c.vocab, 1))) return rc;
-  return argmax_rows(logits, c.vocab, B, c.vocab, eligible, eligible_words, nullptr, tokens_out,
-                     status_out ? status_out : m->status.as<int32_t>(), m->arg_ws.p, m->arg_bytes, st);
+  mark(GLACIER_CUDA_STEP_ARGMAX);
+  rc = argmax_rows(logits, c.vocab, B, c.vocab, eligible, eligible_words, nullptr, tokens_out,
+                   status_out ? status_out : m->status.as<int32_t>(), m->arg_ws.p, m->arg_bytes, st);
+  mark(-1);
+  return rc;
+}
+
+int glacier_cuda_model_profile(glacier_cuda_model* m, int enable) {
+  GLC_REQUIRE(m, "model_profile: null model");
+  m->prof.on = enable != 0;
+  return GLACIER_CUDA_OK;
+}
+
+int glacier_cuda_model_profile_read(glacier_cuda_model* m, double* ms, uint64_t* regions, size_t kinds) {
+  GLC_REQUIRE(m && ms && regions && kinds > 0, "model_profile_read: null argument");
+  const int rc = bind_device(m);
+  if (rc) return rc;
+  return m->prof.read(ms, regions, kinds);
 }
 
 }  // extern "C"

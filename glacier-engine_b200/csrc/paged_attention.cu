@@ -355,7 +355,8 @@ int attention_chunk(size_t lanes, size_t num_kv_heads, size_t max_ctx) {
 int paged_attention(const float* q, size_t ldq, const float* pool, size_t page_floats, const int32_t* block_tables,
                     size_t max_pages, const int32_t* ctx_lens, size_t max_ctx, size_t lanes, size_t layer,
                     size_t num_heads, size_t num_kv_heads, size_t head_dim, float* out, size_t ldo, float* workspace,
-                    size_t workspace_floats, int chunk, cudaStream_t stream, SplitOut so) {
+                    size_t workspace_floats, int chunk, cudaStream_t stream, SplitOut so, StepProfiler* prof,
+                    int combine_kind) {
   GLC_REQUIRE(q && pool && block_tables && ctx_lens && (out || so.xs) && workspace, "paged_attention: null argument");
   GLC_REQUIRE(num_kv_heads > 0 && num_heads % num_kv_heads == 0, "paged_attention: heads %zu / kv heads %zu",
               num_heads, num_kv_heads);
@@ -399,6 +400,7 @@ int paged_attention(const float* q, size_t ldq, const float* pool, size_t page_f
   }
   kern<<<dim3(nsplit, (unsigned)num_kv_heads, (unsigned)lanes), kAttnThreads, smem, stream>>>(prm);
   GLC_CHECK_LAUNCH();
+  if (prof) prof->mark(combine_kind, stream);
   {
     // Cluster of CTAs per lane over its heads (about 7 heads per CTA).
     int cl = 1;

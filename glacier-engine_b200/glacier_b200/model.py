@@ -160,7 +160,10 @@ class DeviceModel:
             self.h = None
 
     def __del__(self):
-        self.close()
+        try:
+            self.close()
+        except Exception:  # interpreter shutdown: ctypes / module globals may already be gone
+            pass
 
 
 class DecodeSession:
@@ -213,7 +216,10 @@ class DecodeSession:
             self.kv = None
 
     def __del__(self):
-        self.close()
+        try:
+            self.close()
+        except Exception:  # interpreter shutdown: ctypes / module globals may already be gone
+            pass
 
 
 def _ptr_tensor(torch, ptr: int, numel: int):

@@ -254,6 +254,31 @@ int glacier_cuda_decode_step(glacier_cuda_model *model, glacier_cuda_kv *kv, siz
                              size_t max_pages, const uint64_t *eligible, size_t eligible_words,
                              int32_t *tokens_out, int32_t *status_out, float *logits_out, void *stream);
 
+/* Diagnostics, no reference counterpart: per kernel class device time of decode steps.
+ * glacier_cuda_model_profile(model, 1) makes later decode steps record CUDA events on their
+ * stream between the step's kernel classes (no synchronisation inside the step); 0 stops.
+ * glacier_cuda_model_profile_read waits for the recorded steps, writes for each class k < kinds
+ * the summed milliseconds ms[k] and the number of timed launches regions[k], and forgets the
+ * records.  A region runs from one class's first launch to the next class's first launch, so it
+ * includes the launch gap before the next class. */
+enum glacier_cuda_step_kind {
+  GLACIER_CUDA_STEP_EMBED = 0,     /* context lengths + embedding gather */
+  GLACIER_CUDA_STEP_NORM,          /* residual add + RMSNorm (and split-K partial sums) */
+  GLACIER_CUDA_STEP_PROJ_QKV,      /* fused Q/K/V INT4 projection */
+  GLACIER_CUDA_STEP_ROPE_APPEND,   /* bias, RoPE, KV page append */
+  GLACIER_CUDA_STEP_ATTENTION,     /* paged attention partials over context chunks */
+  GLACIER_CUDA_STEP_ATTN_COMBINE,  /* merge of the chunk partials */
+  GLACIER_CUDA_STEP_PROJ_O,
+  GLACIER_CUDA_STEP_PROJ_GATE_UP,  /* fused gate/up INT4 projection */
+  GLACIER_CUDA_STEP_SILU,
+  GLACIER_CUDA_STEP_PROJ_DOWN,
+  GLACIER_CUDA_STEP_LM_HEAD,
+  GLACIER_CUDA_STEP_ARGMAX,
+  GLACIER_CUDA_STEP_KINDS
+};
+int glacier_cuda_model_profile(glacier_cuda_model *model, int enable);
+int glacier_cuda_model_profile_read(glacier_cuda_model *model, double *ms, uint64_t *regions, size_t kinds);
+
 #ifdef __cplusplus
 }
 #endif

@@ -85,3 +85,35 @@ def test_decode_tensor_core_mode_16_lanes():
     # more than 4 lanes: every projection runs the tcgen05 GEMM with split-K partials
     cfg = ModelConfig(num_layers=2, dim=512, hidden=1024, num_heads=28, num_kv_heads=4, head_dim=128, vocab=2048)
     assert run_parity(cfg, lanes=16, prompt_len=4, new_tokens=3) >= 30
+
+
+def test_step_profile_counts_every_kernel_class():
+    """The per-class event timing sees each class the expected number of times per step and
+    leaves the step's results unchanged."""
+    import ctypes as C
+    from glacier_b200 import _lib
+    from glacier_b200.model import DecodeSession, DeviceModel, ModelConfig, SyntheticModel
+    cfg = ModelConfig(num_layers=2, dim=512, hidden=1024, num_heads=28, num_kv_heads=4, head_dim=128, vocab=2048)
+    dm = DeviceModel(SyntheticModel(cfg, seed=3), max_positions=64)
+    sess = DecodeSession(dm, 8, 4)
+    toks = [5, 6, 7, 8, 9, 10, 11, 12]
+    plain = sess.step(tokens=toks, positions=[3] * 8).cpu().tolist()
+    _lib.call("glacier_cuda_model_profile", dm.h, 1)
+    steps = 3
+    for _ in range(steps):
+        got = sess.step(tokens=toks, positions=[3] * 8).cpu().tolist()
+        assert got == plain
+    _lib.call("glacier_cuda_model_profile", dm.h, 0)
+    n = 12
+    ms, regions = (C.c_double * n)(), (C.c_uint64 * n)()
+    _lib.call("glacier_cuda_model_profile_read", dm.h, ms, regions, n)
+    per_step = [r // steps for r in regions]
+    L = cfg.num_layers
+    # embed, norm (2 per layer + final), qkv, rope, attention, combine, o, gate_up, silu, down, lm_head, argmax
+    assert per_step == [1, 2 * L + 1, L, L, L, L, L, L, L, L, 1, 1]
+    assert all(ms[k] > 0 for k in range(n))
+    # A second read without new steps reports nothing.
+    _lib.call("glacier_cuda_model_profile_read", dm.h, ms, regions, n)
+    assert list(regions) == [0] * n
+    sess.close()
+    dm.close()
