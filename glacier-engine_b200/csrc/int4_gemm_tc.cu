@@ -18,15 +18,21 @@
 // (N = 2*Np) and a second runs Wlo against Xhi into the same TMEM columns, all
 // accumulated in fp32.
 //
-// Pipeline (one CTA = 128 weight rows x Np activation rows x a K range):
-//   warp 0  TMA producer: 128 x 256-code nibble tiles (SWIZZLE_128B) + the
-//           128 x 8 scale tiles into a 3-slot ring
-//   warp 1  TMA producer: 64-K activation tiles [Xhi | Xlo] (SWIZZLE_128B)
-//   warp 2  allocates TMEM and issues tcgen05.mma from one thread
-//   warps 3-10 (256 threads, two per weight row) convert nibbles + scales to
-//           the -Whi / Wlo tiles in the canonical K-major SWIZZLE_128B layout
-//           (the MMA descriptor negates A back), then run the epilogue
-//           (tcgen05.ld, xs scaling, coalesced stores).
+// Persistent pipeline: one CTA per SM walks a static list of work units
+// (128 weight rows x one K split), with TMEM allocated and barriers set up once:
+//   warp 0      TMA producer: 128 x 256-code nibble tiles (SWIZZLE_128B) plus the
+//               matching 128 x 8 fp16 scale tiles, into a ring of super-stages
+//   warp 1      TMA producer: 64-K activation tiles [Xhi | Xlo] (SWIZZLE_128B)
+//   warp 2      allocates TMEM; one thread issues tcgen05.mma
+//   warps 3-10  converters (two per 32-row TMEM lane quarter): nibbles + scales
+//               -> -Whi / Wlo fp16 pairs written straight into TMEM with
+//               tcgen05.st; the MMA reads A from TMEM (the descriptor's negate
+//               bit restores the sign of Whi), so shared memory carries only
+//               the nibble and activation tiles
+//   warps 11-14 epilogue: tcgen05.ld of a finished accumulator, per-row
+//               activation scale, bias, coalesced stores
+// Accumulators are double-buffered in TMEM when they fit, so a unit's
+// epilogue overlaps the next unit's MMAs.
 // Code order inside each 8-code word is permuted to (0,4,1,5,2,6,3,7) by the
 // unpack; the activation split kernel stores X in the same order, so the
 // contraction is unchanged.  Every wait is bounded; no multicast is used.
@@ -41,12 +47,16 @@ namespace {
 constexpr int kRowsTile = 128;
 constexpr int kChunkK = 64;                     // K per MMA stage (one 128-byte swizzle row of fp16)
 constexpr int kSuperK = 256;                    // K per nibble/scale TMA stage
-constexpr int kMaxSlots = 8;                    // ring slots (runtime counts below this)
-constexpr int kConvWarps = 8;                   // two converter threads per weight row
+constexpr int kMaxSlots = 8;                    // shared-memory ring slots (runtime counts below this)
+constexpr int kConvWarps = 8;                   // two converter warps per TMEM lane quarter
+constexpr int kEpiWarps = 4;                    // one epilogue warp per TMEM lane quarter
+constexpr int kASlots = 4;                      // A chunks (-Whi | Wlo) resident in TMEM
+constexpr uint32_t kAColsPerSlot = 64;          // 32 columns of -Whi + 32 of Wlo (2 fp16 per column)
+constexpr uint32_t kTmemCols = 512;             // the whole TMEM of the SM (one CTA per SM)
 constexpr int kNibBytes = kRowsTile * 128;      // 128 rows x 256 codes
 constexpr int kSclBytes = kRowsTile * 16;       // 128 rows x 8 fp16 scales
-constexpr int kATileBytes = kRowsTile * 128;    // 128 rows x 64 fp16
-constexpr int kThreads = (3 + kConvWarps) * 32;
+constexpr int kThreads = (3 + kConvWarps + kEpiWarps) * 32;
+constexpr int kMinSmem = 120 * 1024;            // keeps a second CTA (and its TMEM request) off the SM
 
 __device__ __forceinline__ uint32_t hfma2_u32(uint32_t a, uint32_t b, uint32_t c) {
   uint32_t d;
@@ -58,7 +68,6 @@ __device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
   asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
   return d;
 }
-__device__ __forceinline__ uint32_t neg_half2(uint32_t a) { return a ^ 0x80008000u; }
 
 // Eight codes -> four half2 of exact (u - 7) in the order {u0,u4},{u1,u5},{u2,u6},{u3,u7}.
 __device__ __forceinline__ void unpack8(uint32_t w, uint32_t (&q)[4]) {
@@ -89,20 +98,12 @@ __host__ __device__ constexpr uint32_t idesc_f16(int n, bool negate_a = false) {
   return (1u << 4) | ((negate_a ? 1u : 0u) << 13) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 }
 
-__device__ __forceinline__ void umma_f16(uint32_t dtmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                         uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(dtmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
-}
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
 }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   uint32_t r[16];
@@ -116,6 +117,26 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// tcgen05.mma with A read from TMEM (kind::f16, cta_group::1).
+__device__ __forceinline__ void umma_f16_ts(uint32_t dtmem, uint32_t atmem, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(dtmem),
+      "r"(atmem), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+// Each thread writes 16 consecutive 32-bit columns of its own TMEM lane.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 struct GemmParams {
   const float* xscale;  // [Np] per activation row
   const float* bias;    // [M] or null, added by split 0
@@ -124,9 +145,25 @@ struct GemmParams {
   int M, K, n, np;      // weight rows, K, live activation rows, padded rows (multiple of 16)
   int chunks_total;     // ceil(K / 64)
   int chunks_per_split; // multiple of 4
-  int nib_slots, a_slots, b_slots;
+  int nsplit, tiles, units;
+  int nib_slots, b_slots;
+  int acc_cols, acc_bufs;  // TMEM columns per accumulator buffer, number of buffers
   int* err;
 };
+
+struct Unit {
+  int row0, split, c0, nch;
+};
+
+__device__ __forceinline__ Unit unit_of(const GemmParams& p, int u) {
+  Unit w;
+  const int tile = u / p.nsplit;
+  w.split = u - tile * p.nsplit;
+  w.row0 = tile * kRowsTile;
+  w.c0 = w.split * p.chunks_per_split;
+  w.nch = max(0, min(p.chunks_total, w.c0 + p.chunks_per_split) - w.c0);
+  return w;
+}
 
 __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_w,
                                                               const __grid_constant__ CUtensorMap tmap_s,
@@ -135,49 +172,48 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int bbytes = 2 * p.np * 128;  // [Xhi | Xlo] tile: 2*Np rows x 64 fp16
-  const int kNibSlots = p.nib_slots, kASlots = p.a_slots, kBSlots = p.b_slots;
-  uint8_t* nib = smem;                                        // kNibSlots x (nibbles + scales)
-  uint8_t* atile = nib + kNibSlots * (kNibBytes + kSclBytes); // kASlots x (-Whi, Wlo)
-  uint8_t* btile = atile + kASlots * 2 * kATileBytes;         // kBSlots x bbytes
-  uint64_t* bars = reinterpret_cast<uint64_t*>(btile + kBSlots * bbytes);
+  const int NS = p.nib_slots, BS = p.b_slots;
+  uint8_t* nib = smem;                                 // NS x (nibbles + scales)
+  uint8_t* btile = nib + NS * (kNibBytes + kSclBytes);  // BS x bbytes
+  uint64_t* bars = reinterpret_cast<uint64_t*>(btile + BS * bbytes);
   uint64_t* nib_full = bars;
   uint64_t* nib_empty = nib_full + kMaxSlots;
-  uint64_t* a_full = nib_empty + kMaxSlots;
-  uint64_t* a_empty = a_full + kMaxSlots;
-  uint64_t* b_full = a_empty + kMaxSlots;
+  uint64_t* b_full = nib_empty + kMaxSlots;
   uint64_t* b_empty = b_full + kMaxSlots;
-  uint64_t* acc_full = b_empty + kMaxSlots;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
-  __shared__ int s_abort;
+  uint64_t* a_full = b_empty + kMaxSlots;
+  uint64_t* a_empty = a_full + kASlots;
+  uint64_t* acc_full = a_empty + kASlots;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* mma_done = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  __shared__ volatile int s_abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tile = blockIdx.x, split = blockIdx.y;
-  const int row0 = tile * kRowsTile;
-  const int c0 = split * p.chunks_per_split;
-  const int c1 = min(p.chunks_total, c0 + p.chunks_per_split);
-  const int nch = max(0, c1 - c0);
-  const uint32_t ncols = (2 * p.np <= 32) ? 32 : (2 * p.np <= 64 ? 64 : (2 * p.np <= 128 ? 128 : 256));
 
   if (threadIdx.x == 0) {
     s_abort = 0;
-    for (int i = 0; i < kNibSlots; ++i) {
+    for (int i = 0; i < NS; ++i) {
       mbar_init(&nib_full[i], 1);
       mbar_init(&nib_empty[i], kConvWarps);
+    }
+    for (int i = 0; i < BS; ++i) {
+      mbar_init(&b_full[i], 1);
+      mbar_init(&b_empty[i], 1);
     }
     for (int i = 0; i < kASlots; ++i) {
       mbar_init(&a_full[i], kConvWarps);
       mbar_init(&a_empty[i], 1);
     }
-    for (int i = 0; i < kBSlots; ++i) {
-      mbar_init(&b_full[i], 1);
-      mbar_init(&b_empty[i], 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], kEpiWarps);
     }
-    mbar_init(acc_full, 1);
+    mbar_init(mma_done, 1);
     fence_mbar_init();
   }
   if (warp == 2) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(ncols)
+                 "r"(kTmemCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -185,125 +221,170 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const uint32_t a_base = (uint32_t)(p.acc_bufs * p.acc_cols);  // A ring follows the accumulators
 
   if (warp == 0) {
-    // ---- nibble + scale producer (one 256-K super-stage per 4 chunks) ----
-    if (lane == 0 && nch > 0) {
+    // ---- nibble + scale producer: one 256-K super-stage per 4 chunks ----
+    if (lane == 0) {
       prefetch_tmap(&tmap_w);
       prefetch_tmap(&tmap_s);
       const uint64_t pol = l2_evict_first_policy();
-      const int nsup = (nch + 3) / 4;
-      int issued = 0;
-      for (int i = 0; i < nsup; ++i) {
-        const int slot = i % kNibSlots, round = i / kNibSlots;
-        if (!mbar_wait(&nib_empty[slot], (round & 1) ^ 1, p.err)) { s_abort = 1; break; }
-        uint8_t* dst = nib + slot * (kNibBytes + kSclBytes);
-        mbar_arrive_expect_tx(&nib_full[slot], kNibBytes + kSclBytes);
-        const int ks = (c0 / 4 + i);  // super-stage index along K
-        tma_load_2d(dst, &tmap_w, ks * 128, row0, &nib_full[slot], pol);
-        tma_load_2d(dst + kNibBytes, &tmap_s, ks * 8, row0, &nib_full[slot], pol);
-        ++issued;
+      uint32_t it = 0;
+      for (int u = blockIdx.x; u < p.units && !s_abort; u += gridDim.x) {
+        const Unit w = unit_of(p, u);
+        const int nsup = (w.nch + 3) / 4;
+        for (int i = 0; i < nsup; ++i, ++it) {
+          const int slot = it % NS;
+          if (!mbar_wait(&nib_empty[slot], ((it / NS) & 1) ^ 1, p.err)) { s_abort = 1; break; }
+          uint8_t* dst = nib + slot * (kNibBytes + kSclBytes);
+          mbar_arrive_expect_tx(&nib_full[slot], kNibBytes + kSclBytes);
+          const int ks = w.c0 / 4 + i;  // super-stage index along K
+          tma_load_2d(dst, &tmap_w, ks * 128, w.row0, &nib_full[slot], pol);
+          tma_load_2d(dst + kNibBytes, &tmap_s, ks * 8, w.row0, &nib_full[slot], pol);
+        }
       }
-      for (int i = max(0, issued - kNibSlots); i < issued; ++i)
-        mbar_wait(&nib_full[i % kNibSlots], (i / kNibSlots) & 1, p.err);
+      // Leave no copy in flight (matters only when a wait gave up).
+      for (uint32_t i = it > (uint32_t)NS ? it - NS : 0; i < it; ++i)
+        mbar_wait(&nib_full[i % NS], (i / NS) & 1, p.err);
     }
   } else if (warp == 1) {
     // ---- activation producer: one [Xhi | Xlo] tile per 64-K chunk ----
-    if (lane == 0 && nch > 0) {
+    if (lane == 0) {
       prefetch_tmap(&tmap_x);
       uint64_t keep;
       asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(keep));
-      int issued = 0;
-      for (int i = 0; i < nch; ++i) {
-        const int slot = i % kBSlots, round = i / kBSlots;
-        if (!mbar_wait(&b_empty[slot], (round & 1) ^ 1, p.err)) { s_abort = 1; break; }
-        mbar_arrive_expect_tx(&b_full[slot], (uint32_t)bbytes);
-        tma_load_2d(btile + slot * bbytes, &tmap_x, (c0 + i) * kChunkK, 0, &b_full[slot], keep);
-        ++issued;
+      uint32_t it = 0;
+      for (int u = blockIdx.x; u < p.units && !s_abort; u += gridDim.x) {
+        const Unit w = unit_of(p, u);
+        for (int i = 0; i < w.nch; ++i, ++it) {
+          const int slot = it % BS;
+          if (!mbar_wait(&b_empty[slot], ((it / BS) & 1) ^ 1, p.err)) { s_abort = 1; break; }
+          mbar_arrive_expect_tx(&b_full[slot], (uint32_t)bbytes);
+          tma_load_2d(btile + slot * bbytes, &tmap_x, (w.c0 + i) * kChunkK, 0, &b_full[slot], keep);
+        }
       }
-      for (int i = max(0, issued - kBSlots); i < issued; ++i)
-        mbar_wait(&b_full[i % kBSlots], (i / kBSlots) & 1, p.err);
+      for (uint32_t i = it > (uint32_t)BS ? it - BS : 0; i < it; ++i)
+        mbar_wait(&b_full[i % BS], (i / BS) & 1, p.err);
     }
   } else if (warp == 2) {
     // ---- MMA issuer ----
-    if (lane == 0 && nch > 0) {
+    if (lane == 0) {
       // A holds -Whi (negated back by the descriptor) and Wlo.
       const uint32_t id_hl = idesc_f16(2 * p.np, true), id_h = idesc_f16(p.np);
-      int done = 0;
-      for (int i = 0; i < nch; ++i) {
-        const int as = i % kASlots, bs = i % kBSlots;
-        if (!mbar_wait(&a_full[as], (i / kASlots) & 1, p.err)) { s_abort = 1; break; }
-        if (!mbar_wait(&b_full[bs], (i / kBSlots) & 1, p.err)) { s_abort = 1; break; }
+      uint32_t ch = 0, acc_i = 0;
+      for (int u = blockIdx.x; u < p.units && !s_abort; u += gridDim.x) {
+        const Unit w = unit_of(p, u);
+        if (w.nch == 0) continue;
+        const int ab = acc_i % p.acc_bufs;
+        const uint32_t use = acc_i / p.acc_bufs;
+        if (!mbar_wait(&acc_empty[ab], (use & 1) ^ 1, p.err)) { s_abort = 1; break; }
         tc_fence_after();
-        const uint32_t ahi = smem_u32(atile + as * 2 * kATileBytes);
-        const uint32_t alo = ahi + kATileBytes;
-        const uint32_t bx = smem_u32(btile + bs * bbytes);
+        const uint32_t d = tmem + (uint32_t)(ab * p.acc_cols);
+        bool ok = true;
+        for (int i = 0; i < w.nch; ++i, ++ch) {
+          const int as = ch % kASlots, bs = ch % BS;
+          if (!mbar_wait(&a_full[as], (ch / kASlots) & 1, p.err) || !mbar_wait(&b_full[bs], (ch / BS) & 1, p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t ahi = tmem + a_base + (uint32_t)as * kAColsPerSlot;
+          const uint32_t alo = ahi + kAColsPerSlot / 2;
+          const uint32_t bx = smem_u32(btile + bs * bbytes);
 #pragma unroll
-        for (int kk = 0; kk < kChunkK / 16; ++kk) {
-          const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
-          umma_f16(tmem, sdesc(ahi + kk * 32), sdesc(bx + kk * 32), id_hl, acc);  // Whi x [Xhi | Xlo]
-          umma_f16(tmem, sdesc(alo + kk * 32), sdesc(bx + kk * 32), id_h, 1u);     // Wlo x Xhi
+          for (int kk = 0; kk < kChunkK / 16; ++kk) {
+            const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+            umma_f16_ts(d, ahi + kk * 8, sdesc(bx + kk * 32), id_hl, acc);  // Whi x [Xhi | Xlo]
+            umma_f16_ts(d, alo + kk * 8, sdesc(bx + kk * 32), id_h, 1u);    // Wlo x Xhi
+          }
+          umma_commit(&a_empty[as]);
+          umma_commit(&b_empty[bs]);
         }
-        umma_commit(&a_empty[as]);
-        umma_commit(&b_empty[bs]);
-        ++done;
+        if (!ok) { s_abort = 1; break; }
+        umma_commit(&acc_full[ab]);  // fires when every MMA of this unit has completed
+        ++acc_i;
       }
-      umma_commit(acc_full);  // fires when every MMA issued above has completed
-      (void)done;
+      umma_commit(mma_done);  // fires once every MMA issued above has completed
+      mbar_wait(mma_done, 0, p.err);
+    }
+  } else if (warp < 3 + kConvWarps) {
+    // ---- converters: thread = weight row (its TMEM lane), 32 codes = one scale group per chunk ----
+    const int quarter = warp & 3;
+    const int hf = (warp - 3) >> 2;  // which 32-code half of the 64-code chunk
+    const int rrow = quarter * 32 + lane;
+    const uint32_t swz = (uint32_t)(rrow & 7);
+    const uint32_t tlane = tmem + ((uint32_t)(quarter * 32) << 16) + a_base + (uint32_t)(16 * hf);
+    uint32_t ch = 0, nsi = 0;
+    for (int u = blockIdx.x; u < p.units && !s_abort; u += gridDim.x) {
+      const Unit w = unit_of(p, u);
+      bool ok = true;
+      for (int i = 0; i < w.nch; ++i, ++ch) {
+        const int sub = i & 3;
+        const int ns = nsi % NS;
+        if (sub == 0 && !__all_sync(0xffffffffu, mbar_wait(&nib_full[ns], (nsi / NS) & 1, p.err))) {
+          ok = false;
+          break;
+        }
+        const int as = ch % kASlots;
+        const uint8_t* nrow = nib + ns * (kNibBytes + kSclBytes) + rrow * 128;
+        const uint8_t* srow = nib + ns * (kNibBytes + kSclBytes) + kNibBytes + rrow * 16;
+        const int grp = 2 * sub + hf;  // 32-code group within the 256-code super stage
+        const uint4 g = *reinterpret_cast<const uint4*>(nrow + (((uint32_t)grp ^ swz) << 4));
+        const uint32_t sh = *reinterpret_cast<const uint16_t*>(srow + 2 * grp);
+        const uint32_t s2 = sh * 0x10001u;      // {s, s}
+        const uint32_t ns2 = s2 ^ 0x80008000u;  // {-s, -s}
+        const uint32_t words[4] = {g.x, g.y, g.z, g.w};
+        uint32_t hi[16], lo[16];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint32_t q[4];
+          unpack8(words[j], q);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            hi[4 * j + e] = hmul2_u32(q[e], ns2);               // -RN(q*s)
+            lo[4 * j + e] = hfma2_u32(q[e], s2, hi[4 * j + e]);  // q*s - RN(q*s), exact
+          }
+        }
+        if (!__all_sync(0xffffffffu, mbar_wait(&a_empty[as], ((ch / kASlots) & 1) ^ 1, p.err))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t ta = tlane + (uint32_t)as * kAColsPerSlot;
+        tmem_st16(ta, hi);
+        tmem_st16(ta + kAColsPerSlot / 2, lo);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&a_full[as]);
+          if (sub == 3 || i == w.nch - 1) mbar_arrive(&nib_empty[ns]);
+        }
+        if (sub == 3 || i == w.nch - 1) ++nsi;
+      }
+      if (!ok) { s_abort = 1; break; }
     }
   } else {
-    // ---- converters (256 threads: two per weight row, 32 codes each), then the epilogue ----
-    const int t = threadIdx.x - 3 * 32;   // 0..255
-    const int rrow = t & (kRowsTile - 1);  // row within the tile
-    const int hf = t >> 7;                 // which 32-code half of the 64-code chunk
-    const uint32_t swz = (uint32_t)(rrow & 7);
-    for (int i = 0; i < nch && !s_abort; ++i) {
-      const int sup = i / 4, sub = i % 4;
-      const int ns = sup % kNibSlots;
-      if (sub == 0 && !mbar_wait(&nib_full[ns], (sup / kNibSlots) & 1, p.err)) { s_abort = 1; break; }
-      const int as = i % kASlots;
-      if (!mbar_wait(&a_empty[as], ((i / kASlots) & 1) ^ 1, p.err)) { s_abort = 1; break; }
-      const uint8_t* nrow = nib + ns * (kNibBytes + kSclBytes) + rrow * 128;
-      const uint8_t* srow = nib + ns * (kNibBytes + kSclBytes) + kNibBytes + rrow * 16;
-      const int grp = 2 * sub + hf;  // 32-code group within the 256-code super stage
-      const uint4 g = *reinterpret_cast<const uint4*>(nrow + (((uint32_t)grp ^ swz) << 4));
-      const uint32_t sh = *reinterpret_cast<const uint16_t*>(srow + 2 * grp);
-      const uint32_t s2 = sh * 0x10001u;           // {s, s}
-      const uint32_t ns2 = s2 ^ 0x80008000u;       // {-s, -s}
-      uint8_t* ahi = atile + as * 2 * kATileBytes + rrow * 128;
-      uint8_t* alo = ahi + kATileBytes;
-      const uint32_t words[4] = {g.x, g.y, g.z, g.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        uint32_t q[4], h[4], l[4];
-        unpack8(words[j], q);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          h[e] = hmul2_u32(q[e], ns2);        // -RN(q*s)
-          l[e] = hfma2_u32(q[e], s2, h[e]);   // q*s - RN(q*s), exact
-        }
-        const uint32_t off = ((uint32_t)(4 * hf + j) ^ swz) << 4;
-        *reinterpret_cast<uint4*>(ahi + off) = make_uint4(h[0], h[1], h[2], h[3]);
-        *reinterpret_cast<uint4*>(alo + off) = make_uint4(l[0], l[1], l[2], l[3]);
-      }
-      fence_proxy_async();  // make the generic-proxy stores visible to the tensor core
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&a_full[as]);
-        if (sub == 3 || i == nch - 1) mbar_arrive(&nib_empty[ns]);
-      }
-    }
-    // Epilogue: TMEM lane = row (this warp's quarter), columns b (hi) and Np + b (lo);
-    // the two converter warps of a quarter split the column blocks.
+    // ---- epilogue: TMEM lane = weight row; columns b (Whi-side hi) and Np + b (lo) ----
     const int quarter = warp & 3;
-    const int row = row0 + quarter * 32 + lane;
-    float* ybase = p.y + (size_t)split * p.split_stride;
-    if (nch > 0 && !s_abort && mbar_wait(acc_full, 0, p.err)) {
+    uint32_t acc_i = 0;
+    for (int u = blockIdx.x; u < p.units && !s_abort; u += gridDim.x) {
+      const Unit w = unit_of(p, u);
+      const int row = w.row0 + quarter * 32 + lane;
+      float* ybase = p.y + (size_t)w.split * p.split_stride;
+      const float bias = (p.bias && w.split == 0 && row < p.M) ? p.bias[row] : 0.f;
+      if (w.nch == 0) {
+        // Empty K-range: this split contributes zeros (plus the bias on split 0).
+        if (row < p.M)
+          for (int b = 0; b < p.n; ++b) ybase[(size_t)b * p.ldy + row] = bias;
+        continue;
+      }
+      const int ab = acc_i % p.acc_bufs;
+      const uint32_t use = acc_i / p.acc_bufs;
+      if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[ab], use & 1, p.err))) { s_abort = 1; break; }
       tc_fence_after();
-      const uint32_t tq = tmem + ((uint32_t)(quarter * 32) << 16);
-      const int nblk16 = p.np / 16;
-      for (int bi = hf; bi < nblk16; bi += 2) {
-        const int b0 = bi * 16;
+      const uint32_t tq = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(ab * p.acc_cols);
+      for (int b0 = 0; b0 < p.np; b0 += 16) {
         float vh[16], vl[16];
         tmem_ld16(tq + (uint32_t)b0, vh);
         tmem_ld16(tq + (uint32_t)(p.np + b0), vl);
@@ -311,26 +392,22 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const int b = b0 + j;
-            if (b < p.n)
-              ybase[(size_t)b * p.ldy + row] =
-                  (vh[j] + vl[j]) * p.xscale[b] + ((p.bias && split == 0) ? p.bias[row] : 0.f);
+            if (b < p.n) ybase[(size_t)b * p.ldy + row] = (vh[j] + vl[j]) * p.xscale[b] + bias;
           }
         }
       }
-    } else if (nch == 0 && hf == 0) {
-      // Empty K-range: this split contributes zeros (plus the bias on split 0).
-      if (row < p.M)
-        for (int b = 0; b < p.n; ++b) ybase[(size_t)b * p.ldy + row] = (p.bias && split == 0) ? p.bias[row] : 0.f;
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[ab]);
+      ++acc_i;
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 2) {
-    // Never release TMEM while an MMA may still write it (aborted runs included).
-    if (lane == 0 && nch > 0) mbar_wait(acc_full, 0, p.err);
-    __syncwarp();
+    // Every MMA has completed (the issuer waited on mma_done) before TMEM is released.
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
   }
 }
 
@@ -398,29 +475,26 @@ int encode_split_map(CUtensorMap* map, const __half* xs, size_t np, size_t K) {
                         (uint32_t)(2 * np), CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
 }
 
-// Ring depths for a padded activation width.  The activation ring is the
-// deepest: its tiles come from L2 with ~1 us of TMA latency and each covers only
-// 64 K, so six of them keep the MMA fed; then three nibble stages (768 K of
-// HBM reads in flight) and two converted weight tiles; all within 227 KB.
-static void gemm_slots(size_t np, int* nib, int* a, int* b) {
-  *nib = 3;
-  *a = 4;
-  *b = 6;
-  auto bytes = [&]() {
-    return 1024 + (size_t)*nib * (kNibBytes + kSclBytes) + (size_t)*a * 2 * kATileBytes + (size_t)*b * 2 * np * 128 +
-           (6 * kMaxSlots + 1) * 8 + 16;
-  };
+// Shared-memory rings for a padded activation width: four nibble super-stages
+// (1024 K of HBM reads in flight) and as many 64-K activation tiles as fit,
+// at most eight; the footprint never drops below kMinSmem so that exactly one
+// CTA (which takes the whole TMEM) runs per SM.
+static void gemm_slots(size_t np, int* nib, int* b) {
+  *nib = 4;
+  *b = kMaxSlots;
+  const size_t fixed = 1024 + (size_t)(4 * kMaxSlots + 2 * kASlots + 5) * 8 + 16;
+  auto bytes = [&]() { return fixed + (size_t)*nib * (kNibBytes + kSclBytes) + (size_t)*b * 2 * np * 128; };
   while (bytes() > 227 * 1024 && *b > 3) --*b;
-  if (bytes() > 227 * 1024) *nib = 2;
-  while (bytes() > 227 * 1024 && *a > 2) --*a;
+  while (bytes() > 227 * 1024 && *nib > 2) --*nib;
   while (bytes() > 227 * 1024 && *b > 2) --*b;
 }
 
 size_t gemm_smem_bytes(size_t np) {
-  int nib, a, b;
-  gemm_slots(np, &nib, &a, &b);
-  return 1024 + (size_t)nib * (kNibBytes + kSclBytes) + (size_t)a * 2 * kATileBytes + (size_t)b * 2 * np * 128 +
-         (6 * kMaxSlots + 1) * 8 + 16;
+  int nib, b;
+  gemm_slots(np, &nib, &b);
+  const size_t bytes = 1024 + (size_t)(4 * kMaxSlots + 2 * kASlots + 5) * 8 + 16 +
+                       (size_t)nib * (kNibBytes + kSclBytes) + (size_t)b * 2 * np * 128;
+  return bytes < (size_t)kMinSmem ? (size_t)kMinSmem : bytes;
 }
 
 // The tensor core's fp32 accumulation does not round every addition, so an
@@ -429,14 +503,27 @@ size_t gemm_smem_bytes(size_t np) {
 // finished on the CUDA cores in rounded fp32 (split-K partials summed in order).
 constexpr size_t kMaxChainK = 4096;
 
-// Number of K splits for a GEMM: enough CTAs to cover the SMs, whole 256-K
-// super-stages, and no accumulation chain longer than kMaxChainK.
+// Number of K splits: the persistent grid (one CTA per SM) runs units of
+// (128 rows, K split) round-robin, so pick the split count that minimises the
+// busiest CTA's chunk count (ties go to fewer splits: fewer partials to sum),
+// with whole 256-K super-stages, no empty split and no chain above kMaxChainK.
 int gemm_splits(size_t M, size_t K) {
-  const int tiles = (int)ceil_div(M, kRowsTile);
-  const int sup = (int)ceil_div(K, kSuperK);
-  int s = 1;
-  while (s < 16 && s * 2 <= sup && (tiles * s < sm_count() || ceil_div(K, (size_t)s) > kMaxChainK)) s *= 2;
-  return s;
+  const long tiles = (long)ceil_div(M, kRowsTile);
+  const long sup = (long)ceil_div(K, kSuperK);
+  const long sms = sm_count();
+  int best = 1;
+  long best_cost = -1;
+  for (long s = 1; s <= 16 && s <= sup; ++s) {
+    const long per = (sup + s - 1) / s;       // super-stages per split
+    if ((s - 1) * per >= sup) continue;       // would leave an empty split
+    if ((size_t)per * kSuperK > kMaxChainK && per > 1) continue;
+    const long cost = ((tiles * s + sms - 1) / sms) * per;
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best = (int)s;
+    }
+  }
+  return best;
 }
 
 namespace {
@@ -464,9 +551,11 @@ int gemm_int4_tc(const Int4Weight& w, const CUtensorMap& xmap, const float* xsca
                  size_t ldy, int nsplit, size_t split_stride, const float* bias, cudaStream_t stream) {
   GLC_REQUIRE(gemm_tc_supported(w), "int4 gemm: weight layout not supported by the tensor-core GEMM");
   GLC_REQUIRE(np % 16 == 0 && np >= 16 && np <= 128 && n <= np, "int4 gemm: padded rows %zu (n=%zu)", np, n);
+  GLC_REQUIRE(nsplit >= 1, "int4 gemm: %d splits", nsplit);
   const int chunks = (int)(w.K / kChunkK);
   const int sup = (int)ceil_div(w.K, kSuperK);
   const int per = (int)ceil_div(sup, nsplit) * 4;
+  const int tiles = (int)ceil_div(w.M, kRowsTile);
   const size_t smem = gemm_smem_bytes(np);
   GLC_REQUIRE(smem <= 227 * 1024, "int4 gemm: %zu bytes of shared memory", smem);
   static size_t attr = 0;
@@ -475,13 +564,37 @@ int gemm_int4_tc(const Int4Weight& w, const CUtensorMap& xmap, const float* xsca
     if (rc) return rc;
     attr = smem;
   }
-  int* err = nullptr;
-  GLC_CHECK_CUDA(cudaGetSymbolAddress((void**)&err, g_gemm_error));
-  int nib_slots, a_slots, b_slots;
-  gemm_slots(np, &nib_slots, &a_slots, &b_slots);
-  GemmParams prm{xscale, bias, y, ldy, split_stride, (int)w.M, (int)w.K, (int)n, (int)np, chunks, per,
-                 nib_slots, a_slots, b_slots, err};
-  dim3 grid((unsigned)ceil_div(w.M, kRowsTile), (unsigned)nsplit);
+  static int* err = nullptr;
+  if (!err) GLC_CHECK_CUDA(cudaGetSymbolAddress((void**)&err, g_gemm_error));
+  int nib_slots, b_slots;
+  gemm_slots(np, &nib_slots, &b_slots);
+  // Accumulator columns: 2*np (hi | lo products), a power of two >= 32; two
+  // buffers when they fit beside the A ring in the 512 TMEM columns.
+  int acc_cols = 32;
+  while (acc_cols < (int)(2 * np)) acc_cols *= 2;
+  const int acc_bufs = (2 * acc_cols + kASlots * (int)kAColsPerSlot <= (int)kTmemCols) ? 2 : 1;
+  GLC_REQUIRE(acc_bufs * acc_cols + kASlots * (int)kAColsPerSlot <= (int)kTmemCols, "int4 gemm: TMEM budget");
+  GemmParams prm{};
+  prm.xscale = xscale;
+  prm.bias = bias;
+  prm.y = y;
+  prm.ldy = ldy;
+  prm.split_stride = split_stride;
+  prm.M = (int)w.M;
+  prm.K = (int)w.K;
+  prm.n = (int)n;
+  prm.np = (int)np;
+  prm.chunks_total = chunks;
+  prm.chunks_per_split = per;
+  prm.nsplit = nsplit;
+  prm.tiles = tiles;
+  prm.units = tiles * nsplit;
+  prm.nib_slots = nib_slots;
+  prm.b_slots = b_slots;
+  prm.acc_cols = acc_cols;
+  prm.acc_bufs = acc_bufs;
+  prm.err = err;
+  const int grid = std::min(prm.units, sm_count());
   gemm_tc_kernel<<<grid, kThreads, smem, stream>>>(w.tmap_w, w.tmap_s, xmap, prm);
   GLC_CHECK_LAUNCH();
   return GLACIER_CUDA_OK;
