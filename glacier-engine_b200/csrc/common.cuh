@@ -207,6 +207,33 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   }
 }
 
+// Non-blocking probe of a phase (no suspension), for the one thread on a
+// pipeline's critical path: a satisfied try_wait costs it hundreds of cycles.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded polling wait built on mbar_test_wait (same limit as mbar_wait).
+__device__ __forceinline__ bool mbar_wait_poll(uint64_t* bar, uint32_t parity, int* err) {
+  if (mbar_test_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+#pragma unroll 1
+  for (int it = 1;; ++it) {
+    if (mbar_test_wait(bar, parity)) return true;
+    if ((it & 63) == 0 && clock64() - t0 > kSpinLimitCycles) {
+      if (err) atomicExch(err, kErrTimeout);
+      return false;
+    }
+  }
+}
+
 // ---- TMA ---------------------------------------------------------------------
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar,
                                             uint64_t policy) {

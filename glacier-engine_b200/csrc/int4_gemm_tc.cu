@@ -51,6 +51,7 @@ constexpr int kMaxSlots = 8;                    // shared-memory ring slots (run
 constexpr int kConvWarps = 8;                   // two converter warps per TMEM lane quarter
 constexpr int kEpiWarps = 4;                    // one epilogue warp per TMEM lane quarter
 constexpr int kASlots = 4;                      // A chunks (-Whi | Wlo) resident in TMEM
+constexpr int kDoneRing = 8;                    // chunk-completion barriers (>= kASlots and >= B slots)
 constexpr uint32_t kAColsPerSlot = 64;          // 32 columns of -Whi + 32 of Wlo (2 fp16 per column)
 constexpr uint32_t kTmemCols = 512;             // the whole TMEM of the SM (one CTA per SM)
 constexpr int kNibBytes = kRowsTile * 128;      // 128 rows x 256 codes
@@ -179,10 +180,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
   uint64_t* nib_full = bars;
   uint64_t* nib_empty = nib_full + kMaxSlots;
   uint64_t* b_full = nib_empty + kMaxSlots;
-  uint64_t* b_empty = b_full + kMaxSlots;
-  uint64_t* a_full = b_empty + kMaxSlots;
-  uint64_t* a_empty = a_full + kASlots;
-  uint64_t* acc_full = a_empty + kASlots;
+  uint64_t* done = b_full + kMaxSlots;             // chunk c's MMAs completed: done[c % kDoneRing]
+  uint64_t* a_full = done + kDoneRing;
+  uint64_t* acc_full = a_full + kASlots;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* mma_done = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
@@ -196,14 +196,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
       mbar_init(&nib_full[i], 1);
       mbar_init(&nib_empty[i], kConvWarps);
     }
-    for (int i = 0; i < BS; ++i) {
-      mbar_init(&b_full[i], 1);
-      mbar_init(&b_empty[i], 1);
-    }
-    for (int i = 0; i < kASlots; ++i) {
-      mbar_init(&a_full[i], kConvWarps);
-      mbar_init(&a_empty[i], 1);
-    }
+    for (int i = 0; i < BS; ++i) mbar_init(&b_full[i], 1);
+    for (int i = 0; i < kDoneRing; ++i) mbar_init(&done[i], 1);
+    for (int i = 0; i < kASlots; ++i) mbar_init(&a_full[i], kConvWarps);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], kEpiWarps);
@@ -229,18 +224,18 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
       prefetch_tmap(&tmap_w);
       prefetch_tmap(&tmap_s);
       const uint64_t pol = l2_evict_first_policy();
-      uint32_t it = 0;
+      uint32_t it = 0, slot = 0, ph = 0;
       for (int u = blockIdx.x; u < p.units && !s_abort; u += gridDim.x) {
         const Unit w = unit_of(p, u);
         const int nsup = (w.nch + 3) / 4;
         for (int i = 0; i < nsup; ++i, ++it) {
-          const int slot = it % NS;
-          if (!mbar_wait(&nib_empty[slot], ((it / NS) & 1) ^ 1, p.err)) { s_abort = 1; break; }
+          if (!mbar_wait(&nib_empty[slot], ph ^ 1, p.err)) { s_abort = 1; break; }
           uint8_t* dst = nib + slot * (kNibBytes + kSclBytes);
           mbar_arrive_expect_tx(&nib_full[slot], kNibBytes + kSclBytes);
           const int ks = w.c0 / 4 + i;  // super-stage index along K
           tma_load_2d(dst, &tmap_w, ks * 128, w.row0, &nib_full[slot], pol);
           tma_load_2d(dst + kNibBytes, &tmap_s, ks * 8, w.row0, &nib_full[slot], pol);
+          if (++slot == (uint32_t)NS) { slot = 0; ph ^= 1; }
         }
       }
       // Leave no copy in flight (matters only when a wait gave up).
@@ -253,14 +248,18 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
       prefetch_tmap(&tmap_x);
       uint64_t keep;
       asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(keep));
-      uint32_t it = 0;
+      uint32_t it = 0, slot = 0, prev = 0;  // chunk counter, its B slot, chunk that last held the slot
       for (int u = blockIdx.x; u < p.units && !s_abort; u += gridDim.x) {
         const Unit w = unit_of(p, u);
         for (int i = 0; i < w.nch; ++i, ++it) {
-          const int slot = it % BS;
-          if (!mbar_wait(&b_empty[slot], ((it / BS) & 1) ^ 1, p.err)) { s_abort = 1; break; }
+          // The slot last held chunk it - BS; wait until its MMAs completed.
+          if (it >= (uint32_t)BS) {
+            if (!mbar_wait(&done[prev % kDoneRing], (prev / kDoneRing) & 1, p.err)) { s_abort = 1; break; }
+            ++prev;
+          }
           mbar_arrive_expect_tx(&b_full[slot], (uint32_t)bbytes);
           tma_load_2d(btile + slot * bbytes, &tmap_x, (w.c0 + i) * kChunkK, 0, &b_full[slot], keep);
+          if (++slot == (uint32_t)BS) slot = 0;
         }
       }
       for (uint32_t i = it > (uint32_t)BS ? it - BS : 0; i < it; ++i)
@@ -271,7 +270,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     if (lane == 0) {
       // A holds -Whi (negated back by the descriptor) and Wlo.
       const uint32_t id_hl = idesc_f16(2 * p.np, true), id_h = idesc_f16(p.np);
+      const uint64_t bdesc0 = sdesc(smem_u32(btile));
+      const uint64_t bstep = (uint64_t)(bbytes >> 4);  // descriptor address units per B slot
       uint32_t ch = 0, acc_i = 0;
+      uint32_t as = 0, a_ph = 0, bs = 0, b_ph = 0;  // ring positions and phases, advanced per chunk
       for (int u = blockIdx.x; u < p.units && !s_abort; u += gridDim.x) {
         const Unit w = unit_of(p, u);
         if (w.nch == 0) continue;
@@ -282,23 +284,24 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
         const uint32_t d = tmem + (uint32_t)(ab * p.acc_cols);
         bool ok = true;
         for (int i = 0; i < w.nch; ++i, ++ch) {
-          const int as = ch % kASlots, bs = ch % BS;
-          if (!mbar_wait(&a_full[as], (ch / kASlots) & 1, p.err) || !mbar_wait(&b_full[bs], (ch / BS) & 1, p.err)) {
+          if (!mbar_wait_poll(&b_full[bs], b_ph, p.err) || !mbar_wait_poll(&a_full[as], a_ph, p.err)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t ahi = tmem + a_base + (uint32_t)as * kAColsPerSlot;
           const uint32_t alo = ahi + kAColsPerSlot / 2;
-          const uint32_t bx = smem_u32(btile + bs * bbytes);
+          const uint64_t bd = bdesc0 + (uint64_t)bs * bstep;  // +2 per 16-K step (32 bytes)
+          umma_f16_ts(d, ahi, bd, id_hl, i > 0 ? 1u : 0u);     // Whi x [Xhi | Xlo]
+          umma_f16_ts(d, alo, bd, id_h, 1u);                   // Wlo x Xhi
 #pragma unroll
-          for (int kk = 0; kk < kChunkK / 16; ++kk) {
-            const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
-            umma_f16_ts(d, ahi + kk * 8, sdesc(bx + kk * 32), id_hl, acc);  // Whi x [Xhi | Xlo]
-            umma_f16_ts(d, alo + kk * 8, sdesc(bx + kk * 32), id_h, 1u);    // Wlo x Xhi
+          for (int kk = 1; kk < kChunkK / 16; ++kk) {
+            umma_f16_ts(d, ahi + kk * 8, bd + 2 * kk, id_hl, 1u);
+            umma_f16_ts(d, alo + kk * 8, bd + 2 * kk, id_h, 1u);
           }
-          umma_commit(&a_empty[as]);
-          umma_commit(&b_empty[bs]);
+          umma_commit(&done[ch % kDoneRing]);  // frees A slot ch % kASlots and B slot ch % BS
+          if (++as == (uint32_t)kASlots) { as = 0; a_ph ^= 1; }
+          if (++bs == (uint32_t)BS) { bs = 0; b_ph ^= 1; }
         }
         if (!ok) { s_abort = 1; break; }
         umma_commit(&acc_full[ab]);  // fires when every MMA of this unit has completed
@@ -314,14 +317,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     const int rrow = quarter * 32 + lane;
     const uint32_t swz = (uint32_t)(rrow & 7);
     const uint32_t tlane = tmem + ((uint32_t)(quarter * 32) << 16) + a_base + (uint32_t)(16 * hf);
-    uint32_t ch = 0, nsi = 0;
+    uint32_t ch = 0, ns = 0, ns_ph = 0;  // chunk counter; nibble slot and phase
     for (int u = blockIdx.x; u < p.units && !s_abort; u += gridDim.x) {
       const Unit w = unit_of(p, u);
       bool ok = true;
       for (int i = 0; i < w.nch; ++i, ++ch) {
         const int sub = i & 3;
-        const int ns = nsi % NS;
-        if (sub == 0 && !__all_sync(0xffffffffu, mbar_wait(&nib_full[ns], (nsi / NS) & 1, p.err))) {
+        if (sub == 0 && !__all_sync(0xffffffffu, mbar_wait(&nib_full[ns], ns_ph, p.err))) {
           ok = false;
           break;
         }
@@ -345,9 +347,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
             lo[4 * j + e] = hfma2_u32(q[e], s2, hi[4 * j + e]);  // q*s - RN(q*s), exact
           }
         }
-        if (!__all_sync(0xffffffffu, mbar_wait(&a_empty[as], ((ch / kASlots) & 1) ^ 1, p.err))) {
-          ok = false;
-          break;
+        // The A slot last held chunk ch - kASlots; wait until its MMAs completed.
+        if (ch >= (uint32_t)kASlots) {
+          const uint32_t prev = ch - kASlots;
+          if (!__all_sync(0xffffffffu, mbar_wait(&done[prev % kDoneRing], (prev / kDoneRing) & 1, p.err))) {
+            ok = false;
+            break;
+          }
         }
         tc_fence_after();
         const uint32_t ta = tlane + (uint32_t)as * kAColsPerSlot;
@@ -360,7 +366,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
           mbar_arrive(&a_full[as]);
           if (sub == 3 || i == w.nch - 1) mbar_arrive(&nib_empty[ns]);
         }
-        if (sub == 3 || i == w.nch - 1) ++nsi;
+        if (sub == 3 || i == w.nch - 1) {
+          if (++ns == (uint32_t)NS) { ns = 0; ns_ph ^= 1; }
+        }
       }
       if (!ok) { s_abort = 1; break; }
     }
@@ -482,7 +490,7 @@ int encode_split_map(CUtensorMap* map, const __half* xs, size_t np, size_t K) {
 static void gemm_slots(size_t np, int* nib, int* b) {
   *nib = 4;
   *b = kMaxSlots;
-  const size_t fixed = 1024 + (size_t)(4 * kMaxSlots + 2 * kASlots + 5) * 8 + 16;
+  const size_t fixed = 1024 + (size_t)(3 * kMaxSlots + kDoneRing + kASlots + 5) * 8 + 16;
   auto bytes = [&]() { return fixed + (size_t)*nib * (kNibBytes + kSclBytes) + (size_t)*b * 2 * np * 128; };
   while (bytes() > 227 * 1024 && *b > 3) --*b;
   while (bytes() > 227 * 1024 && *nib > 2) --*nib;
@@ -492,7 +500,7 @@ static void gemm_slots(size_t np, int* nib, int* b) {
 size_t gemm_smem_bytes(size_t np) {
   int nib, b;
   gemm_slots(np, &nib, &b);
-  const size_t bytes = 1024 + (size_t)(4 * kMaxSlots + 2 * kASlots + 5) * 8 + 16 +
+  const size_t bytes = 1024 + (size_t)(3 * kMaxSlots + kDoneRing + kASlots + 5) * 8 + 16 +
                        (size_t)nib * (kNibBytes + kSclBytes) + (size_t)b * 2 * np * 128;
   return bytes < (size_t)kMinSmem ? (size_t)kMinSmem : bytes;
 }
