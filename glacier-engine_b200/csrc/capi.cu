@@ -109,6 +109,7 @@ int encode_split_map(CUtensorMap* map, const __half* xs, size_t np, size_t K);
 int gemm_int4_tc(const Int4Weight& w, const CUtensorMap& xmap, const float* xscale, size_t n, size_t np, float* y,
                  size_t ldy, int nsplit, size_t split_stride, const float* bias, cudaStream_t stream);
 int gemm_device_error(int clear);
+int attn_device_error(int clear);
 int gemm_splits(size_t M, size_t K);
 int reduce_splits(const float* part, size_t split_stride, int nsplit, float* y, size_t n, cudaStream_t stream);
 
@@ -126,9 +127,10 @@ unsigned long long glacier_cuda_launch_count(void) { return g_launches.load(std:
 
 int glacier_cuda_device_status(int clear) {
   GLC_CHECK_CUDA(cudaDeviceSynchronize());
-  const int v = gemv_device_error(clear), w = ops_device_error(clear), g = gemm_device_error(clear);
-  if (v < 0 || w < 0 || g < 0) return set_error(GLACIER_CUDA_ECUDA, "device status read failed");
-  return (v || g) ? 1 : (w ? 2 : 0);
+  const int v = gemv_device_error(clear), w = ops_device_error(clear), g = gemm_device_error(clear),
+            a = attn_device_error(clear);
+  if (v < 0 || w < 0 || g < 0 || a < 0) return set_error(GLACIER_CUDA_ECUDA, "device status read failed");
+  return (v || g || a) ? 1 : (w ? 2 : 0);
 }
 
 int glacier_cuda_int4_matvec_f32(const float* x, const uint8_t* packed, const float* scales,

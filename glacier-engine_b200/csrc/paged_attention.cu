@@ -7,27 +7,23 @@
 // (src/paged_kv_cache.zig:1421-1442); block_tables[lane][logical page] gives
 // the physical page.
 //
-// B200 design (flash-decoding): the context is split into chunks; one CTA owns
-// (lane, kv head, chunk) and serves all G = H/Hkv query heads of the GQA
-// group from a single read of each K and V row (the reference's shared-KV
-// tile, forward.zig:544-620).  Pass 1: each warp takes 8 positions at a time,
-// four lanes per position (a quarter of the head dims each, contiguous K loads,
-// q from bank-padded shared memory, packed fp32x2 FMAs, a two-step shuffle
-// reduction).  Pass 2: per-head chunk max and exp-sum.  Pass 3: lanes over head
-// dims accumulate p * V from coalesced V rows with packed FMAs.
-// A combine kernel merges the chunks with the usual max/sum rescaling, in
-// chunk order (deterministic).
+// B200 design (flash-decoding over TMA-fed warps): the context of each
+// (lane, kv head) is cut into chunks; warps claim chunks dynamically and serve
+// all G = H/Hkv query heads of the GQA group from a single read of each K and V
+// row (the reference's shared-KV tile, forward.zig:544-620).  A combine kernel
+// merges a lane's chunks with the usual max/sum rescaling, in chunk order
+// (deterministic).
 #include <type_traits>
 
 #include "common.cuh"
 
 namespace glacier {
 
+__device__ int g_attn_error;
+
 namespace {
 
-constexpr int kAttnThreads = 128;  // 4 warps
-constexpr int kMaxGroup = 8;       // query heads per kv head
-constexpr int kBlock = 8;          // positions per warp iteration
+constexpr int kMaxGroup = 8;  // query heads per kv head
 
 struct AttnParams {
   const float* q;  // [lanes, H*hd]
@@ -45,220 +41,305 @@ struct AttnParams {
   float* part_ml;               // [lanes, H, nsplit, 2]  (max, sum)
 };
 
-// Pass 1 maps a warp onto 8 positions x 4 head-dim slices (HD/4 dims per lane,
-// contiguous 16-byte loads of each K row), pass 3 onto head dims (HD/32 per
-// lane, one coalesced row load per position).
-template <int HD>
-__global__ void __launch_bounds__(kAttnThreads) attn_chunk_kernel(const AttnParams p) {
-  constexpr int SL = HD / 4;      // dims per lane in pass 1
-  constexpr int SL4 = SL / 4;     // float4 per lane in pass 1
-  constexpr int QPITCH = SL + 4;  // padded q slice pitch (floats): slices land in different banks
-  constexpr int DPL = HD / 32;    // dims per lane in pass 3
-  extern __shared__ float sm[];
-  float* qs = sm;                                  // [G][4 slices][QPITCH]
-  float* sc = qs + kMaxGroup * 4 * QPITCH;         // [chunk][8]  scores, then probabilities
-  float* red = sc + (size_t)p.chunk * kMaxGroup;   // [4 warps][G][HD] pass-3 partials
-  __shared__ float mx[kMaxGroup], wred[kAttnThreads / 32][kMaxGroup];
+// ---------------------------------------------------------------------------
+// TMA-fed persistent form.  Work item = (lane, kv head, chunk of positions);
+// every warp owns a private ring of half-page stages (8 positions of K and V
+// of one kv head) and walks its own list of items (gw, gw + total warps, ...),
+// so no warp ever waits for another:
+//   * lane 0 streams each stage's K and V tiles (8 rows x HD floats, two 2D TMA
+//     boxes over the pool viewed as [rows, kv_dim]) into the next free slot,
+//     running kAttnStages stages ahead across item boundaries;
+//   * scores: 16 lanes per position, 2 positions per step, q of all G heads in
+//     registers (HD/16 dims per lane, interleaved so a step's shared-memory
+//     reads are conflict-free), packed fp32x2 FMAs and a butterfly that leaves
+//     lanes (16p + 2h, 16p + 2h + 1) with the score of position p, head h;
+//   * online softmax per stage (running max and sum per head, acc rescaled);
+//   * P.V: lanes over head dims, V rows and probabilities from shared memory.
+// Each item writes one (max, sum, unnormalised o) partial for the combine.
+constexpr int kAttnWarps = 8;   // warps per CTA (one CTA per SM)
+constexpr int kAttnStages = 3;  // half-page stages per warp
+constexpr int kStageRows = 8;   // positions per stage
 
-  const int lane_id = blockIdx.z;
-  const int kvh = blockIdx.y;
-  const int split = blockIdx.x;
-  const int G = p.group;
-  const int ctx = p.ctx_lens[lane_id];
-  const int j0 = split * p.chunk;
-  const int j1 = min(ctx, j0 + p.chunk);
-  const int n = j1 - j0;
-  const int kv_dim = p.num_kv_heads * HD;
+__device__ __forceinline__ void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// 2^x on the special-function unit (relative error about 2^-22; results below
+// the normal range flush to zero, far below what a softmax weight can matter).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// NG = query heads per kv head (compile time); HD = head dim.
+template <int HD, int NG>
+__global__ void __launch_bounds__(kAttnWarps * 32, 1)
+    attn_tma_kernel(const __grid_constant__ CUtensorMap kvmap, const AttnParams p, int lanes, int rows_per_page,
+                    int* work_counter, int* err) {
+  constexpr int TILE = kStageRows * HD;  // floats per K (or V) stage tile of one kv head
+  constexpr int DL = HD / 16;            // score phase: dims per lane (16 lanes per position)
+  constexpr int DL4 = DL / 4;
+  constexpr int VD = HD / 32;            // P.V phase: dims per lane
+  constexpr float kLog2e = 1.4426950408889634f;
+  extern __shared__ __align__(128) float sm[];
+  __shared__ uint64_t bars[kAttnWarps][kAttnStages];
+  __shared__ __align__(16) float scr_all[kAttnWarps][kStageRows * kMaxGroup];
+  __shared__ __align__(16) float2 prb_all[kAttnWarps][kStageRows * kMaxGroup];  // {p, p} per (position, head)
+  __shared__ int queue[kAttnWarps][8];  // items claimed by lane 0, in issue order (-1 ends the list)
+
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const size_t part_base = ((size_t)lane_id * p.num_heads + (size_t)kvh * G) * p.nsplit + split;
-
-  if (n <= 0) {  // empty chunk: neutral partial (max -inf, sum 0)
-    for (int g = threadIdx.x; g < G; g += blockDim.x) {
-      p.part_ml[(part_base + (size_t)g * p.nsplit) * 2 + 0] = -INFINITY;
-      p.part_ml[(part_base + (size_t)g * p.nsplit) * 2 + 1] = 0.f;
-    }
-    return;
+  const int l16 = lane & 15, ph = lane >> 4;
+  float* ring = sm + (size_t)warp * kAttnStages * 2 * TILE;
+  float* scr = scr_all[warp];
+  float2* prb = prb_all[warp];
+  constexpr int G = NG;
+  const int Hkv = p.num_kv_heads;
+  const int total = lanes * Hkv * p.nsplit;
+  if (lane == 0) {
+    for (int i = 0; i < kAttnStages; ++i) mbar_init(&bars[warp][i], 1);
+    fence_mbar_init();
   }
-  for (int i = threadIdx.x; i < kMaxGroup * HD; i += blockDim.x) {
-    const int g = i / HD, d = i % HD;
-    const float v = g < G ? p.q[lane_id * p.ldq + (size_t)(kvh * G + g) * HD + d] * p.scale : 0.f;
-    qs[(g * 4 + d / SL) * QPITCH + d % SL] = v;
-  }
-  __syncthreads();
+  __syncwarp();
 
-  const int32_t* bt = p.block_tables + (size_t)lane_id * p.max_pages;
-  const size_t k_off = (size_t)(p.layer * 2 + 0) * 16 * kv_dim + (size_t)kvh * HD;
-  const size_t v_off = (size_t)(p.layer * 2 + 1) * 16 * kv_dim + (size_t)kvh * HD;
-  const int nblocks = (n + kBlock - 1) / kBlock;
+  // Items are numbered split-major (all lanes' first chunks, then the second
+  // ones, ...) and claimed dynamically, so long contexts do not pile up on
+  // some warps.  Stages of item `it` (0 when the chunk lies past the context).
+  auto item_stages = [&](int it, int& lid, int& kvh, int& split, int& n) {
+    split = it / (lanes * Hkv);
+    const int r = it - split * lanes * Hkv;
+    lid = r / Hkv;
+    kvh = r - lid * Hkv;
+    const int ctx = p.ctx_lens[lid];
+    const int j0 = split * p.chunk;
+    n = max(0, min(ctx, j0 + p.chunk) - j0);
+    return (n + kStageRows - 1) / kStageRows;
+  };
 
-  // ---- pass 1: scores = (q * scale) . k for the G heads -------------------------
-  // The K loads of the warp's next block are issued before the current block is
-  // consumed (register double buffering), so every lane keeps 2 x HD/4 floats in flight.
-  {
-    const int pp = lane >> 2, sl = lane & 3;
-    auto krow_of = [&](int bk) {
-      const int j = j0 + min(bk * kBlock + pp, n - 1);  // clamp the tail to a valid row
-      return reinterpret_cast<const float4*>(p.pool + (size_t)bt[j >> 4] * p.page_floats + k_off +
-                                             (size_t)(j & 15) * kv_dim + sl * SL);
-    };
-    float4 kv[SL4], kn[SL4];
-    int bk = warp;
-    if (bk < nblocks) {
-      const float4* kr = krow_of(bk);
-#pragma unroll
-      for (int i = 0; i < SL4; ++i) kv[i] = __ldg(kr + i);
-    }
-    for (; bk < nblocks; bk += kAttnThreads / 32) {
-      const int bn = bk + kAttnThreads / 32;
-      if (bn < nblocks) {
-        const float4* kr = krow_of(bn);
-#pragma unroll
-        for (int i = 0; i < SL4; ++i) kn[i] = __ldg(kr + i);
+  // ---- issue cursor (lane 0): the next stage of this warp's sequence ----
+  int c_item = 0, c_st = 0, c_ns = 0, c_lid = 0, c_kvh = 0, c_split = 0, c_n = 0;
+  uint32_t claimed = 0;
+  bool drained = false;  // no work left to claim (the -1 marker is queued)
+  auto claim = [&]() {  // lane 0: next non-empty item into the queue, or the end marker
+    while (true) {
+      const int it = atomicAdd(work_counter, 1);
+      if (it >= total) {
+        queue[warp][claimed++ & 7] = -1;
+        drained = true;
+        return;
       }
-      const int jj = bk * kBlock + pp;
-      float2 acc[kMaxGroup];
+      const int ns = item_stages(it, c_lid, c_kvh, c_split, c_n);
+      if (ns > 0) {
+        c_item = it;
+        c_ns = ns;
+        c_st = 0;
+        queue[warp][claimed++ & 7] = it;
+        return;
+      }
+    }
+  };
+  if (lane == 0) claim();
+  uint64_t pol = 0;
+  if (lane == 0) {
+    prefetch_tmap(&kvmap);
+    pol = l2_evict_first_policy();
+  }
+  uint32_t issued = 0;
+  auto issue_next = [&]() {  // lane 0 only
+    if (drained) return;
+    if (c_st >= c_ns) {
+      claim();
+      if (drained) return;
+    }
+    const int s = issued % kAttnStages;
+    const int j = c_split * p.chunk + c_st * kStageRows;  // first position of the stage
+    const int phys = p.block_tables[(size_t)c_lid * p.max_pages + (j >> 4)];
+    const int yk = phys * rows_per_page + p.layer * 32 + (j & 15);
+    float* dst = ring + (size_t)s * 2 * TILE;
+    mbar_arrive_expect_tx(&bars[warp][s], 2 * TILE * (uint32_t)sizeof(float));
+    tma_load_2d(dst, &kvmap, c_kvh * HD, yk, &bars[warp][s], pol);
+    tma_load_2d(dst + TILE, &kvmap, c_kvh * HD, yk + 16, &bars[warp][s], pol);
+    ++issued;
+    ++c_st;
+  };
+  if (lane == 0)
+    for (int i = 0; i < kAttnStages; ++i) issue_next();
+
+  uint32_t consumed = 0, taken = 0;
+  bool ok = true;
+  while (ok) {
+    __syncwarp();
+    const int item = queue[warp][taken++ & 7];
+    if (item < 0) break;
+    int lid, kvh, split, n;
+    const int nst = item_stages(item, lid, kvh, split, n);
+    const size_t part_base = ((size_t)lid * p.num_heads + (size_t)kvh * G) * p.nsplit + split;
+    // q of the G heads, scaled by 1/sqrt(hd) * log2(e) (softmax in base 2), this
+    // lane's dims 4*l16 + 64*i + c.
+    const float qs = p.scale * kLog2e;
+    float2 q2[NG][DL / 2];
+    const float* qrow = p.q + (size_t)lid * p.ldq + (size_t)kvh * G * HD;
 #pragma unroll
-      for (int g = 0; g < kMaxGroup; ++g) acc[g] = make_float2(0.f, 0.f);
+    for (int g = 0; g < NG; ++g) {
 #pragma unroll
-      for (int i = 0; i < SL4; ++i) {
+      for (int i = 0; i < DL4; ++i) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(qrow + (size_t)g * HD + 4 * l16 + 64 * i));
+        q2[g][2 * i] = make_float2(v.x * qs, v.y * qs);
+        q2[g][2 * i + 1] = make_float2(v.z * qs, v.w * qs);
+      }
+    }
+    float m[NG], l[NG];
+    float2 acc[NG][VD / 2];
 #pragma unroll
-        for (int g = 0; g < kMaxGroup; ++g) {
-          if (g < G) {
-            const float4 qv = *reinterpret_cast<const float4*>(qs + (g * 4 + sl) * QPITCH + 4 * i);
-            acc[g] = __ffma2_rn(make_float2(qv.x, qv.y), make_float2(kv[i].x, kv[i].y), acc[g]);
-            acc[g] = __ffma2_rn(make_float2(qv.z, qv.w), make_float2(kv[i].z, kv[i].w), acc[g]);
+    for (int g = 0; g < NG; ++g) {
+      m[g] = -INFINITY;
+      l[g] = 0.f;
+#pragma unroll
+      for (int i = 0; i < VD / 2; ++i) acc[g][i] = make_float2(0.f, 0.f);
+    }
+    for (int st = 0; st < nst; ++st, ++consumed) {
+      const int s = consumed % kAttnStages;
+      if (!__all_sync(0xffffffffu, mbar_wait(&bars[warp][s], (consumed / kAttnStages) & 1, err))) {
+        ok = false;
+        break;
+      }
+      const float* Kt = ring + (size_t)s * 2 * TILE;
+      const float* Vt = Kt + TILE;
+      const int nvalid = min(kStageRows, n - kStageRows * st);
+      // -- scores (base-2 logits) for 8 positions, 2 per step --
+#pragma unroll
+      for (int step = 0; step < kStageRows / 2; ++step) {
+        const int pos = 2 * step + ph;
+        float4 kv[DL4];
+#pragma unroll
+        for (int i = 0; i < DL4; ++i) kv[i] = *reinterpret_cast<const float4*>(Kt + pos * HD + 4 * l16 + 64 * i);
+        float v[kMaxGroup];
+#pragma unroll
+        for (int g = NG; g < kMaxGroup; ++g) v[g] = 0.f;
+#pragma unroll
+        for (int g = 0; g < NG; ++g) {
+          float2 a = __fmul2_rn(q2[g][0], make_float2(kv[0].x, kv[0].y));
+          a = __ffma2_rn(q2[g][1], make_float2(kv[0].z, kv[0].w), a);
+#pragma unroll
+          for (int i = 1; i < DL4; ++i) {
+            a = __ffma2_rn(q2[g][2 * i], make_float2(kv[i].x, kv[i].y), a);
+            a = __ffma2_rn(q2[g][2 * i + 1], make_float2(kv[i].z, kv[i].w), a);
           }
+          v[g] = a.x + a.y;
+        }
+        // Butterfly over the 16 lanes of this position: lanes 2h, 2h+1 end with head h.
+        const bool b8 = (l16 & 8) != 0, b4 = (l16 & 4) != 0, b2 = (l16 & 2) != 0;
+        float w4[4], w2[2];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float send = b8 ? v[k] : v[k + 4];
+          const float keep = b8 ? v[k + 4] : v[k];
+          w4[k] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+        }
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          const float send = b4 ? w4[k] : w4[k + 2];
+          const float keep = b4 ? w4[k + 2] : w4[k];
+          w2[k] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+        }
+        const float send = b2 ? w2[0] : w2[1];
+        const float keep = b2 ? w2[1] : w2[0];
+        float sc = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+        sc += __shfl_xor_sync(0xffffffffu, sc, 1);
+        const int h = l16 >> 1;
+        if (h >= G || (nvalid < kStageRows && pos >= nvalid)) sc = -INFINITY;
+        if ((l16 & 1) == 0) scr[pos * kMaxGroup + h] = sc;
+      }
+      __syncwarp();
+      // -- online softmax over this stage: lane = (head lane & 7, positions (lane >> 3) + 4k) --
+      const int hh = lane & 7, r0 = lane >> 3;
+      const float s0 = scr[r0 * kMaxGroup + hh], s1 = scr[(r0 + 4) * kMaxGroup + hh];
+      float mp = fmaxf(s0, s1);
+      mp = fmaxf(mp, __shfl_xor_sync(0xffffffffu, mp, 8));
+      mp = fmaxf(mp, __shfl_xor_sync(0xffffffffu, mp, 16));
+      float alpha[NG], mh = 0.f;
+#pragma unroll
+      for (int g = 0; g < NG; ++g) {
+        const float mn = fmaxf(m[g], __shfl_sync(0xffffffffu, mp, g));
+        alpha[g] = (m[g] == -INFINITY) ? 0.f : ex2_approx(m[g] - mn);
+        m[g] = mn;
+        if (g == hh) mh = mn;
+      }
+      // Masked scores are -inf and give ex2(-inf) = 0; padding heads (hh >= G) are zeroed.
+      const float e0 = hh < G ? ex2_approx(s0 - mh) : 0.f;
+      const float e1 = hh < G ? ex2_approx(s1 - mh) : 0.f;
+      prb[r0 * kMaxGroup + hh] = make_float2(e0, e0);
+      prb[(r0 + 4) * kMaxGroup + hh] = make_float2(e1, e1);
+      float ps = e0 + e1;
+      ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+      ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+#pragma unroll
+      for (int g = 0; g < NG; ++g) {
+        l[g] = l[g] * alpha[g] + __shfl_sync(0xffffffffu, ps, g);
+        const float2 a2 = make_float2(alpha[g], alpha[g]);
+#pragma unroll
+        for (int i = 0; i < VD / 2; ++i) acc[g][i] = __fmul2_rn(acc[g][i], a2);
+      }
+      __syncwarp();
+      // -- P.V over the stage (positions past the context carry probability 0
+      //    and are skipped, so stale rows never enter the sum) --
+      auto pv_row = [&](int pos) {
+        float vv[VD];
+        if constexpr (VD == 4) {
+          const float4 t = *reinterpret_cast<const float4*>(Vt + pos * HD + 4 * lane);
+          vv[0] = t.x; vv[1] = t.y; vv[2] = t.z; vv[3] = t.w;
+        } else {
+          const float2 t = *reinterpret_cast<const float2*>(Vt + pos * HD + 2 * lane);
+          vv[0] = t.x; vv[1] = t.y;
+        }
+#pragma unroll
+        for (int g = 0; g < NG; ++g) {
+          const float2 pp = prb[pos * kMaxGroup + g];
+#pragma unroll
+          for (int i = 0; i < VD / 2; ++i)
+            acc[g][i] = __ffma2_rn(pp, make_float2(vv[2 * i], vv[2 * i + 1]), acc[g][i]);
+        }
+      };
+      if (nvalid == kStageRows) {
+#pragma unroll
+        for (int pos = 0; pos < kStageRows; ++pos) pv_row(pos);
+      } else {
+        for (int pos = 0; pos < nvalid; ++pos) pv_row(pos);
+      }
+      __syncwarp();
+      if (lane == 0) {
+        fence_async_shared();  // this slot's generic reads precede the next async write into it
+        issue_next();
+      }
+    }
+    if (!ok) break;
+    // -- partial of this item: unnormalised o, running max (natural log base) and sum --
+#pragma unroll
+    for (int g = 0; g < NG; ++g) {
+      {
+        float* dst = p.part_o + (part_base + (size_t)g * p.nsplit) * HD + VD * lane;
+        if constexpr (VD == 4) {
+          *reinterpret_cast<float4*>(dst) = make_float4(acc[g][0].x, acc[g][0].y, acc[g][1].x, acc[g][1].y);
+        } else {
+          *reinterpret_cast<float2*>(dst) = acc[g][0];
         }
       }
-      float sv[kMaxGroup];
-#pragma unroll
-      for (int g = 0; g < kMaxGroup; ++g) {
-        float v = acc[g].x + acc[g].y;
-        v += __shfl_xor_sync(0xffffffffu, v, 1);
-        v += __shfl_xor_sync(0xffffffffu, v, 2);
-        sv[g] = v;
-      }
-      if (sl == 0 && jj < n) {
-        float4* dst = reinterpret_cast<float4*>(sc + (size_t)jj * kMaxGroup);
-        dst[0] = make_float4(sv[0], sv[1], sv[2], sv[3]);
-        dst[1] = make_float4(sv[4], sv[5], sv[6], sv[7]);
-      }
-#pragma unroll
-      for (int i = 0; i < SL4; ++i) kv[i] = kn[i];
     }
-  }
-  __syncthreads();
-
-  // ---- pass 2: per-head chunk max, exp, sum ---------------------------------------
-  {
-    // thread t covers head g = t & 7 over positions (t >> 3), (t >> 3) + 16, ...
-    const int g = threadIdx.x & 7, r = threadIdx.x >> 3;  // r in 0..15
-    float m = -INFINITY;
-    for (int jj = r; jj < n; jj += 16) m = fmaxf(m, sc[jj * kMaxGroup + g]);
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 8));
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 16));
-    if (lane < 8) wred[warp][g] = m;
-    __syncthreads();
-    if (threadIdx.x < kMaxGroup) {
-      float v = wred[0][threadIdx.x];
-      for (int w = 1; w < kAttnThreads / 32; ++w) v = fmaxf(v, wred[w][threadIdx.x]);
-      mx[threadIdx.x] = v;
-    }
-    __syncthreads();
-    const float mg = mx[g];
-    float sum = 0.f;
-    for (int jj = r; jj < n; jj += 16) {
-      const float e = g < G ? expf(sc[jj * kMaxGroup + g] - mg) : 0.f;
-      sc[jj * kMaxGroup + g] = e;
-      sum += e;
-    }
-    sum += __shfl_xor_sync(0xffffffffu, sum, 8);
-    sum += __shfl_xor_sync(0xffffffffu, sum, 16);
-    __syncthreads();
-    if (lane < 8) wred[warp][g] = sum;
-    __syncthreads();
-    if (threadIdx.x < G) {
-      float v = 0.f;
-      for (int w = 0; w < kAttnThreads / 32; ++w) v += wred[w][threadIdx.x];
-      p.part_ml[(part_base + (size_t)threadIdx.x * p.nsplit) * 2 + 0] = mx[threadIdx.x];
-      p.part_ml[(part_base + (size_t)threadIdx.x * p.nsplit) * 2 + 1] = v;
-    }
-  }
-  __syncthreads();
-
-  // ---- pass 3: o[g][d] = sum_j p[g][j] * v_j[d], lanes over head dims ------------
-  {
-    float2 acc[kMaxGroup][DPL / 2];
+    if (lane < G) {
+      float mm = m[0], ll = l[0];
 #pragma unroll
-    for (int g = 0; g < kMaxGroup; ++g)
-#pragma unroll
-      for (int i = 0; i < DPL / 2; ++i) acc[g][i] = make_float2(0.f, 0.f);
-    // All 8 V rows of a block are loaded before use, and the next block's rows
-    // are in flight while the current block is accumulated.
-    using VecT = typename std::conditional<DPL == 4, float4, float2>::type;
-    auto vrow_of = [&](int bk, int pp) {
-      const int j = j0 + min(bk * kBlock + pp, n - 1);
-      return reinterpret_cast<const VecT*>(p.pool + (size_t)bt[j >> 4] * p.page_floats + v_off +
-                                           (size_t)(j & 15) * kv_dim) + lane;
-    };
-    VecT vc[kBlock], vn[kBlock];
-    int bk = warp;
-    if (bk < nblocks) {
-#pragma unroll
-      for (int pp = 0; pp < kBlock; ++pp) vc[pp] = __ldg(vrow_of(bk, pp));
-    }
-    for (; bk < nblocks; bk += kAttnThreads / 32) {
-      const int bn = bk + kAttnThreads / 32;
-      if (bn < nblocks) {
-#pragma unroll
-        for (int pp = 0; pp < kBlock; ++pp) vn[pp] = __ldg(vrow_of(bn, pp));
-      }
-#pragma unroll
-      for (int pp = 0; pp < kBlock; ++pp) {
-        const int jj = bk * kBlock + pp;
-        if (jj < n) {  // positions past the chunk end carry no probability
-          float vv[DPL];
-          if constexpr (DPL == 4) {
-            vv[0] = vc[pp].x; vv[1] = vc[pp].y; vv[2] = vc[pp].z; vv[3] = vc[pp].w;
-          } else {
-            vv[0] = vc[pp].x; vv[1] = vc[pp].y;
-          }
-          const float4 p0 = *reinterpret_cast<const float4*>(sc + (size_t)jj * kMaxGroup);
-          const float4 p1 = *reinterpret_cast<const float4*>(sc + (size_t)jj * kMaxGroup + 4);
-          const float pg[kMaxGroup] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
-#pragma unroll
-          for (int g = 0; g < kMaxGroup; ++g) {
-            if (g < G) {
-#pragma unroll
-              for (int i = 0; i < DPL / 2; ++i)
-                acc[g][i] = __ffma2_rn(make_float2(pg[g], pg[g]), make_float2(vv[2 * i], vv[2 * i + 1]), acc[g][i]);
-            }
-          }
+      for (int g = 1; g < NG; ++g)
+        if (g == lane) {
+          mm = m[g];
+          ll = l[g];
         }
-      }
-#pragma unroll
-      for (int pp = 0; pp < kBlock; ++pp) vc[pp] = vn[pp];
-    }
-    // reduce the 4 warps' partials through shared memory (scores are no longer needed)
-#pragma unroll
-    for (int g = 0; g < kMaxGroup; ++g) {
-      if (g < G) {
-#pragma unroll
-        for (int i = 0; i < DPL / 2; ++i) {
-          red[((size_t)warp * kMaxGroup + g) * HD + lane * DPL + 2 * i] = acc[g][i].x;
-          red[((size_t)warp * kMaxGroup + g) * HD + lane * DPL + 2 * i + 1] = acc[g][i].y;
-        }
-      }
-    }
-    __syncthreads();
-    for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
-      const int g = i / HD, d = i % HD;
-      float v = 0.f;
-#pragma unroll
-      for (int w = 0; w < kAttnThreads / 32; ++w) v += red[((size_t)w * kMaxGroup + g) * HD + d];
-      p.part_o[(part_base + (size_t)g * p.nsplit) * HD + d] = v;
+      p.part_ml[(part_base + (size_t)lane * p.nsplit) * 2 + 0] = mm / kLog2e;
+      p.part_ml[(part_base + (size_t)lane * p.nsplit) * 2 + 1] = ll;
     }
   }
+  // Leave no copy in flight (a wait that gave up leaves some outstanding).
+  if (lane == 0) {
+    for (uint32_t i = consumed; i < issued; ++i) mbar_wait(&bars[warp][i % kAttnStages], (i / kAttnStages) & 1, err);
+  }
+  __syncwarp();
 }
 
 // out[lane, h, :] = sum_s o_s * e^(m_s - M) / sum_s l_s * e^(m_s - M), in split
@@ -268,20 +349,23 @@ __global__ void __launch_bounds__(kAttnThreads) attn_chunk_kernel(const AttnPara
 __global__ void __launch_bounds__(256) attn_combine_kernel(const float* __restrict__ part_o,
                                                            const float* __restrict__ part_ml, int nsplit, int head_dim,
                                                            int num_heads, float* __restrict__ out, size_t ldo,
-                                                           SplitOut so) {
+                                                           SplitOut so, const int32_t* __restrict__ ctx_lens,
+                                                           int chunk) {
   extern __shared__ float row[];  // this CTA's heads x head_dim (split outputs)
   __shared__ float hm[kMaxGroup * 4], hinv[kMaxGroup * 4];
   __shared__ float sh[32], xch;
   const int lane_id = blockIdx.y;
+  // Only the chunks that hold part of this lane's context have partials.
+  const int nsplit_lane = min(nsplit, (ctx_lens[lane_id] + chunk - 1) / chunk);
   const int cr = (int)cluster_ctarank(), cn = (int)cluster_nctarank();
   const int hpc = (num_heads + cn - 1) / cn;
   const int h0 = min(num_heads, cr * hpc), h1 = min(num_heads, h0 + hpc);
   for (int t = threadIdx.x; t < h1 - h0; t += blockDim.x) {
     const size_t base = ((size_t)lane_id * num_heads + h0 + t) * nsplit;
     float M = -INFINITY;
-    for (int s = 0; s < nsplit; ++s) M = fmaxf(M, part_ml[(base + s) * 2]);
+    for (int s = 0; s < nsplit_lane; ++s) M = fmaxf(M, part_ml[(base + s) * 2]);
     float L = 0.f;
-    for (int s = 0; s < nsplit; ++s) {
+    for (int s = 0; s < nsplit_lane; ++s) {
       const float m = part_ml[(base + s) * 2];
       if (m != -INFINITY) L += part_ml[(base + s) * 2 + 1] * expf(m - M);
     }
@@ -294,7 +378,7 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const float* __restri
     const int t = i / head_dim, d = i % head_dim;
     const size_t base = ((size_t)lane_id * num_heads + h0 + t) * nsplit;
     float acc = 0.f;
-    for (int s = 0; s < nsplit; ++s) {
+    for (int s = 0; s < nsplit_lane; ++s) {
       const float m = part_ml[(base + s) * 2];
       if (m != -INFINITY) acc = fmaf(part_o[(base + s) * head_dim + d], expf(m - hm[t]), acc);
     }
@@ -337,19 +421,57 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const float* __restri
 
 // Workspace floats needed by paged_attention for the given split count.
 size_t attention_workspace_floats(size_t lanes, size_t num_heads, size_t head_dim, size_t nsplit) {
-  return lanes * num_heads * nsplit * (head_dim + 2);
+  return lanes * num_heads * nsplit * (head_dim + 2) + 4;  // + the work counter
 }
 
-// Positions per chunk: splits so that lanes * kv_heads * splits covers the
-// SMs about four times, chunks of 64..512 positions in whole pages.
+// Positions per work item: 256 (16 pages) unless that leaves fewer than two
+// items per warp of the persistent grid, then halved down to 64.
 int attention_chunk(size_t lanes, size_t num_kv_heads, size_t max_ctx) {
-  const size_t units = lanes * num_kv_heads;
-  size_t want = ceil_div(4 * (size_t)sm_count(), units);
-  size_t chunk = ceil_div(max_ctx, want);
-  chunk = ceil_div(chunk, 32) * 32;
-  if (chunk < 64) chunk = 64;
-  if (chunk > 512) chunk = 512;
+  const size_t warps = (size_t)sm_count() * kAttnWarps;
+  size_t chunk = 256;
+  while (chunk > 64 && lanes * num_kv_heads * ceil_div(max_ctx, chunk) < 2 * warps) chunk /= 2;
   return (int)chunk;
+}
+
+int attn_device_error(int clear) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_attn_error, sizeof(int)) != cudaSuccess) return -1;
+  if (clear && v) {
+    int z = 0;
+    cudaMemcpyToSymbol(g_attn_error, &z, sizeof(int));
+  }
+  return v;
+}
+
+// TMA view of a KV pool: [rows, kv_dim] floats, boxes of 16 rows x head_dim;
+// encoded once per (pool, geometry) and cached per host thread.
+static int attn_kv_map(const float* pool, size_t kv_dim, size_t head_dim, const CUtensorMap** out) {
+  struct Entry {
+    const float* pool;
+    size_t kv_dim, head_dim;
+    CUtensorMap map;
+  };
+  thread_local Entry cache[4];
+  thread_local int next = 0;
+  for (auto& e : cache)
+    if (e.pool == pool && e.kv_dim == kv_dim && e.head_dim == head_dim) {
+      *out = &e.map;
+      return GLACIER_CUDA_OK;
+    }
+  Entry& e = cache[next];
+  next = (next + 1) % 4;
+  // Rows cover any pool that fits in device memory; block tables select within it.
+  const uint64_t rows = ((uint64_t)192 << 30) / (kv_dim * sizeof(float));
+  e.pool = nullptr;
+  const int rc = encode_tmap_2d(&e.map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, pool, kv_dim, rows, kv_dim * sizeof(float),
+                                (uint32_t)head_dim, kStageRows, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+  if (rc) return rc;
+  e.pool = pool;
+  e.kv_dim = kv_dim;
+  e.head_dim = head_dim;
+  *out = &e.map;
+  return GLACIER_CUDA_OK;
 }
 
 int paged_attention(const float* q, size_t ldq, const float* pool, size_t page_floats, const int32_t* block_tables,
@@ -388,17 +510,44 @@ int paged_attention(const float* q, size_t ldq, const float* pool, size_t page_f
   prm.scale = 1.0f / sqrtf((float)head_dim);
   prm.part_o = workspace;
   prm.part_ml = workspace + lanes * num_heads * nsplit * head_dim;
-  const size_t smem =
-      ((size_t)kMaxGroup * 4 * (head_dim / 4 + 4) + (size_t)chunk * kMaxGroup + 4 * kMaxGroup * head_dim) * sizeof(float);
-  auto kern = head_dim == 128 ? attn_chunk_kernel<128> : attn_chunk_kernel<64>;
-  static size_t attr[2] = {0, 0};
-  size_t& done = attr[head_dim == 128 ? 1 : 0];
-  if (smem > 48 * 1024 && done < smem) {
-    const int rc = allow_dynamic_smem((const void*)kern, (int)smem);
-    if (rc) return rc;
-    done = smem;
+  const size_t kv_dim = num_kv_heads * head_dim;
+  GLC_REQUIRE(page_floats % kv_dim == 0 && page_floats / kv_dim >= (layer + 1) * 32,
+              "paged_attention: page of %zu floats does not hold layer %zu", page_floats, layer);
+  const CUtensorMap* kvmap = nullptr;
+  int rc = attn_kv_map(pool, kv_dim, head_dim, &kvmap);
+  if (rc) return rc;
+  const size_t smem = (size_t)kAttnWarps * kAttnStages * 2 * kStageRows * head_dim * sizeof(float);
+  using Kern = void (*)(const CUtensorMap, const AttnParams, int, int, int*, int*);
+  Kern kern = nullptr;
+#define GLC_ATTN_CASE(hd, ng) \
+  if (head_dim == hd && group == ng) kern = attn_tma_kernel<hd, ng>;
+  GLC_ATTN_CASE(128, 1) GLC_ATTN_CASE(128, 2) GLC_ATTN_CASE(128, 3) GLC_ATTN_CASE(128, 4)
+  GLC_ATTN_CASE(128, 5) GLC_ATTN_CASE(128, 6) GLC_ATTN_CASE(128, 7) GLC_ATTN_CASE(128, 8)
+  GLC_ATTN_CASE(64, 1) GLC_ATTN_CASE(64, 2) GLC_ATTN_CASE(64, 3) GLC_ATTN_CASE(64, 4)
+  GLC_ATTN_CASE(64, 5) GLC_ATTN_CASE(64, 6) GLC_ATTN_CASE(64, 7) GLC_ATTN_CASE(64, 8)
+#undef GLC_ATTN_CASE
+  GLC_REQUIRE(kern != nullptr, "paged_attention: no kernel for head_dim %zu / group %zu", head_dim, group);
+  {
+    // The shared-memory attribute is per kernel instance; set it once per instance.
+    static const void* ready[16] = {};
+    bool seen = false;
+    for (const void* r : ready) seen |= r == (const void*)kern;
+    if (!seen) {
+      if ((rc = allow_dynamic_smem((const void*)kern, (int)smem))) return rc;
+      for (auto& r : ready)
+        if (!r) {
+          r = (const void*)kern;
+          break;
+        }
+    }
   }
-  kern<<<dim3(nsplit, (unsigned)num_kv_heads, (unsigned)lanes), kAttnThreads, smem, stream>>>(prm);
+  static int* err = nullptr;
+  if (!err) GLC_CHECK_CUDA(cudaGetSymbolAddress((void**)&err, g_attn_error));
+  const size_t items = lanes * num_kv_heads * (size_t)nsplit;
+  const int grid = (int)std::min<size_t>((size_t)sm_count(), ceil_div(items, (size_t)kAttnWarps));
+  int* counter = reinterpret_cast<int*>(workspace + lanes * num_heads * nsplit * (head_dim + 2));
+  GLC_CHECK_CUDA(cudaMemsetAsync(counter, 0, sizeof(int), stream));
+  kern<<<grid, kAttnWarps * 32, smem, stream>>>(*kvmap, prm, (int)lanes, (int)(page_floats / kv_dim), counter, err);
   GLC_CHECK_LAUNCH();
   if (prof) prof->mark(combine_kind, stream);
   {
@@ -421,7 +570,7 @@ int paged_attention(const float* q, size_t ldq, const float* pool, size_t page_f
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     GLC_CHECK_CUDA(cudaLaunchKernelEx(&cfg, attn_combine_kernel, (const float*)prm.part_o, (const float*)prm.part_ml,
-                                      nsplit, (int)head_dim, (int)num_heads, out, ldo, so));
+                                      nsplit, (int)head_dim, (int)num_heads, out, ldo, so, ctx_lens, chunk));
     note_launch();
   }
   return GLACIER_CUDA_OK;
