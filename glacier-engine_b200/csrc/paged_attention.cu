@@ -351,8 +351,7 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const float* __restri
                                                            int num_heads, float* __restrict__ out, size_t ldo,
                                                            SplitOut so, const int32_t* __restrict__ ctx_lens,
                                                            int chunk) {
-  extern __shared__ float row[];  // this CTA's heads x head_dim (split outputs)
-  __shared__ float hm[kMaxGroup * 4], hinv[kMaxGroup * 4];
+  extern __shared__ float dyn[];  // [hpc][nsplit] chunk weights, then (split outputs) hpc x head_dim values
   __shared__ float sh[32], xch;
   const int lane_id = blockIdx.y;
   // Only the chunks that hold part of this lane's context have partials.
@@ -360,29 +359,36 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const float* __restri
   const int cr = (int)cluster_ctarank(), cn = (int)cluster_nctarank();
   const int hpc = (num_heads + cn - 1) / cn;
   const int h0 = min(num_heads, cr * hpc), h1 = min(num_heads, h0 + hpc);
-  for (int t = threadIdx.x; t < h1 - h0; t += blockDim.x) {
+  float* wts = dyn;
+  float* row = dyn + hpc * nsplit;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  // Chunk weights e^(m_s - M) / L per head, one warp per head (lanes over chunks).
+  for (int t = warp; t < h1 - h0; t += nwarps) {
     const size_t base = ((size_t)lane_id * num_heads + h0 + t) * nsplit;
     float M = -INFINITY;
-    for (int s = 0; s < nsplit_lane; ++s) M = fmaxf(M, part_ml[(base + s) * 2]);
+    for (int s = lane; s < nsplit_lane; s += 32) M = fmaxf(M, part_ml[(base + s) * 2]);
+    M = warp_max(M);
     float L = 0.f;
-    for (int s = 0; s < nsplit_lane; ++s) {
+    for (int s = lane; s < nsplit_lane; s += 32) {
       const float m = part_ml[(base + s) * 2];
-      if (m != -INFINITY) L += part_ml[(base + s) * 2 + 1] * expf(m - M);
+      const float e = m == -INFINITY ? 0.f : expf(m - M);
+      wts[t * nsplit + s] = e;
+      L += part_ml[(base + s) * 2 + 1] * e;
     }
-    hm[t] = M;
-    hinv[t] = 1.0f / L;
+    L = warp_sum(L);
+    const float inv = 1.0f / L;
+    for (int s = lane; s < nsplit_lane; s += 32) wts[t * nsplit + s] *= inv;
   }
   __syncthreads();
   float mx = 0.f;
   for (int i = threadIdx.x; i < (h1 - h0) * head_dim; i += blockDim.x) {
     const int t = i / head_dim, d = i % head_dim;
-    const size_t base = ((size_t)lane_id * num_heads + h0 + t) * nsplit;
+    const float* po = part_o + ((size_t)lane_id * num_heads + h0 + t) * nsplit * head_dim + d;
+    const float* wt = wts + t * nsplit;
     float acc = 0.f;
-    for (int s = 0; s < nsplit_lane; ++s) {
-      const float m = part_ml[(base + s) * 2];
-      if (m != -INFINITY) acc = fmaf(part_o[(base + s) * head_dim + d], expf(m - hm[t]), acc);
-    }
-    const float v = acc * hinv[t];
+#pragma unroll 4
+    for (int s = 0; s < nsplit_lane; ++s) acc = fmaf(po[(size_t)s * head_dim], wt[s], acc);
+    const float v = acc;
     if (so.xs) {
       row[i] = v;
       mx = fmaxf(mx, fabsf(v));
@@ -556,7 +562,8 @@ int paged_attention(const float* q, size_t ldq, const float* pool, size_t page_f
     while (cl < 8 && (size_t)cl * 7 < num_heads) cl *= 2;
     const int hpc = (int)ceil_div(num_heads, (size_t)cl);
     GLC_REQUIRE(hpc <= 4 * kMaxGroup, "paged_attention: too many heads per combine CTA");
-    const size_t csmem = so.xs ? (size_t)hpc * head_dim * sizeof(float) : 0;
+    const size_t csmem = ((size_t)hpc * nsplit + (so.xs ? (size_t)hpc * head_dim : 0)) * sizeof(float);
+    GLC_REQUIRE(csmem <= 48 * 1024, "paged_attention: %d chunks per lane exceed the combine's shared memory", nsplit);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)cl, (unsigned)lanes);
     cfg.blockDim = dim3(256);
