@@ -120,6 +120,17 @@ def lane_contexts(args, lanes: int, rank: int) -> np.ndarray:
     return rng.integers(args.ctx_min, args.ctx_max + 1, size=lanes).astype(np.int32)
 
 
+def max_over_ranks(values, world_size: int, device) -> list:
+    """Element-wise maximum of per-rank timings (the job is as slow as its slowest rank)."""
+    if world_size <= 1:
+        return [float(v) for v in values]
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor(values, dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(v) for v in t.tolist()]
+
+
 def cpu_threads() -> int:
     try:
         return max(1, min(16, len(os.sched_getaffinity(0))))
@@ -292,10 +303,7 @@ def run_glacier(args):
     dom = step_kernel_timing(torch, dm, sess, cfg, lanes, stream, args.profile_steps, device_step)
     dom["kernels"].update(gemv_batch1_timing(torch, cfg, stream))
 
-    times = torch.tensor([dev_ms, e2e_s * 1e3], dtype=torch.float64, device=dev)
-    if ws > 1:
-        torch.distributed.all_reduce(times, op=torch.distributed.ReduceOp.MAX)
-    dev_ms, e2e_ms = float(times[0]), float(times[1])
+    dev_ms, e2e_ms = max_over_ranks([dev_ms, e2e_s * 1e3], ws, dev)
     tokens_total = lanes * args.steps * ws
     value = tokens_total / (dev_ms / 1e3)
     e2e_value = tokens_total / (e2e_ms / 1e3)
