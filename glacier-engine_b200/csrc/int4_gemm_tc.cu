@@ -45,14 +45,17 @@ __device__ int g_gemm_error;
 namespace {
 
 constexpr int kRowsTile = 128;
-constexpr int kChunkK = 64;                     // K per MMA stage (one 128-byte swizzle row of fp16)
+constexpr int kChunkK = 64;                     // K per MMA group (one 128-byte swizzle row of fp16)
+constexpr int kSub = 2;                         // MMA groups per pipeline chunk
+constexpr int kPipeK = kChunkK * kSub;          // K per pipeline chunk: one A slot, one B stage, one commit
 constexpr int kSuperK = 256;                    // K per nibble/scale TMA stage
+constexpr int kChunksPerSuper = kSuperK / kPipeK;
 constexpr int kMaxSlots = 8;                    // shared-memory ring slots (runtime counts below this)
 constexpr int kConvWarps = 8;                   // two converter warps per TMEM lane quarter
 constexpr int kEpiWarps = 4;                    // one epilogue warp per TMEM lane quarter
-constexpr int kASlots = 4;                      // A chunks (-Whi | Wlo) resident in TMEM
+constexpr int kASlots = 2;                      // A chunks (-Whi | Wlo) resident in TMEM
 constexpr int kDoneRing = 8;                    // chunk-completion barriers (>= kASlots and >= B slots)
-constexpr uint32_t kAColsPerSlot = 64;          // 32 columns of -Whi + 32 of Wlo (2 fp16 per column)
+constexpr uint32_t kAColsPerSlot = 128;         // 64 columns of -Whi + 64 of Wlo (2 fp16 per column)
 constexpr uint32_t kTmemCols = 512;             // the whole TMEM of the SM (one CTA per SM)
 constexpr int kNibBytes = kRowsTile * 128;      // 128 rows x 256 codes
 constexpr int kSclBytes = kRowsTile * 16;       // 128 rows x 8 fp16 scales
@@ -144,8 +147,8 @@ struct GemmParams {
   float* y;             // [n, ldy] (+ split * split_stride)
   size_t ldy, split_stride;
   int M, K, n, np;      // weight rows, K, live activation rows, padded rows (multiple of 16)
-  int chunks_total;     // ceil(K / 64)
-  int chunks_per_split; // multiple of 4
+  int chunks_total;     // K / kPipeK
+  int chunks_per_split; // multiple of kChunksPerSuper
   int nsplit, tiles, units;
   int nib_slots, b_slots;
   int acc_cols, acc_bufs;  // TMEM columns per accumulator buffer, number of buffers
@@ -172,11 +175,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
                                                               const GemmParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int bbytes = 2 * p.np * 128;  // [Xhi | Xlo] tile: 2*Np rows x 64 fp16
+  const int bbytes = 2 * p.np * 128;  // [Xhi | Xlo] box: 2*Np rows x 64 fp16; a B stage holds kSub boxes
   const int NS = p.nib_slots, BS = p.b_slots;
   uint8_t* nib = smem;                                 // NS x (nibbles + scales)
-  uint8_t* btile = nib + NS * (kNibBytes + kSclBytes);  // BS x bbytes
-  uint64_t* bars = reinterpret_cast<uint64_t*>(btile + BS * bbytes);
+  uint8_t* btile = nib + NS * (kNibBytes + kSclBytes);  // BS x kSub x bbytes
+  uint64_t* bars = reinterpret_cast<uint64_t*>(btile + BS * kSub * bbytes);
   uint64_t* nib_full = bars;
   uint64_t* nib_empty = nib_full + kMaxSlots;
   uint64_t* b_full = nib_empty + kMaxSlots;
@@ -219,7 +222,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
   const uint32_t a_base = (uint32_t)(p.acc_bufs * p.acc_cols);  // A ring follows the accumulators
 
   if (warp == 0) {
-    // ---- nibble + scale producer: one 256-K super-stage per 4 chunks ----
+    // ---- nibble + scale producer: one 256-K super-stage per kChunksPerSuper chunks ----
     if (lane == 0) {
       prefetch_tmap(&tmap_w);
       prefetch_tmap(&tmap_s);
@@ -227,12 +230,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
       uint32_t it = 0, slot = 0, ph = 0;
       for (int u = blockIdx.x; u < p.units && !s_abort; u += gridDim.x) {
         const Unit w = unit_of(p, u);
-        const int nsup = (w.nch + 3) / 4;
+        const int nsup = (w.nch + kChunksPerSuper - 1) / kChunksPerSuper;
         for (int i = 0; i < nsup; ++i, ++it) {
           if (!mbar_wait(&nib_empty[slot], ph ^ 1, p.err)) { s_abort = 1; break; }
           uint8_t* dst = nib + slot * (kNibBytes + kSclBytes);
           mbar_arrive_expect_tx(&nib_full[slot], kNibBytes + kSclBytes);
-          const int ks = w.c0 / 4 + i;  // super-stage index along K
+          const int ks = w.c0 / kChunksPerSuper + i;  // super-stage index along K
           tma_load_2d(dst, &tmap_w, ks * 128, w.row0, &nib_full[slot], pol);
           tma_load_2d(dst + kNibBytes, &tmap_s, ks * 8, w.row0, &nib_full[slot], pol);
           if (++slot == (uint32_t)NS) { slot = 0; ph ^= 1; }
@@ -243,7 +246,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
         mbar_wait(&nib_full[i % NS], (i / NS) & 1, p.err);
     }
   } else if (warp == 1) {
-    // ---- activation producer: one [Xhi | Xlo] tile per 64-K chunk ----
+    // ---- activation producer: kSub [Xhi | Xlo] boxes per 128-K chunk ----
     if (lane == 0) {
       prefetch_tmap(&tmap_x);
       uint64_t keep;
@@ -257,8 +260,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
             if (!mbar_wait(&done[prev % kDoneRing], (prev / kDoneRing) & 1, p.err)) { s_abort = 1; break; }
             ++prev;
           }
-          mbar_arrive_expect_tx(&b_full[slot], (uint32_t)bbytes);
-          tma_load_2d(btile + slot * bbytes, &tmap_x, (w.c0 + i) * kChunkK, 0, &b_full[slot], keep);
+          mbar_arrive_expect_tx(&b_full[slot], (uint32_t)(kSub * bbytes));
+#pragma unroll
+          for (int j = 0; j < kSub; ++j)
+            tma_load_2d(btile + (slot * kSub + j) * bbytes, &tmap_x, (w.c0 + i) * kPipeK + j * kChunkK, 0,
+                        &b_full[slot], keep);
           if (++slot == (uint32_t)BS) slot = 0;
         }
       }
@@ -271,7 +277,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
       // A holds -Whi (negated back by the descriptor) and Wlo.
       const uint32_t id_hl = idesc_f16(2 * p.np, true), id_h = idesc_f16(p.np);
       const uint64_t bdesc0 = sdesc(smem_u32(btile));
-      const uint64_t bstep = (uint64_t)(bbytes >> 4);  // descriptor address units per B slot
+      const uint64_t bbox = (uint64_t)(bbytes >> 4);  // descriptor address units per B box
       uint32_t ch = 0, acc_i = 0;
       uint32_t as = 0, a_ph = 0, bs = 0, b_ph = 0;  // ring positions and phases, advanced per chunk
       for (int u = blockIdx.x; u < p.units && !s_abort; u += gridDim.x) {
@@ -291,13 +297,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
           tc_fence_after();
           const uint32_t ahi = tmem + a_base + (uint32_t)as * kAColsPerSlot;
           const uint32_t alo = ahi + kAColsPerSlot / 2;
-          const uint64_t bd = bdesc0 + (uint64_t)bs * bstep;  // +2 per 16-K step (32 bytes)
+          const uint64_t bd = bdesc0 + (uint64_t)bs * kSub * bbox;  // +2 per 16-K step (32 bytes)
           umma_f16_ts(d, ahi, bd, id_hl, i > 0 ? 1u : 0u);     // Whi x [Xhi | Xlo]
           umma_f16_ts(d, alo, bd, id_h, 1u);                   // Wlo x Xhi
 #pragma unroll
-          for (int kk = 1; kk < kChunkK / 16; ++kk) {
-            umma_f16_ts(d, ahi + kk * 8, bd + 2 * kk, id_hl, 1u);
-            umma_f16_ts(d, alo + kk * 8, bd + 2 * kk, id_h, 1u);
+          for (int kk = 1; kk < kPipeK / 16; ++kk) {
+            const uint32_t ac = (uint32_t)(kk * 8);                       // 8 columns per 16 K
+            const uint64_t bk = (uint64_t)((kk >> 2) * bbox + 2 * (kk & 3));  // box, then 32 B steps
+            umma_f16_ts(d, ahi + ac, bd + bk, id_hl, 1u);
+            umma_f16_ts(d, alo + ac, bd + bk, id_h, 1u);
           }
           umma_commit(&done[ch % kDoneRing]);  // frees A slot ch % kASlots and B slot ch % BS
           if (++as == (uint32_t)kASlots) { as = 0; a_ph ^= 1; }
@@ -311,9 +319,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
       mbar_wait(mma_done, 0, p.err);
     }
   } else if (warp < 3 + kConvWarps) {
-    // ---- converters: thread = weight row (its TMEM lane), 32 codes = one scale group per chunk ----
+    // ---- converters: thread = weight row (its TMEM lane); per chunk, one 32-code scale group
+    //      of each 64-K MMA group ----
     const int quarter = warp & 3;
-    const int hf = (warp - 3) >> 2;  // which 32-code half of the 64-code chunk
+    const int hf = (warp - 3) >> 2;  // which 32-code half of each 64-code group
     const int rrow = quarter * 32 + lane;
     const uint32_t swz = (uint32_t)(rrow & 7);
     const uint32_t tlane = tmem + ((uint32_t)(quarter * 32) << 16) + a_base + (uint32_t)(16 * hf);
@@ -322,7 +331,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
       const Unit w = unit_of(p, u);
       bool ok = true;
       for (int i = 0; i < w.nch; ++i, ++ch) {
-        const int sub = i & 3;
+        const int sub = i % kChunksPerSuper;
         if (sub == 0 && !__all_sync(0xffffffffu, mbar_wait(&nib_full[ns], ns_ph, p.err))) {
           ok = false;
           break;
@@ -330,21 +339,24 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
         const int as = ch % kASlots;
         const uint8_t* nrow = nib + ns * (kNibBytes + kSclBytes) + rrow * 128;
         const uint8_t* srow = nib + ns * (kNibBytes + kSclBytes) + kNibBytes + rrow * 16;
-        const int grp = 2 * sub + hf;  // 32-code group within the 256-code super stage
-        const uint4 g = *reinterpret_cast<const uint4*>(nrow + (((uint32_t)grp ^ swz) << 4));
-        const uint32_t sh = *reinterpret_cast<const uint16_t*>(srow + 2 * grp);
-        const uint32_t s2 = sh * 0x10001u;      // {s, s}
-        const uint32_t ns2 = s2 ^ 0x80008000u;  // {-s, -s}
-        const uint32_t words[4] = {g.x, g.y, g.z, g.w};
-        uint32_t hi[16], lo[16];
+        uint32_t hi[kSub][16], lo[kSub][16];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          uint32_t q[4];
-          unpack8(words[j], q);
+        for (int gsub = 0; gsub < kSub; ++gsub) {
+          const int grp = (sub * kSub + gsub) * 2 + hf;  // 32-code group within the 256-code super stage
+          const uint4 g = *reinterpret_cast<const uint4*>(nrow + (((uint32_t)grp ^ swz) << 4));
+          const uint32_t sh = *reinterpret_cast<const uint16_t*>(srow + 2 * grp);
+          const uint32_t s2 = sh * 0x10001u;      // {s, s}
+          const uint32_t ns2 = s2 ^ 0x80008000u;  // {-s, -s}
+          const uint32_t words[4] = {g.x, g.y, g.z, g.w};
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            hi[4 * j + e] = hmul2_u32(q[e], ns2);               // -RN(q*s)
-            lo[4 * j + e] = hfma2_u32(q[e], s2, hi[4 * j + e]);  // q*s - RN(q*s), exact
+          for (int j = 0; j < 4; ++j) {
+            uint32_t q[4];
+            unpack8(words[j], q);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              hi[gsub][4 * j + e] = hmul2_u32(q[e], ns2);                      // -RN(q*s)
+              lo[gsub][4 * j + e] = hfma2_u32(q[e], s2, hi[gsub][4 * j + e]);  // q*s - RN(q*s), exact
+            }
           }
         }
         // The A slot last held chunk ch - kASlots; wait until its MMAs completed.
@@ -357,16 +369,19 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
         }
         tc_fence_after();
         const uint32_t ta = tlane + (uint32_t)as * kAColsPerSlot;
-        tmem_st16(ta, hi);
-        tmem_st16(ta + kAColsPerSlot / 2, lo);
+#pragma unroll
+        for (int gsub = 0; gsub < kSub; ++gsub) {
+          tmem_st16(ta + 32 * gsub, hi[gsub]);
+          tmem_st16(ta + kAColsPerSlot / 2 + 32 * gsub, lo[gsub]);
+        }
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(&a_full[as]);
-          if (sub == 3 || i == w.nch - 1) mbar_arrive(&nib_empty[ns]);
+          if (sub == kChunksPerSuper - 1 || i == w.nch - 1) mbar_arrive(&nib_empty[ns]);
         }
-        if (sub == 3 || i == w.nch - 1) {
+        if (sub == kChunksPerSuper - 1 || i == w.nch - 1) {
           if (++ns == (uint32_t)NS) { ns = 0; ns_ph ^= 1; }
         }
       }
@@ -467,7 +482,7 @@ __global__ void split_activation_kernel(const float* __restrict__ x, size_t ldx,
 
 size_t gemm_split_bytes(size_t np, size_t K) { return 2 * np * K * sizeof(__half) + np * sizeof(float) + 256; }
 
-bool gemm_tc_supported(const Int4Weight& w) { return w.tc && w.f16 && w.K % kChunkK == 0; }
+bool gemm_tc_supported(const Int4Weight& w) { return w.tc && w.f16 && w.K % kPipeK == 0; }
 
 // Activations in split form for the GEMM: xs [2*np, K] fp16 + xscale [np].
 int split_activation(const float* x, size_t ldx, size_t n, size_t K, size_t np, __half* xs, float* xscale,
@@ -491,7 +506,7 @@ static void gemm_slots(size_t np, int* nib, int* b) {
   *nib = 4;
   *b = kMaxSlots;
   const size_t fixed = 1024 + (size_t)(3 * kMaxSlots + kDoneRing + kASlots + 5) * 8 + 16;
-  auto bytes = [&]() { return fixed + (size_t)*nib * (kNibBytes + kSclBytes) + (size_t)*b * 2 * np * 128; };
+  auto bytes = [&]() { return fixed + (size_t)*nib * (kNibBytes + kSclBytes) + (size_t)*b * kSub * 2 * np * 128; };
   while (bytes() > 227 * 1024 && *b > 3) --*b;
   while (bytes() > 227 * 1024 && *nib > 2) --*nib;
   while (bytes() > 227 * 1024 && *b > 2) --*b;
@@ -501,7 +516,7 @@ size_t gemm_smem_bytes(size_t np) {
   int nib, b;
   gemm_slots(np, &nib, &b);
   const size_t bytes = 1024 + (size_t)(3 * kMaxSlots + kDoneRing + kASlots + 5) * 8 + 16 +
-                       (size_t)nib * (kNibBytes + kSclBytes) + (size_t)b * 2 * np * 128;
+                       (size_t)nib * (kNibBytes + kSclBytes) + (size_t)b * kSub * 2 * np * 128;
   return bytes < (size_t)kMinSmem ? (size_t)kMinSmem : bytes;
 }
 
@@ -560,9 +575,9 @@ int gemm_int4_tc(const Int4Weight& w, const CUtensorMap& xmap, const float* xsca
   GLC_REQUIRE(gemm_tc_supported(w), "int4 gemm: weight layout not supported by the tensor-core GEMM");
   GLC_REQUIRE(np % 16 == 0 && np >= 16 && np <= 128 && n <= np, "int4 gemm: padded rows %zu (n=%zu)", np, n);
   GLC_REQUIRE(nsplit >= 1, "int4 gemm: %d splits", nsplit);
-  const int chunks = (int)(w.K / kChunkK);
+  const int chunks = (int)(w.K / kPipeK);
   const int sup = (int)ceil_div(w.K, kSuperK);
-  const int per = (int)ceil_div(sup, nsplit) * 4;
+  const int per = (int)ceil_div(sup, nsplit) * kChunksPerSuper;
   const int tiles = (int)ceil_div(w.M, kRowsTile);
   const size_t smem = gemm_smem_bytes(np);
   GLC_REQUIRE(smem <= 227 * 1024, "int4 gemm: %zu bytes of shared memory", smem);
