@@ -49,6 +49,8 @@ __device__ __forceinline__ Cand warp_best(Cand c) {
 __global__ void __launch_bounds__(kArgThreads) argmax_partial_kernel(
     const float* __restrict__ logits, size_t ld, int n, const uint64_t* __restrict__ words, int word_count,
     float* __restrict__ pv, int* __restrict__ pi, int* __restrict__ pflags, int nchunks) {
+  griddep_launch();
+  griddep_wait();
   const int row = blockIdx.y, chunk = blockIdx.x;
   const int c0 = chunk * kArgChunk, c1 = min(n, c0 + kArgChunk);
   const float* lg = logits + row * ld;
@@ -106,6 +108,8 @@ __global__ void argmax_final_kernel(const float* __restrict__ pv, const int* __r
                                     const int* __restrict__ pflags, int nchunks, int masked,
                                     glacier_argmax_result* __restrict__ out, int32_t* __restrict__ tokens,
                                     int32_t* __restrict__ status) {
+  griddep_launch();
+  griddep_wait();
   const int row = blockIdx.x;
   if (threadIdx.x != 0) return;
   Cand b{0.f, -1};
@@ -151,11 +155,12 @@ int argmax_rows(const float* logits, size_t ld, size_t batch, size_t n, const ui
   float* pv = static_cast<float*>(workspace);
   int* pi = reinterpret_cast<int*>(pv + batch * chunks);
   int* pf = pi + batch * chunks;
-  argmax_partial_kernel<<<dim3(chunks, (unsigned)batch), kArgThreads, 0, stream>>>(logits, ld, (int)n, words,
-                                                                                   (int)word_count, pv, pi, pf, chunks);
-  GLC_CHECK_LAUNCH();
-  argmax_final_kernel<<<(unsigned)batch, 32, 0, stream>>>(pv, pi, pf, chunks, words != nullptr, out, tokens, status);
-  GLC_CHECK_LAUNCH();
+  int rc = launch_pdl(argmax_partial_kernel, dim3(chunks, (unsigned)batch), dim3(kArgThreads), 0, stream, 1, logits,
+                      ld, (int)n, words, (int)word_count, pv, pi, pf, chunks);
+  if (rc) return rc;
+  rc = launch_pdl(argmax_final_kernel, dim3((unsigned)batch), dim3(32), 0, stream, 1, (const float*)pv, (const int*)pi,
+                  (const int*)pf, chunks, (int)(words != nullptr), out, tokens, status);
+  if (rc) return rc;
   return GLACIER_CUDA_OK;
 }
 

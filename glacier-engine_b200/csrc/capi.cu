@@ -65,6 +65,31 @@ int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base
   return GLACIER_CUDA_OK;
 }
 
+void* device_symbol_address_raw(const void* symbol) {
+  constexpr int kMaxDevices = 64, kMaxSymbols = 16;
+  struct Slot {
+    const void* symbol;
+    void* address;
+  };
+  static Slot table[kMaxDevices][kMaxSymbols] = {};
+  static std::mutex mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  for (auto& e : table[dev]) {
+    if (e.symbol == symbol) return e.address;
+    if (!e.symbol) {
+      void* p = nullptr;
+      if (cudaGetSymbolAddress(&p, symbol) != cudaSuccess) return nullptr;
+      e.symbol = symbol;
+      e.address = p;
+      return p;
+    }
+  }
+  void* p = nullptr;
+  return cudaGetSymbolAddress(&p, symbol) == cudaSuccess ? p : nullptr;
+}
+
 int allow_dynamic_smem(const void* kernel, int bytes) {
   GLC_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
   return GLACIER_CUDA_OK;
@@ -251,6 +276,10 @@ int glacier_cuda_paged_attention_f32(const float* q, const float* kv_pages, size
                                      size_t head_dim, float* out, float* workspace, size_t workspace_floats,
                                      void* stream) {
   GLC_REQUIRE(lanes > 0 && num_kv_heads > 0, "paged_attention: empty batch");
+  // The kernel's work counters sit at the end of the workspace and must start at zero.
+  const size_t need = glacier_cuda_paged_attention_workspace(lanes, num_heads, num_kv_heads, head_dim, max_ctx);
+  GLC_REQUIRE(workspace && workspace_floats >= need, "paged_attention: workspace of %zu floats needed", need);
+  GLC_CHECK_CUDA(cudaMemsetAsync(workspace, 0, 4 * sizeof(float), (cudaStream_t)stream));
   return paged_attention(q, num_heads * head_dim, kv_pages, page_floats, block_tables, max_pages, ctx_lens, max_ctx,
                          lanes, layer, num_heads, num_kv_heads, head_dim, out, num_heads * head_dim, workspace,
                          workspace_floats, attention_chunk(lanes, num_kv_heads, max_ctx), (cudaStream_t)stream);

@@ -45,6 +45,11 @@ void note_launch();
 
 __host__ __device__ inline size_t ceil_div(size_t a, size_t b) { return (a + b - 1) / b; }
 
+// Programmatic dependent launch: let the next kernel in the stream start its
+// prologue now; wait until the previous kernel's writes are visible.
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // Number of SMs of the current device (cached per device).
 int sm_count();
 
@@ -54,8 +59,48 @@ int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base
                    uint64_t outer, uint64_t outer_stride_bytes, uint32_t box_inner, uint32_t box_outer,
                    CUtensorMapSwizzle swizzle, CUtensorMapL2promotion promo);
 
+// Device address of a library __device__ variable on the current device, looked
+// up once per (variable, device) (host code cannot use the variable's name as
+// an address).  Returns nullptr on failure.
+void* device_symbol_address_raw(const void* symbol);
+template <typename T>
+inline T* device_symbol_address(const T& symbol) {
+  return static_cast<T*>(device_symbol_address_raw(static_cast<const void*>(&symbol)));
+}
+
 // Allows `bytes` of dynamic shared memory for `kernel` (once per kernel).
 int allow_dynamic_smem(const void* kernel, int bytes);
+
+// Launch with programmatic dependent launch allowed (and an optional cluster
+// size): the kernel may start while its stream predecessor is still running,
+// and every kernel of this library calls griddep_wait() before it touches
+// memory that a predecessor writes, so results are as if serialised.
+template <typename Kern, typename... Args>
+inline int launch_pdl(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, int cluster,
+                      Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[n].val.programmaticStreamSerializationAllowed = 1;
+  ++n;
+  if (cluster > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = (unsigned)cluster;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  GLC_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, static_cast<Args&&>(args)...));
+  note_launch();
+  return GLACIER_CUDA_OK;
+}
 
 // Optional per-kernel-class timing of a multi-kernel step: while `on`, mark()
 // records a CUDA event on the launching stream that closes the open region and

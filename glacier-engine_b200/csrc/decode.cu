@@ -108,6 +108,8 @@ StepProfiler::~StepProfiler() {
 namespace {
 
 __global__ void ctx_from_pos_kernel(const int32_t* __restrict__ pos, int32_t* __restrict__ ctx, int n) {
+  griddep_launch();
+  griddep_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) ctx[i] = pos[i] + 1;
 }
@@ -495,6 +497,9 @@ int glacier_cuda_model_reserve(glacier_cuda_model* m, size_t max_lanes, size_t m
       (rc = m->ctx.alloc(L * 4)) || (rc = m->att_ws.alloc(m->att_floats * 4)) ||
       (rc = m->arg_ws.alloc(m->arg_bytes)) || (rc = m->status.alloc(L * 4)))
     return rc;
+  // The attention kernel's work counters (start of its workspace) begin at zero
+  // and every launch leaves them at zero.
+  GLC_CHECK_CUDA(cudaMemset(m->att_ws.p, 0, 4 * sizeof(float)));
   m->max_lanes = max_lanes;
   m->max_pages = max_pages;
   m->gemm = max_lanes > 4 && gemm_tc_supported(m->layers[0]->qkv.w) && gemm_tc_supported(m->layers[0]->o.w) &&
@@ -572,8 +577,9 @@ int glacier_cuda_decode_step(glacier_cuda_model* m, glacier_cuda_kv* kv, size_t 
     if (prof) prof->mark(kind, st);
   };
   mark(GLACIER_CUDA_STEP_EMBED);
-  ctx_from_pos_kernel<<<(unsigned)ceil_div(B, 128), 128, 0, st>>>(positions, m->ctx.as<int32_t>(), (int)B);
-  GLC_CHECK_LAUNCH();
+  if ((rc = launch_pdl(ctx_from_pos_kernel, dim3((unsigned)ceil_div(B, 128)), dim3(128), 0, st, 1, positions,
+                       m->ctx.as<int32_t>(), (int)B)))
+    return rc;
   if ((rc = embed_gather(m->embedding.as<__half>(), c.vocab, D, tokens, B, x, D, st))) return rc;
   // Split-form destinations of the GEMM inputs (tensor-core mode only).
   auto split_of = [&](DevBuf& xs, size_t K) {

@@ -76,6 +76,8 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(
     const float* __restrict__ a, size_t lda, const float* __restrict__ b, size_t ldb, size_t b_split_stride,
     int nb, float* __restrict__ residual, size_t ldr, const float* __restrict__ w, float eps, float* __restrict__ out,
     size_t ldo, SplitOut so, int dim) {
+  griddep_launch();
+  griddep_wait();
   extern __shared__ float row[];
   __shared__ float sh[32];
   __shared__ float xch[2];
@@ -133,6 +135,8 @@ __global__ void __launch_bounds__(kNormThreads) silu_mul_split_kernel(const floa
                                                                         const float* __restrict__ up, size_t ld_in,
                                                                         float* __restrict__ out, size_t ld_out,
                                                                         SplitOut so, int n) {
+  griddep_launch();
+  griddep_wait();
   extern __shared__ float row[];
   __shared__ float sh[32];
   __shared__ float xch;
@@ -170,6 +174,8 @@ __global__ void __launch_bounds__(kNormThreads) silu_mul_split_kernel(const floa
 // out[b, i] = silu(gate[b, i]) * up[b, i]; silu(g) = g * (1 / (1 + exp(-g))).
 __global__ void silu_mul_kernel(const float* __restrict__ gate, const float* __restrict__ up, size_t ld_in,
                                 float* __restrict__ out, size_t ld_out, int n, int batch) {
+  griddep_launch();
+  griddep_wait();
   const size_t total = (size_t)n * batch;
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
     const int b = (int)(i / n), k = (int)(i % n);
@@ -182,6 +188,8 @@ __global__ void silu_mul_kernel(const float* __restrict__ gate, const float* __r
 // x[b, :] = float(table[token[b], :])
 __global__ void embed_kernel(const __half* __restrict__ table, const int32_t* __restrict__ tokens, int vocab, int dim,
                              float* __restrict__ out, size_t ldo, int* __restrict__ bad) {
+  griddep_launch();
+  griddep_wait();
   const int b = blockIdx.y;
   const int tok = tokens[b];
   if (tok < 0 || tok >= vocab) {
@@ -204,6 +212,8 @@ __global__ void qkv_rope_append_kernel(const float* __restrict__ qkv, size_t ld,
                                        size_t ldq, float* __restrict__ pool, size_t page_floats,
                                        const int32_t* __restrict__ block_tables, int max_pages, int layer,
                                        int* __restrict__ bad) {
+  griddep_launch();
+  griddep_wait();
   const int b = blockIdx.x;
   const int p = pos[b];
   const int half = head_dim >> 1;
@@ -262,11 +272,7 @@ int ops_device_error(int clear) {
   return v;
 }
 
-static int* ops_err_ptr() {
-  int* p = nullptr;
-  cudaGetSymbolAddress((void**)&p, g_ops_error);
-  return p;
-}
+static int* ops_err_ptr() { return device_symbol_address(g_ops_error); }
 
 // Cluster size for a row of `dim` values: about 1024 values per CTA, at most 8.
 static int row_cluster(size_t dim) {
@@ -281,13 +287,15 @@ static int launch_row_cluster(const void* kern, void** args, size_t rows, int cl
   cfg.blockDim = dim3(kNormThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = cl;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see launch_pdl
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   GLC_CHECK_CUDA(cudaLaunchKernelExC(&cfg, kern, args));
   note_launch();
   return GLACIER_CUDA_OK;
@@ -321,9 +329,8 @@ int silu_mul(const float* gate, const float* up, size_t ld_in, float* out, size_
   if (!so.xs) {
     const size_t total = batch * n;
     const unsigned grid = (unsigned)std::min<size_t>(ceil_div(total, 256), (size_t)sm_count() * 8);
-    silu_mul_kernel<<<grid, 256, 0, stream>>>(gate, up, ld_in, out, ld_out, (int)n, (int)batch);
-    GLC_CHECK_LAUNCH();
-    return GLACIER_CUDA_OK;
+    return launch_pdl(silu_mul_kernel, dim3(grid), dim3(256), 0, stream, 1, gate, up, ld_in, out, ld_out, (int)n,
+                      (int)batch);
   }
   const int cl = row_cluster(n);
   const size_t slice = ((ceil_div(n, (size_t)cl)) + 7) & ~(size_t)7;
@@ -344,9 +351,8 @@ int embed_gather(const __half* table, size_t vocab, size_t dim, const int32_t* t
                  size_t ldo, cudaStream_t stream) {
   GLC_REQUIRE(table && tokens && out && batch > 0 && dim > 0, "embedding: empty or null argument");
   dim3 grid((unsigned)std::min<size_t>(ceil_div(dim, 256), 16), (unsigned)batch);
-  embed_kernel<<<grid, 256, 0, stream>>>(table, tokens, (int)vocab, (int)dim, out, ldo, ops_err_ptr());
-  GLC_CHECK_LAUNCH();
-  return GLACIER_CUDA_OK;
+  return launch_pdl(embed_kernel, grid, dim3(256), 0, stream, 1, table, tokens, (int)vocab, (int)dim, out, ldo,
+                    ops_err_ptr());
 }
 
 int qkv_rope_append(const float* qkv, size_t ld, size_t split_stride, int nsplit, const float* bias,
@@ -358,11 +364,10 @@ int qkv_rope_append(const float* qkv, size_t ld, size_t split_stride, int nsplit
               "qkv_rope_append: null argument");
   GLC_REQUIRE(head_dim % 2 == 0 && num_kv_heads > 0 && num_heads % num_kv_heads == 0,
               "qkv_rope_append: bad head geometry");
-  qkv_rope_append_kernel<<<dim3((unsigned)batch, 4), 256, 0, stream>>>(
-      qkv, ld, split_stride, nsplit, bias, cos_t, sin_t, (int)positions, pos, (int)num_heads, (int)num_kv_heads,
-      (int)head_dim, q_out, ldq, pool, page_floats, block_tables, (int)max_pages, (int)layer, ops_err_ptr());
-  GLC_CHECK_LAUNCH();
-  return GLACIER_CUDA_OK;
+  return launch_pdl(qkv_rope_append_kernel, dim3((unsigned)batch, 4), dim3(256), 0, stream, 1, qkv, ld, split_stride,
+                    nsplit, bias, cos_t, sin_t, (int)positions, pos, (int)num_heads, (int)num_kv_heads,
+                    (int)head_dim, q_out, ldq, pool, page_floats, block_tables, (int)max_pages, (int)layer,
+                    ops_err_ptr());
 }
 
 }  // namespace glacier

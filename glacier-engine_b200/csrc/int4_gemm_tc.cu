@@ -192,6 +192,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
   __shared__ volatile int s_abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // Weights do not depend on the previous kernel: the nibble producer and the
+  // converters start at once; the activation producer and the epilogue wait for
+  // the previous kernel's writes (griddep_wait) before touching its outputs.
+  griddep_launch();
 
   if (threadIdx.x == 0) {
     s_abort = 0;
@@ -247,6 +251,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     }
   } else if (warp == 1) {
     // ---- activation producer: kSub [Xhi | Xlo] boxes per 128-K chunk ----
+    griddep_wait();
     if (lane == 0) {
       prefetch_tmap(&tmap_x);
       uint64_t keep;
@@ -389,6 +394,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     }
   } else {
     // ---- epilogue: TMEM lane = weight row; columns b (Whi-side hi) and Np + b (lo) ----
+    griddep_wait();
     const int quarter = warp & 3;
     uint32_t acc_i = 0;
     for (int u = blockIdx.x; u < p.units && !s_abort; u += gridDim.x) {
@@ -438,6 +444,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
 // (0,4,1,5,2,6,3,7) per 8 and xscale[row] = 2^e with max|x|/2^e in [2^14, 2^15).
 __global__ void split_activation_kernel(const float* __restrict__ x, size_t ldx, int K, int np,
                                         __half* __restrict__ xs, float* __restrict__ xscale) {
+  griddep_launch();
+  griddep_wait();
   const int r = blockIdx.x;
   const float* xr = x + (size_t)r * ldx;
   float m = 0.f;
@@ -488,9 +496,8 @@ bool gemm_tc_supported(const Int4Weight& w) { return w.tc && w.f16 && w.K % kPip
 int split_activation(const float* x, size_t ldx, size_t n, size_t K, size_t np, __half* xs, float* xscale,
                      cudaStream_t stream) {
   GLC_REQUIRE(K % 8 == 0 && n <= np, "split_activation: K %% 8 and n <= np required");
-  split_activation_kernel<<<(unsigned)n, 256, 0, stream>>>(x, ldx, (int)K, (int)np, xs, xscale);
-  GLC_CHECK_LAUNCH();
-  return GLACIER_CUDA_OK;
+  return launch_pdl(split_activation_kernel, dim3((unsigned)n), dim3(256), 0, stream, 1, x, ldx, (int)K, (int)np, xs,
+                    xscale);
 }
 
 int encode_split_map(CUtensorMap* map, const __half* xs, size_t np, size_t K) {
@@ -552,6 +559,8 @@ int gemm_splits(size_t M, size_t K) {
 namespace {
 __global__ void reduce_splits_kernel(const float* __restrict__ part, size_t split_stride, int nsplit,
                                      float* __restrict__ y, size_t n) {
+  griddep_launch();
+  griddep_wait();
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
     float v = part[i];
     for (int s = 1; s < nsplit; ++s) v += part[s * split_stride + i];
@@ -563,9 +572,7 @@ __global__ void reduce_splits_kernel(const float* __restrict__ part, size_t spli
 // y[i] = sum over nsplit partial arrays (in split order), i < n.
 int reduce_splits(const float* part, size_t split_stride, int nsplit, float* y, size_t n, cudaStream_t stream) {
   const unsigned grid = (unsigned)std::min<size_t>(ceil_div(n, 256), (size_t)sm_count() * 8);
-  reduce_splits_kernel<<<grid, 256, 0, stream>>>(part, split_stride, nsplit, y, n);
-  GLC_CHECK_LAUNCH();
-  return GLACIER_CUDA_OK;
+  return launch_pdl(reduce_splits_kernel, dim3(grid), dim3(256), 0, stream, 1, part, split_stride, nsplit, y, n);
 }
 
 // y (+ split * split_stride) = X W^T for the np-padded activation block whose
@@ -587,8 +594,8 @@ int gemm_int4_tc(const Int4Weight& w, const CUtensorMap& xmap, const float* xsca
     if (rc) return rc;
     attr = smem;
   }
-  static int* err = nullptr;
-  if (!err) GLC_CHECK_CUDA(cudaGetSymbolAddress((void**)&err, g_gemm_error));
+  int* err = device_symbol_address(g_gemm_error);
+  GLC_REQUIRE(err != nullptr, "int4 gemm: device status word unavailable");
   int nib_slots, b_slots;
   gemm_slots(np, &nib_slots, &b_slots);
   // Accumulator columns: 2*np (hi | lo products), a power of two >= 32; two
@@ -618,8 +625,7 @@ int gemm_int4_tc(const Int4Weight& w, const CUtensorMap& xmap, const float* xsca
   prm.acc_bufs = acc_bufs;
   prm.err = err;
   const int grid = std::min(prm.units, sm_count());
-  gemm_tc_kernel<<<grid, kThreads, smem, stream>>>(w.tmap_w, w.tmap_s, xmap, prm);
-  GLC_CHECK_LAUNCH();
+  return launch_pdl(gemm_tc_kernel, dim3(grid), dim3(kThreads), smem, stream, 1, w.tmap_w, w.tmap_s, xmap, prm);
   return GLACIER_CUDA_OK;
 }
 

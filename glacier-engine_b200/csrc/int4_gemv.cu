@@ -40,6 +40,8 @@ __global__ void __launch_bounds__(256) gemv_int4_kernel(
     const float* __restrict__ x, size_t ldx, const uint8_t* __restrict__ packed,
     const ScaleT* __restrict__ scales, size_t scale_stride, const float* __restrict__ bias,
     float* __restrict__ y, size_t ldy, int M, int K, int group_shift) {
+  griddep_launch();
+  griddep_wait();
   // 8 warps = (8 / KS) row groups x KS K-slices; a row group owns R rows.
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -178,6 +180,8 @@ __global__ void __launch_bounds__(256) gemv_int4_generic_kernel(
     const float* __restrict__ x, size_t ldx, const uint8_t* __restrict__ packed,
     const ScaleT* __restrict__ scales, size_t scale_stride, const float* __restrict__ bias,
     float* __restrict__ y, size_t ldy, int M, int K, int group, int batch) {
+  griddep_launch();
+  griddep_wait();
   const int lane = threadIdx.x & 31;
   const size_t wid = (size_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (wid >= (size_t)M * batch) return;

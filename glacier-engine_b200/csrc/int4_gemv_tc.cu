@@ -130,6 +130,8 @@ template <typename ScaleT>
 __global__ void __launch_bounds__(kThreads, 2) gemv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w,
                                                               const __grid_constant__ CUtensorMap tmap_s,
                                                               const GemvParams p) {
+  griddep_launch();
+  griddep_wait();
   constexpr int kScaleBytes = kRows * 8 * (int)sizeof(ScaleT);  // 8 groups per row per stage
   constexpr int kStageBytes = kNibBytes + kScaleBytes;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -313,13 +315,15 @@ int launch_gemv_tc(const Int4Weight& w, const float* x, size_t ldx, size_t batch
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = cs;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see launch_pdl
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   GLC_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, w.tmap_w, w.tmap_s, prm));
   note_launch();
   return GLACIER_CUDA_OK;

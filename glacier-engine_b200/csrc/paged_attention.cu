@@ -86,6 +86,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
   __shared__ __align__(16) float2 prb_all[kAttnWarps][kStageRows * kMaxGroup];  // {p, p} per (position, head)
   __shared__ int queue[kAttnWarps][8];  // items claimed by lane 0, in issue order (-1 ends the list)
 
+  griddep_launch();
+  griddep_wait();  // q, the KV pages and the work counter come from earlier kernels
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int l16 = lane & 15, ph = lane >> 4;
   float* ring = sm + (size_t)warp * kAttnStages * 2 * TILE;
@@ -338,6 +340,13 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
   // Leave no copy in flight (a wait that gave up leaves some outstanding).
   if (lane == 0) {
     for (uint32_t i = consumed; i < issued; ++i) mbar_wait(&bars[warp][i % kAttnStages], (i / kAttnStages) & 1, err);
+    // The last warp to finish zeroes the work counters for the next launch.
+    __threadfence();
+    if (atomicAdd(work_counter + 1, 1) == (int)(gridDim.x * kAttnWarps) - 1) {
+      work_counter[0] = 0;
+      work_counter[1] = 0;
+      __threadfence();
+    }
   }
   __syncwarp();
 }
@@ -351,6 +360,8 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const float* __restri
                                                            int num_heads, float* __restrict__ out, size_t ldo,
                                                            SplitOut so, const int32_t* __restrict__ ctx_lens,
                                                            int chunk) {
+  griddep_launch();
+  griddep_wait();
   extern __shared__ float dyn[];  // [hpc][nsplit] chunk weights, then (split outputs) hpc x head_dim values
   __shared__ float sh[32], xch;
   const int lane_id = blockIdx.y;
@@ -427,7 +438,7 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const float* __restri
 
 // Workspace floats needed by paged_attention for the given split count.
 size_t attention_workspace_floats(size_t lanes, size_t num_heads, size_t head_dim, size_t nsplit) {
-  return lanes * num_heads * nsplit * (head_dim + 2) + 4;  // + the work counter
+  return 4 + lanes * num_heads * nsplit * (head_dim + 2);  // work counters + chunk partials
 }
 
 // Positions per work item: 256 (16 pages) unless that leaves fewer than two
@@ -514,8 +525,9 @@ int paged_attention(const float* q, size_t ldq, const float* pool, size_t page_f
   prm.chunk = chunk;
   prm.nsplit = nsplit;
   prm.scale = 1.0f / sqrtf((float)head_dim);
-  prm.part_o = workspace;
-  prm.part_ml = workspace + lanes * num_heads * nsplit * head_dim;
+  // Workspace: two work counters (4 floats reserved), then the chunk partials.
+  prm.part_o = workspace + 4;
+  prm.part_ml = prm.part_o + lanes * num_heads * nsplit * head_dim;
   const size_t kv_dim = num_kv_heads * head_dim;
   GLC_REQUIRE(page_floats % kv_dim == 0 && page_floats / kv_dim >= (layer + 1) * 32,
               "paged_attention: page of %zu floats does not hold layer %zu", page_floats, layer);
@@ -547,14 +559,16 @@ int paged_attention(const float* q, size_t ldq, const float* pool, size_t page_f
         }
     }
   }
-  static int* err = nullptr;
-  if (!err) GLC_CHECK_CUDA(cudaGetSymbolAddress((void**)&err, g_attn_error));
+  int* err = device_symbol_address(g_attn_error);
+  GLC_REQUIRE(err != nullptr, "paged_attention: device status word unavailable");
   const size_t items = lanes * num_kv_heads * (size_t)nsplit;
   const int grid = (int)std::min<size_t>((size_t)sm_count(), ceil_div(items, (size_t)kAttnWarps));
-  int* counter = reinterpret_cast<int*>(workspace + lanes * num_heads * nsplit * (head_dim + 2));
-  GLC_CHECK_CUDA(cudaMemsetAsync(counter, 0, sizeof(int), stream));
-  kern<<<grid, kAttnWarps * 32, smem, stream>>>(*kvmap, prm, (int)lanes, (int)(page_floats / kv_dim), counter, err);
-  GLC_CHECK_LAUNCH();
+  // The two work counters at the start of the workspace start at zero (the
+  // caller clears them once) and the kernel leaves them at zero.
+  int* counter = reinterpret_cast<int*>(workspace);
+  if ((rc = launch_pdl(kern, dim3(grid), dim3(kAttnWarps * 32), smem, stream, 1, *kvmap, prm, (int)lanes,
+                       (int)(page_floats / kv_dim), counter, err)))
+    return rc;
   if (prof) prof->mark(combine_kind, stream);
   {
     // Cluster of CTAs per lane over its heads (about 7 heads per CTA).
@@ -564,21 +578,10 @@ int paged_attention(const float* q, size_t ldq, const float* pool, size_t page_f
     GLC_REQUIRE(hpc <= 4 * kMaxGroup, "paged_attention: too many heads per combine CTA");
     const size_t csmem = ((size_t)hpc * nsplit + (so.xs ? (size_t)hpc * head_dim : 0)) * sizeof(float);
     GLC_REQUIRE(csmem <= 48 * 1024, "paged_attention: %d chunks per lane exceed the combine's shared memory", nsplit);
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)cl, (unsigned)lanes);
-    cfg.blockDim = dim3(256);
-    cfg.dynamicSmemBytes = csmem;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = cl;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    GLC_CHECK_CUDA(cudaLaunchKernelEx(&cfg, attn_combine_kernel, (const float*)prm.part_o, (const float*)prm.part_ml,
-                                      nsplit, (int)head_dim, (int)num_heads, out, ldo, so, ctx_lens, chunk));
-    note_launch();
+    if ((rc = launch_pdl(attn_combine_kernel, dim3((unsigned)cl, (unsigned)lanes), dim3(256), csmem, stream, cl,
+                         (const float*)prm.part_o, (const float*)prm.part_ml, nsplit, (int)head_dim, (int)num_heads,
+                         out, ldo, so, ctx_lens, chunk)))
+      return rc;
   }
   return GLACIER_CUDA_OK;
 }
