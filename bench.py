@@ -355,8 +355,9 @@ def load_peaks() -> dict:
 # DRAM bytes (dram__bytes_read + write) per algorithmic byte, from one ncu capture of a smaller
 # case of the same kernel (profiles/); traffic scales with the K/V rows a launch reads.
 DRAM_TRAFFIC_RATIO = {
-    "attention": (269.3e6 / 266.1e6, "ncu: 269.3 MB DRAM for 266.1 MB algorithmic (1 layer, 32 lanes, mean ctx "
-                                     "2015), scaled to this launch's K/V bytes; profiles/attn_chunk_128_32lanes.md"),
+    "attention": (271.8e6 / 265.1e6, "ncu: 265.7 MB read + 6.1 MB written for 265.1 MB algorithmic (1 layer, 32 "
+                                     "lanes, mean ctx 2015), scaled to this launch's K/V bytes; "
+                                     "profiles/attn_tma_128x7_32lanes.md"),
 }
 
 STEP_KINDS = ("embed", "norm", "proj_qkv", "rope_append", "attention", "attn_combine", "proj_o", "proj_gate_up",
@@ -410,7 +411,7 @@ def step_kernel_timing(torch, dm, sess, cfg, lanes, stream, steps, device_step) 
         kernels[name] = e
     dom_name = max((k for k in kernels if "gbs" in kernels[k]), key=lambda k: kernels[k]["share"])
     d = kernels[dom_name]
-    what = {"attention": f"paged decode attention (attn_chunk_kernel), one layer, {lanes} lanes, mean ctx "
+    what = {"attention": f"paged decode attention (attn_tma_kernel), one layer, {lanes} lanes, mean ctx "
                          f"{ctx_sum / steps / lanes:.0f}, {nl} launches per step"}.get(
         dom_name, f"{dom_name} ({nl} launches per step)")
     traffic, tsrc = None, None
