@@ -129,6 +129,142 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(
   cluster_sync_all();  // peers may still read this CTA's exchange words
 }
 
+// ---- Split-output forms: each thread owns 8 consecutive values in registers ----
+// A row is cut into `cn` CTAs (a cluster when cn > 1); thread t of CTA c owns
+// values [8g, 8g + 8) with g = c * per + t.  One block (and cluster) reduction
+// gives the row's statistics, then every thread writes its 8 values straight
+// to the GEMM's split form.
+
+// (sum, max) over the row: block reduction, then the cluster's CTAs through DSMEM.
+__device__ __forceinline__ float2 row_sum_max(float s, float m, float2* sh, float2* xch) {
+  s = warp_sum(s);
+  m = warp_max(m);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = (blockDim.x + 31) >> 5;
+  if (l == 0) sh[w] = make_float2(s, m);
+  __syncthreads();
+  if (w == 0) {
+    float2 t = l < nw ? sh[l] : make_float2(0.f, 0.f);
+    t.x = warp_sum(t.x);
+    t.y = warp_max(t.y);
+    if (l == 0) *xch = t;
+  }
+  const uint32_t cn = cluster_nctarank();
+  if (cn == 1) {
+    __syncthreads();
+    return *xch;
+  }
+  cluster_sync_all();
+  const uint32_t a = smem_u32(xch);
+  float2 r = make_float2(0.f, 0.f);
+  for (uint32_t q = 0; q < cn; ++q) {
+    const uint32_t pa = mapa_shared(a, q);
+    r.x += ld_dsmem_f32(pa);
+    r.y = fmaxf(r.y, ld_dsmem_f32(pa + 4));
+  }
+  return r;
+}
+
+__device__ __forceinline__ void load8(const float* p, float (&v)[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+// residual = a + sum of b's split-K partials (in split order); split(rmsnorm(residual) * w).
+__global__ void __launch_bounds__(1024) add_rmsnorm_split8_kernel(
+    const float* __restrict__ a, size_t lda, const float* __restrict__ b, size_t ldb, size_t b_split_stride, int nb,
+    float* __restrict__ residual, size_t ldr, const float* __restrict__ w, float eps, SplitOut so, int dim) {
+  griddep_launch();
+  griddep_wait();
+  __shared__ float2 sh[32];
+  __shared__ __align__(8) float2 xch;
+  const int r = blockIdx.y;
+  const int per = blockDim.x;
+  const int g = (int)cluster_ctarank() * per + threadIdx.x;
+  const bool active = 8 * g < dim;
+  const int k = 8 * g;
+  float v[8], wv[8];
+  float ss = 0.f, mx = 0.f;
+  if (active) {
+    load8(a + (size_t)r * lda + k, v);
+    if (nb > 0) {
+      float t[8];
+      load8(b + (size_t)r * ldb + k, t);
+#pragma unroll 4
+      for (int s = 1; s < nb; ++s) {
+        float u[8];
+        load8(b + (size_t)s * b_split_stride + (size_t)r * ldb + k, u);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) t[i] += u[i];
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = v[i] + t[i];  // addInto (generate.zig:3642)
+    }
+    load8(w + k, wv);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      ss = fmaf(v[i], v[i], ss);
+      mx = fmaxf(mx, fabsf(v[i] * wv[i]));
+    }
+  }
+  const float2 tot = row_sum_max(ss, mx, sh, &xch);
+  const float inv = 1.0f / sqrtf(tot.x / (float)dim + eps);
+  const float scale = split_scale(tot.y * inv);
+  if (active) {
+    if (residual) {
+      float4* rp = reinterpret_cast<float4*>(residual + (size_t)r * ldr + k);
+      rp[0] = make_float4(v[0], v[1], v[2], v[3]);
+      rp[1] = make_float4(v[4], v[5], v[6], v[7]);
+    }
+    float o[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = v[i] * inv * wv[i];
+    store_split8(so, r, (size_t)dim, (size_t)k, o, 1.0f / scale);
+  }
+  if (g == 0) so.xscale[r] = scale;
+  if (cluster_nctarank() > 1) cluster_sync_all();  // peers may still read this CTA's exchange slot
+}
+
+// split(silu(gate) * up) per row (kernels.zig:465-507).
+__global__ void __launch_bounds__(1024) silu_mul_split8_kernel(const float* __restrict__ gate,
+                                                               const float* __restrict__ up, size_t ld_in,
+                                                               SplitOut so, int n) {
+  griddep_launch();
+  griddep_wait();
+  __shared__ float2 sh[32];
+  __shared__ __align__(8) float2 xch;
+  const int r = blockIdx.y;
+  const int g = (int)cluster_ctarank() * blockDim.x + threadIdx.x;
+  const bool active = 8 * g < n;
+  const int k = 8 * g;
+  float h[8];
+  float mx = 0.f;
+  if (active) {
+    float gv[8], uv[8];
+    load8(gate + (size_t)r * ld_in + k, gv);
+    load8(up + (size_t)r * ld_in + k, uv);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float sig = 1.0f / (1.0f + expf(-gv[i]));
+      h[i] = gv[i] * sig * uv[i];
+      mx = fmaxf(mx, fabsf(h[i]));
+    }
+  }
+  const float2 tot = row_sum_max(0.f, mx, sh, &xch);
+  const float scale = split_scale(tot.y);
+  if (active) store_split8(so, r, (size_t)n, (size_t)k, h, 1.0f / scale);
+  if (g == 0) so.xscale[r] = scale;
+  if (cluster_nctarank() > 1) cluster_sync_all();
+}
+
+// Threads per CTA and cluster size for a split8 row of `dim` values.
+static void split8_shape(size_t dim, int* threads, int* cl) {
+  const size_t groups = dim / 8;
+  int c = 1;
+  while (c < 8 && ceil_div(groups, (size_t)c) > 1024) c *= 2;
+  *cl = c;
+  *threads = (int)(ceil_div(ceil_div(groups, (size_t)c), 32) * 32);
+}
+
 // One cluster per row: out = silu(gate) * up (kernels.zig:465-507), as fp32
 // or in split form with the row max combined across the cluster.
 __global__ void __launch_bounds__(kNormThreads) silu_mul_split_kernel(const float* __restrict__ gate,
@@ -232,6 +368,7 @@ __global__ void qkv_rope_append_kernel(const float* __restrict__ qkv, size_t ld,
   const float* row = qkv + b * ld;
   auto val = [&](int i) {
     float v = row[i];
+#pragma unroll 4
     for (int s = 1; s < nsplit; ++s) v += row[s * split_stride + i];
     return bias ? v + bias[i] : v;
   };
@@ -306,6 +443,12 @@ int add_rmsnorm(const float* a, size_t lda, const float* b, size_t ldb, size_t b
                 size_t dim, cudaStream_t stream, SplitOut so) {
   GLC_REQUIRE(a && w && (out || so.xs) && batch > 0 && dim > 0, "rmsnorm: empty or null argument");
   GLC_REQUIRE(!so.xs || dim % 8 == 0, "rmsnorm: split output needs dim %% 8 == 0");
+  if (so.xs && lda % 4 == 0 && ldb % 4 == 0 && b_split_stride % 4 == 0 && ldr % 4 == 0) {
+    int threads, cl;
+    split8_shape(dim, &threads, &cl);
+    return launch_pdl(add_rmsnorm_split8_kernel, dim3((unsigned)cl, (unsigned)batch), dim3(threads), 0, stream, cl,
+                      a, lda, b, ldb, b_split_stride, nb, residual, ldr, w, eps, so, (int)dim);
+  }
   const int cl = row_cluster(dim);
   const size_t slice = ((ceil_div(dim, (size_t)cl)) + 7) & ~(size_t)7;
   const size_t smem = slice * sizeof(float);
@@ -331,6 +474,12 @@ int silu_mul(const float* gate, const float* up, size_t ld_in, float* out, size_
     const unsigned grid = (unsigned)std::min<size_t>(ceil_div(total, 256), (size_t)sm_count() * 8);
     return launch_pdl(silu_mul_kernel, dim3(grid), dim3(256), 0, stream, 1, gate, up, ld_in, out, ld_out, (int)n,
                       (int)batch);
+  }
+  if (ld_in % 4 == 0) {
+    int threads, cl;
+    split8_shape(n, &threads, &cl);
+    return launch_pdl(silu_mul_split8_kernel, dim3((unsigned)cl, (unsigned)batch), dim3(threads), 0, stream, cl, gate,
+                      up, ld_in, so, (int)n);
   }
   const int cl = row_cluster(n);
   const size_t slice = ((ceil_div(n, (size_t)cl)) + 7) & ~(size_t)7;
