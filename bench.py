@@ -40,7 +40,7 @@ UNIT = "tok/s"
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["glacier", "reference"], default="glacier")
     ap.add_argument("--lanes", type=int, default=64)
@@ -62,22 +62,26 @@ def parse():
 # ---------------------------------------------------------------------------
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms while running."""
+    """nvidia-smi clocks and throttle reasons, sampled every 50 ms from before the
+    warm-up until after the timed region; summary() keeps the samples that arrived
+    inside the timed window (host timestamps taken with the device synchronised)."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index: int):
+    def __init__(self, index: int, interval_ms: int = 50):
         self.index = index
+        self.interval_ms = interval_ms
         self.proc = None
-        self.lines: list[str] = []
+        self.lines: list[tuple[float, str]] = []
+        self.t0 = self.t1 = None
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", str(self.interval_ms)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
         except OSError:
@@ -86,10 +90,17 @@ class ClockSampler:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.perf_counter(), line.strip()))
+
+    def start_window(self):
+        self.t0 = time.perf_counter()
+
+    def end_window(self):
+        self.t1 = time.perf_counter()
 
     def __exit__(self, *exc):
         if self.proc:
+            time.sleep(2 * self.interval_ms / 1e3)  # let the sample after the window arrive
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -99,7 +110,11 @@ class ClockSampler:
     def summary(self) -> dict:
         sm, mx, reasons = [], 0.0, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        lo = self.t0 if self.t0 is not None else -1e18
+        hi = (self.t1 if self.t1 is not None else 1e18) + self.interval_ms / 1e3
+        for ts, ln in self.lines:
+            if not (lo <= ts <= hi):
+                continue
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
                 continue
@@ -253,6 +268,7 @@ def run_glacier(args):
         sess.tokens.copy_(out)
         sess.positions.add_(1)
 
+    clk = ClockSampler(local).__enter__()
     for _ in range(args.warmup):
         device_step()
     torch.cuda.synchronize()
@@ -261,14 +277,16 @@ def run_glacier(args):
     torch.cuda.synchronize()
     launches0 = _lib.lib().glacier_cuda_launch_count()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
-        torch.cuda.nvtx.range_push("timed_steps")  # lets a profiler select the timed launches
-        e0.record(stream)
-        for _ in range(args.steps):
-            device_step()
-        e1.record(stream)
-        torch.cuda.synchronize()
-        torch.cuda.nvtx.range_pop()
+    clk.start_window()
+    torch.cuda.nvtx.range_push("timed_steps")  # lets a profiler select the timed launches
+    e0.record(stream)
+    for _ in range(args.steps):
+        device_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_pop()
+    clk.end_window()
+    clk.__exit__(None, None, None)
     launches = _lib.lib().glacier_cuda_launch_count() - launches0
     dev_ms = e0.elapsed_time(e1)
     status = sess.status.cpu().numpy()

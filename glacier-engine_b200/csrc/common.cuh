@@ -326,6 +326,40 @@ __device__ __forceinline__ float split_scale(float m) {
   return ldexpf(1.f, e - 15);
 }
 
+// (sum, max) over the row: block reduction, then the cluster's CTAs through DSMEM.
+__device__ __forceinline__ float2 row_sum_max(float s, float m, float2* sh, float2* xch) {
+  s = warp_sum(s);
+  m = warp_max(m);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = (blockDim.x + 31) >> 5;
+  if (l == 0) sh[w] = make_float2(s, m);
+  __syncthreads();
+  if (w == 0) {
+    float2 t = l < nw ? sh[l] : make_float2(0.f, 0.f);
+    t.x = warp_sum(t.x);
+    t.y = warp_max(t.y);
+    if (l == 0) *xch = t;
+  }
+  const uint32_t cn = cluster_nctarank();
+  if (cn == 1) {
+    __syncthreads();
+    return *xch;
+  }
+  cluster_sync_all();
+  const uint32_t a = smem_u32(xch);
+  float2 r = make_float2(0.f, 0.f);
+  for (uint32_t q = 0; q < cn; ++q) {
+    const uint32_t pa = mapa_shared(a, q);
+    r.x += ld_dsmem_f32(pa);
+    r.y = fmaxf(r.y, ld_dsmem_f32(pa + 4));
+  }
+  return r;
+}
+
+__device__ __forceinline__ void load8(const float* p, float (&v)[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
 // Writes 8 consecutive values (k = base..base+7 of row r) in split form.
 __device__ __forceinline__ void store_split8(const SplitOut& so, int r, size_t K, size_t base, const float (&v)[8],
                                              float inv_scale) {

@@ -129,45 +129,69 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(
   cluster_sync_all();  // peers may still read this CTA's exchange words
 }
 
+// Vectorised RoPE + append: one CTA per lane; a thread owns 4 consecutive rotary
+// pairs of one q or k head (or 4 consecutive v values), loads every split-K
+// partial of them at once, and writes the rotated q, k and the v row.
+__global__ void __launch_bounds__(1024) qkv_rope_append4_kernel(
+    const float* __restrict__ qkv, size_t ld, size_t split_stride, int nsplit, const float* __restrict__ bias,
+    const float* __restrict__ cos_t, const float* __restrict__ sin_t, int positions, const int32_t* __restrict__ pos,
+    int num_heads, int num_kv_heads, int head_dim, float* __restrict__ q_out, size_t ldq, float* __restrict__ pool,
+    size_t page_floats, const int32_t* __restrict__ block_tables, int max_pages, int layer, int* __restrict__ bad) {
+  griddep_launch();
+  griddep_wait();
+  const int b = blockIdx.x;
+  const int p = pos[b];
+  const int half = head_dim >> 1;
+  const int q_dim = num_heads * head_dim, kv_dim = num_kv_heads * head_dim;
+  const int page_idx = p >> 4;
+  if (p < 0 || p >= positions || page_idx >= max_pages) {
+    if (threadIdx.x == 0) atomicExch(bad, 1);
+    return;
+  }
+  const int32_t page = block_tables[b * max_pages + page_idx];
+  float* kdst = pool + (size_t)page * page_floats + ((size_t)(layer * 2 + 0) * 16 + (p & 15)) * kv_dim;
+  float* vdst = pool + (size_t)page * page_floats + ((size_t)(layer * 2 + 1) * 16 + (p & 15)) * kv_dim;
+  const float* row = qkv + b * ld;
+  auto val4 = [&](int i) {  // split-K partials summed in split order, then the bias
+    float4 v = *reinterpret_cast<const float4*>(row + i);
+#pragma unroll 4
+    for (int s = 1; s < nsplit; ++s) {
+      const float4 u = *reinterpret_cast<const float4*>(row + (size_t)s * split_stride + i);
+      v.x += u.x; v.y += u.y; v.z += u.z; v.w += u.w;
+    }
+    if (bias) {
+      const float4 c = *reinterpret_cast<const float4*>(bias + i);
+      v.x += c.x; v.y += c.y; v.z += c.z; v.w += c.w;
+    }
+    return v;
+  };
+  const int pair_quads = (num_heads + num_kv_heads) * half / 4;
+  const int t = threadIdx.x;
+  if (t < pair_quads) {
+    const int i = 4 * t;
+    const int hh = i / half, j = i - hh * half;
+    const int src = hh < num_heads ? hh * head_dim + j : q_dim + (hh - num_heads) * head_dim + j;
+    const float4 x0 = val4(src), x1 = val4(src + half);
+    const float4 c = *reinterpret_cast<const float4*>(cos_t + (size_t)p * half + j);
+    const float4 sn = *reinterpret_cast<const float4*>(sin_t + (size_t)p * half + j);
+    const float4 y0 = make_float4(x0.x * c.x - x1.x * sn.x, x0.y * c.y - x1.y * sn.y, x0.z * c.z - x1.z * sn.z,
+                                  x0.w * c.w - x1.w * sn.w);
+    const float4 y1 = make_float4(x0.x * sn.x + x1.x * c.x, x0.y * sn.y + x1.y * c.y, x0.z * sn.z + x1.z * c.z,
+                                  x0.w * sn.w + x1.w * c.w);
+    float* dst = hh < num_heads ? q_out + b * ldq + hh * head_dim + j : kdst + (hh - num_heads) * head_dim + j;
+    *reinterpret_cast<float4*>(dst) = y0;
+    *reinterpret_cast<float4*>(dst + half) = y1;
+  } else if (t < pair_quads + kv_dim / 4) {
+    const int i = 4 * (t - pair_quads);
+    *reinterpret_cast<float4*>(vdst + i) = val4(q_dim + kv_dim + i);
+  }
+}
+
 // ---- Split-output forms: each thread owns 8 consecutive values in registers ----
 // A row is cut into `cn` CTAs (a cluster when cn > 1); thread t of CTA c owns
 // values [8g, 8g + 8) with g = c * per + t.  One block (and cluster) reduction
 // gives the row's statistics, then every thread writes its 8 values straight
 // to the GEMM's split form.
-
-// (sum, max) over the row: block reduction, then the cluster's CTAs through DSMEM.
-__device__ __forceinline__ float2 row_sum_max(float s, float m, float2* sh, float2* xch) {
-  s = warp_sum(s);
-  m = warp_max(m);
-  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = (blockDim.x + 31) >> 5;
-  if (l == 0) sh[w] = make_float2(s, m);
-  __syncthreads();
-  if (w == 0) {
-    float2 t = l < nw ? sh[l] : make_float2(0.f, 0.f);
-    t.x = warp_sum(t.x);
-    t.y = warp_max(t.y);
-    if (l == 0) *xch = t;
-  }
-  const uint32_t cn = cluster_nctarank();
-  if (cn == 1) {
-    __syncthreads();
-    return *xch;
-  }
-  cluster_sync_all();
-  const uint32_t a = smem_u32(xch);
-  float2 r = make_float2(0.f, 0.f);
-  for (uint32_t q = 0; q < cn; ++q) {
-    const uint32_t pa = mapa_shared(a, q);
-    r.x += ld_dsmem_f32(pa);
-    r.y = fmaxf(r.y, ld_dsmem_f32(pa + 4));
-  }
-  return r;
-}
-
-__device__ __forceinline__ void load8(const float* p, float (&v)[8]) {
-  const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
-  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-}
 
 // residual = a + sum of b's split-K partials (in split order); split(rmsnorm(residual) * w).
 __global__ void __launch_bounds__(1024) add_rmsnorm_split8_kernel(
@@ -513,6 +537,13 @@ int qkv_rope_append(const float* qkv, size_t ld, size_t split_stride, int nsplit
               "qkv_rope_append: null argument");
   GLC_REQUIRE(head_dim % 2 == 0 && num_kv_heads > 0 && num_heads % num_kv_heads == 0,
               "qkv_rope_append: bad head geometry");
+  const int quads = (int)((num_heads + num_kv_heads) * (head_dim / 2) / 4 + num_kv_heads * head_dim / 4);
+  if (head_dim % 8 == 0 && ld % 4 == 0 && split_stride % 4 == 0 && ldq % 4 == 0 && page_floats % 4 == 0 &&
+      quads <= 1024)
+    return launch_pdl(qkv_rope_append4_kernel, dim3((unsigned)batch), dim3((unsigned)ceil_div(quads, 32) * 32), 0,
+                      stream, 1, qkv, ld, split_stride, nsplit, bias, cos_t, sin_t, (int)positions, pos,
+                      (int)num_heads, (int)num_kv_heads, (int)head_dim, q_out, ldq, pool, page_floats, block_tables,
+                      (int)max_pages, (int)layer, ops_err_ptr());
   return launch_pdl(qkv_rope_append_kernel, dim3((unsigned)batch, 4), dim3(256), 0, stream, 1, qkv, ld, split_stride,
                     nsplit, bias, cos_t, sin_t, (int)positions, pos, (int)num_heads, (int)num_kv_heads,
                     (int)head_dim, q_out, ldq, pool, page_floats, block_tables, (int)max_pages, (int)layer,

@@ -351,31 +351,36 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
   __syncwarp();
 }
 
-// out[lane, h, :] = sum_s o_s * e^(m_s - M) / sum_s l_s * e^(m_s - M), in split
-// order.  A cluster of CTAs covers one lane (blockIdx.y), each a range of
-// heads; split outputs (the o-projection's GEMM input) share the lane's row
-// max through distributed shared memory.
-__global__ void __launch_bounds__(256) attn_combine_kernel(const float* __restrict__ part_o,
-                                                           const float* __restrict__ part_ml, int nsplit, int head_dim,
-                                                           int num_heads, float* __restrict__ out, size_t ldo,
-                                                           SplitOut so, const int32_t* __restrict__ ctx_lens,
-                                                           int chunk) {
+// out[lane, h, :] = sum_s o_s * e^(m_s - M) / sum_s l_s * e^(m_s - M), in chunk
+// order.  One CTA per lane: a warp per head computes the chunk weights once,
+// then each thread combines 8 consecutive values of one head from registers
+// and writes them as fp32 or, for the o-projection GEMM, in split form with the
+// lane's row max from one block reduction.
+__global__ void __launch_bounds__(1024) attn_combine_kernel(const float* __restrict__ part_o,
+                                                            const float* __restrict__ part_ml, int nsplit,
+                                                            int head_dim, int num_heads, float* __restrict__ out,
+                                                            size_t ldo, SplitOut so,
+                                                            const int32_t* __restrict__ ctx_lens, int chunk) {
   griddep_launch();
   griddep_wait();
-  extern __shared__ float dyn[];  // [hpc][nsplit] chunk weights, then (split outputs) hpc x head_dim values
-  __shared__ float sh[32], xch;
-  const int lane_id = blockIdx.y;
+  extern __shared__ float wts[];  // [num_heads][nsplit] chunk weights
+  __shared__ float2 sh[32];
+  __shared__ __align__(8) float2 xch;
+  const int lane_id = blockIdx.x;
   // Only the chunks that hold part of this lane's context have partials.
   const int nsplit_lane = min(nsplit, (ctx_lens[lane_id] + chunk - 1) / chunk);
-  const int cr = (int)cluster_ctarank(), cn = (int)cluster_nctarank();
-  const int hpc = (num_heads + cn - 1) / cn;
-  const int h0 = min(num_heads, cr * hpc), h1 = min(num_heads, h0 + hpc);
-  float* wts = dyn;
-  float* row = dyn + hpc * nsplit;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
-  // Chunk weights e^(m_s - M) / L per head, one warp per head (lanes over chunks).
-  for (int t = warp; t < h1 - h0; t += nwarps) {
-    const size_t base = ((size_t)lane_id * num_heads + h0 + t) * nsplit;
+  for (int t = warp; t < num_heads; t += nwarps) {
+    const size_t base = ((size_t)lane_id * num_heads + t) * nsplit;
+    if (nsplit_lane <= 32) {  // one chunk per lane of the warp: one load of (max, sum)
+      const float2 ml = lane < nsplit_lane ? *reinterpret_cast<const float2*>(part_ml + (base + lane) * 2)
+                                           : make_float2(-INFINITY, 0.f);
+      const float M = warp_max(ml.x);
+      const float e = ml.x == -INFINITY ? 0.f : expf(ml.x - M);
+      const float L = warp_sum(ml.y * e);
+      if (lane < nsplit_lane) wts[t * nsplit + lane] = e * (1.0f / L);
+      continue;
+    }
     float M = -INFINITY;
     for (int s = lane; s < nsplit_lane; s += 32) M = fmaxf(M, part_ml[(base + s) * 2]);
     M = warp_max(M);
@@ -391,46 +396,34 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const float* __restri
     for (int s = lane; s < nsplit_lane; s += 32) wts[t * nsplit + s] *= inv;
   }
   __syncthreads();
+  const int e0 = 8 * threadIdx.x;
+  const bool active = e0 < num_heads * head_dim;
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   float mx = 0.f;
-  for (int i = threadIdx.x; i < (h1 - h0) * head_dim; i += blockDim.x) {
-    const int t = i / head_dim, d = i % head_dim;
-    const float* po = part_o + ((size_t)lane_id * num_heads + h0 + t) * nsplit * head_dim + d;
+  if (active) {
+    const int t = e0 / head_dim, d = e0 - t * head_dim;
+    const float* po = part_o + ((size_t)lane_id * num_heads + t) * nsplit * head_dim + d;
     const float* wt = wts + t * nsplit;
-    float acc = 0.f;
 #pragma unroll 4
-    for (int s = 0; s < nsplit_lane; ++s) acc = fmaf(po[(size_t)s * head_dim], wt[s], acc);
-    const float v = acc;
-    if (so.xs) {
-      row[i] = v;
-      mx = fmaxf(mx, fabsf(v));
-    } else {
-      out[lane_id * ldo + (size_t)(h0 + t) * head_dim + d] = v;
+    for (int s = 0; s < nsplit_lane; ++s) {
+      float v[8];
+      load8(po + (size_t)s * head_dim, v);
+      const float w = wt[s];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = fmaf(v[i], w, acc[i]);
     }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) mx = fmaxf(mx, fabsf(acc[i]));
   }
   if (so.xs) {
-    mx = warp_max(mx);
-    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = mx;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      float t = 0.f;
-      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t = fmaxf(t, sh[w]);
-      xch = t;
-    }
-    cluster_sync_all();
-    float rm = 0.f;
-    const uint32_t a = smem_u32(&xch);
-    for (int q = 0; q < cn; ++q) rm = fmaxf(rm, ld_dsmem_f32(mapa_shared(a, (uint32_t)q)));
-    const float scale = split_scale(rm);
-    const float iscale = 1.0f / scale;
-    const int K = num_heads * head_dim;
-    for (int k8 = threadIdx.x; k8 < (h1 - h0) * head_dim / 8; k8 += blockDim.x) {
-      float v[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) v[i] = row[k8 * 8 + i];
-      store_split8(so, lane_id, K, (size_t)h0 * head_dim + (size_t)k8 * 8, v, iscale);
-    }
-    if (cr == 0 && threadIdx.x == 0) so.xscale[lane_id] = scale;
-    cluster_sync_all();
+    const float2 tot = row_sum_max(0.f, mx, sh, &xch);
+    const float scale = split_scale(tot.y);
+    if (active) store_split8(so, lane_id, (size_t)num_heads * head_dim, (size_t)e0, acc, 1.0f / scale);
+    if (threadIdx.x == 0) so.xscale[lane_id] = scale;
+  } else if (active) {
+    float4* dst = reinterpret_cast<float4*>(out + lane_id * ldo + e0);
+    dst[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    dst[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
   }
 }
 
@@ -441,11 +434,11 @@ size_t attention_workspace_floats(size_t lanes, size_t num_heads, size_t head_di
   return 4 + lanes * num_heads * nsplit * (head_dim + 2);  // work counters + chunk partials
 }
 
-// Positions per work item: 256 (16 pages) unless that leaves fewer than two
+// Positions per work item: 512 (32 pages) unless that leaves fewer than two
 // items per warp of the persistent grid, then halved down to 64.
 int attention_chunk(size_t lanes, size_t num_kv_heads, size_t max_ctx) {
   const size_t warps = (size_t)sm_count() * kAttnWarps;
-  size_t chunk = 256;
+  size_t chunk = 512;
   while (chunk > 64 && lanes * num_kv_heads * ceil_div(max_ctx, chunk) < 2 * warps) chunk /= 2;
   return (int)chunk;
 }
@@ -571,14 +564,14 @@ int paged_attention(const float* q, size_t ldq, const float* pool, size_t page_f
     return rc;
   if (prof) prof->mark(combine_kind, stream);
   {
-    // Cluster of CTAs per lane over its heads (about 7 heads per CTA).
-    int cl = 1;
-    while (cl < 8 && (size_t)cl * 7 < num_heads) cl *= 2;
-    const int hpc = (int)ceil_div(num_heads, (size_t)cl);
-    GLC_REQUIRE(hpc <= 4 * kMaxGroup, "paged_attention: too many heads per combine CTA");
-    const size_t csmem = ((size_t)hpc * nsplit + (so.xs ? (size_t)hpc * head_dim : 0)) * sizeof(float);
+    GLC_REQUIRE(head_dim % 8 == 0 && ldo % 4 == 0 && (num_heads * head_dim) / 8 <= 1024,
+                "paged_attention: combine geometry %zu x %zu unsupported", num_heads, head_dim);
+    const size_t csmem = num_heads * (size_t)nsplit * sizeof(float);
     GLC_REQUIRE(csmem <= 48 * 1024, "paged_attention: %d chunks per lane exceed the combine's shared memory", nsplit);
-    if ((rc = launch_pdl(attn_combine_kernel, dim3((unsigned)cl, (unsigned)lanes), dim3(256), csmem, stream, cl,
+    // One warp per head for the weights (up to 32 warps), enough threads for 8 values each.
+    const size_t vals = ceil_div(num_heads * head_dim / 8, (size_t)32) * 32;
+    const unsigned threads = (unsigned)std::min<size_t>(1024, std::max(vals, num_heads * (size_t)32));
+    if ((rc = launch_pdl(attn_combine_kernel, dim3((unsigned)lanes), dim3(threads), csmem, stream, 1,
                          (const float*)prm.part_o, (const float*)prm.part_ml, nsplit, (int)head_dim, (int)num_heads,
                          out, ldo, so, ctx_lens, chunk)))
       return rc;
