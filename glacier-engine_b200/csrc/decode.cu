@@ -22,6 +22,7 @@
 #include <math.h>
 #include <string.h>
 
+#include <algorithm>
 #include <memory>
 #include <vector>
 
@@ -106,6 +107,16 @@ StepProfiler::~StepProfiler() {
 }
 
 namespace {
+
+// Row i of a prompt chunk: position first + i and a copy of the request's block table.
+__global__ void prefill_rows_kernel(const int32_t* __restrict__ table, int max_pages, int first,
+                                    int32_t* __restrict__ pos, int32_t* __restrict__ tables) {
+  griddep_launch();
+  griddep_wait();
+  const int i = blockIdx.x;
+  if (threadIdx.x == 0) pos[i] = first + i;
+  for (int j = threadIdx.x; j < max_pages; j += blockDim.x) tables[(size_t)i * max_pages + j] = table[j];
+}
 
 __global__ void ctx_from_pos_kernel(const int32_t* __restrict__ pos, int32_t* __restrict__ ctx, int n) {
   griddep_launch();
@@ -242,6 +253,7 @@ struct glacier_cuda_model {
   DevBuf xs_d, xs_q, xs_f, xscale;
   CUtensorMap map_d, map_q, map_f;
   int split_qkv = 1, split_o = 1, split_d = 1;
+  DevBuf pf_pos, pf_bt;  // prompt-chunk positions and per-row block tables (prefill)
   StepProfiler prof;  // optional per-kernel-class timing of decode steps
 };
 
@@ -495,7 +507,8 @@ int glacier_cuda_model_reserve(glacier_cuda_model* m, size_t max_lanes, size_t m
       (rc = m->gu.alloc(L * 2 * (size_t)c.hidden * 4)) || (rc = m->act.alloc(L * (size_t)c.hidden * 4)) ||
       (rc = m->down.alloc(L * c.dim * 4)) || (rc = m->logits.alloc(L * (size_t)c.vocab * 4)) ||
       (rc = m->ctx.alloc(L * 4)) || (rc = m->att_ws.alloc(m->att_floats * 4)) ||
-      (rc = m->arg_ws.alloc(m->arg_bytes)) || (rc = m->status.alloc(L * 4)))
+      (rc = m->arg_ws.alloc(m->arg_bytes)) || (rc = m->status.alloc(L * 4)) || (rc = m->pf_pos.alloc(L * 4)) ||
+      (rc = m->pf_bt.alloc(L * max_pages * 4)))
     return rc;
   // The attention kernel's work counters (start of its workspace) begin at zero
   // and every launch leaves them at zero.
@@ -553,19 +566,16 @@ float* glacier_cuda_kv_pages(glacier_cuda_kv* kv) { return kv ? kv->pool.as<floa
 
 size_t glacier_cuda_kv_page_floats(const glacier_cuda_kv* kv) { return kv ? kv->page_floats : 0; }
 
-int glacier_cuda_decode_step(glacier_cuda_model* m, glacier_cuda_kv* kv, size_t lanes, const int32_t* tokens,
-                             const int32_t* positions, const int32_t* block_tables, size_t max_pages,
-                             const uint64_t* eligible, size_t eligible_words, int32_t* tokens_out,
-                             int32_t* status_out, float* logits_out, void* stream_ptr) {
-  GLC_REQUIRE(m && kv && m->finalized, "decode_step: model not finalized");
-  GLC_REQUIRE(lanes > 0 && lanes <= m->max_lanes, "decode_step: %zu lanes, %zu reserved", lanes, m->max_lanes);
-  GLC_REQUIRE(max_pages > 0 && max_pages <= m->max_pages, "decode_step: %zu pages per lane, %zu reserved", max_pages,
-              m->max_pages);
-  GLC_REQUIRE(tokens && positions && block_tables && tokens_out, "decode_step: null argument");
-  if (eligible)
-    GLC_REQUIRE(eligible_words == ceil_div(m->cfg.vocab, 64), "decode_step: eligible mask needs %zu words per lane",
-                ceil_div(m->cfg.vocab, 64));
-  cudaStream_t st = (cudaStream_t)stream_ptr;
+// How a step ends: every row through the LM head and argmax (decode), no head
+// (a prompt chunk before the last), or the head for the last row only (the
+// last prompt chunk).
+enum StepHead { kHeadAllRows, kHeadNone, kHeadLastRow };
+
+// One batched pass of `lanes` rows through every layer (validated by the caller).
+static int step_impl(glacier_cuda_model* m, glacier_cuda_kv* kv, size_t lanes, const int32_t* tokens,
+                     const int32_t* positions, const int32_t* block_tables, size_t max_pages, const uint64_t* eligible,
+                     size_t eligible_words, int32_t* tokens_out, int32_t* status_out, float* logits_out,
+                     cudaStream_t st, StepHead head) {
   const auto& c = m->cfg;
   const size_t D = c.dim, F = c.hidden, B = lanes;
   const size_t max_ctx = max_pages * 16;
@@ -636,6 +646,26 @@ int glacier_cuda_decode_step(glacier_cuda_model* m, glacier_cuda_kv* kv, size_t 
     mark(GLACIER_CUDA_STEP_PROJ_DOWN);
     if ((rc = project(L.d.w, m->act.as<float>(), F, so_f, m->map_f, m->down.as<float>(), D, sd))) return rc;
   }
+  if (head == kHeadNone) {
+    mark(-1);
+    return GLACIER_CUDA_OK;
+  }
+  if (head == kHeadLastRow) {
+    // Final residual + RMSNorm of the last row only (fp32), its LM-head GEMV and argmax.
+    const size_t r = B - 1;
+    mark(GLACIER_CUDA_STEP_NORM);
+    if ((rc = add_rmsnorm(x + r * D, D, m->down.as<float>() + r * D, D, B * D, sd, x + r * D, D,
+                          m->final_norm.as<float>(), c.rms_eps, hn, D, 1, D, st)))
+      return rc;
+    float* logits = logits_out ? logits_out : m->logits.as<float>();
+    mark(GLACIER_CUDA_STEP_LM_HEAD);
+    if ((rc = int4_linear(m->lm.w, hn, D, 1, nullptr, logits, c.vocab, st))) return rc;
+    mark(GLACIER_CUDA_STEP_ARGMAX);
+    rc = argmax_rows(logits, c.vocab, 1, c.vocab, eligible, eligible_words, nullptr, tokens_out,
+                     status_out ? status_out : m->status.as<int32_t>(), m->arg_ws.p, m->arg_bytes, st);
+    mark(-1);
+    return rc;
+  }
   mark(GLACIER_CUDA_STEP_NORM);
   if ((rc = add_rmsnorm(x, D, m->down.as<float>(), D, B * D, sd, x, D, m->final_norm.as<float>(), c.rms_eps,
                         m->gemm ? nullptr : hn, D, B, D, st, so_d)))
@@ -648,6 +678,53 @@ int glacier_cuda_decode_step(glacier_cuda_model* m, glacier_cuda_kv* kv, size_t 
                    status_out ? status_out : m->status.as<int32_t>(), m->arg_ws.p, m->arg_bytes, st);
   mark(-1);
   return rc;
+}
+
+int glacier_cuda_decode_step(glacier_cuda_model* m, glacier_cuda_kv* kv, size_t lanes, const int32_t* tokens,
+                             const int32_t* positions, const int32_t* block_tables, size_t max_pages,
+                             const uint64_t* eligible, size_t eligible_words, int32_t* tokens_out,
+                             int32_t* status_out, float* logits_out, void* stream_ptr) {
+  GLC_REQUIRE(m && kv && m->finalized, "decode_step: model not finalized");
+  GLC_REQUIRE(lanes > 0 && lanes <= m->max_lanes, "decode_step: %zu lanes, %zu reserved", lanes, m->max_lanes);
+  GLC_REQUIRE(max_pages > 0 && max_pages <= m->max_pages, "decode_step: %zu pages per lane, %zu reserved", max_pages,
+              m->max_pages);
+  GLC_REQUIRE(tokens && positions && block_tables && tokens_out, "decode_step: null argument");
+  if (eligible)
+    GLC_REQUIRE(eligible_words == ceil_div(m->cfg.vocab, 64), "decode_step: eligible mask needs %zu words per lane",
+                ceil_div(m->cfg.vocab, 64));
+  return step_impl(m, kv, lanes, tokens, positions, block_tables, max_pages, eligible, eligible_words, tokens_out,
+                   status_out, logits_out, (cudaStream_t)stream_ptr, kHeadAllRows);
+}
+
+int glacier_cuda_prefill(glacier_cuda_model* m, glacier_cuda_kv* kv, const int32_t* tokens, size_t count,
+                         int32_t start, const int32_t* block_table, size_t max_pages, const uint64_t* eligible,
+                         size_t eligible_words, int32_t* token_out, int32_t* status_out, float* logits_out,
+                         void* stream_ptr) {
+  GLC_REQUIRE(m && kv && m->finalized && m->max_lanes > 0, "prefill: model not finalized and reserved");
+  GLC_REQUIRE(tokens && block_table && token_out && count > 0 && start >= 0, "prefill: null or empty argument");
+  GLC_REQUIRE(max_pages > 0 && max_pages <= m->max_pages, "prefill: %zu pages, %zu reserved", max_pages,
+              m->max_pages);
+  GLC_REQUIRE((size_t)start + count <= max_pages * 16, "prefill: positions %d..%zu exceed the block table", start,
+              (size_t)start + count - 1);
+  if (eligible)
+    GLC_REQUIRE(eligible_words == ceil_div(m->cfg.vocab, 64), "prefill: eligible mask needs %zu words",
+                ceil_div(m->cfg.vocab, 64));
+  cudaStream_t st = (cudaStream_t)stream_ptr;
+  const size_t chunk = m->max_lanes;
+  int32_t* pos = m->pf_pos.as<int32_t>();
+  int32_t* bt = m->pf_bt.as<int32_t>();
+  for (size_t b0 = 0; b0 < count; b0 += chunk) {
+    const size_t nb = std::min(chunk, count - b0);
+    // Positions start + b0 + i and the request's block table for every row of the chunk.
+    int rc = launch_pdl(prefill_rows_kernel, dim3((unsigned)nb), dim3(256), 0, st, 1, block_table, (int)max_pages,
+                        start + (int)b0, pos, bt);
+    if (rc) return rc;
+    const bool last = b0 + nb == count;
+    rc = step_impl(m, kv, nb, tokens + b0, pos, bt, max_pages, eligible, eligible_words, token_out, status_out,
+                   logits_out, st, last ? kHeadLastRow : kHeadNone);
+    if (rc) return rc;
+  }
+  return GLACIER_CUDA_OK;
 }
 
 int glacier_cuda_model_profile(glacier_cuda_model* m, int enable) {

@@ -210,6 +210,24 @@ class DecodeSession:
                   self.status.data_ptr(), None if logits is None else logits.data_ptr(), s.cuda_stream)
         return self.out
 
+    def prefill(self, prompt, lane: int = 0, start: int = 0, eligible=None, logits=None, stream=None):
+        """Feeds prompt tokens (host sequence or device int32 tensor) of one request at positions
+        start.. through lane `lane`'s block table; returns the device int32 tensor [1] holding
+        the greedy token that follows (generate.zig prompt loop, batched)."""
+        torch = self.torch
+        dev = self.tokens.device
+        toks = torch.as_tensor(prompt, dtype=torch.int32).to(dev).contiguous()
+        out = torch.empty(1, dtype=torch.int32, device=dev)
+        status = torch.empty(1, dtype=torch.int32, device=dev)
+        s = stream if stream is not None else torch.cuda.current_stream()
+        words = 0 if eligible is None else eligible.shape[-1]
+        _lib.call("glacier_cuda_prefill", self.dm.h, self.kv, toks.data_ptr(), toks.numel(), start,
+                  self.block_tables[lane].data_ptr(), self.max_pages,
+                  None if eligible is None else eligible.data_ptr(), words, out.data_ptr(), status.data_ptr(),
+                  None if logits is None else logits.data_ptr(), s.cuda_stream)
+        self.last_status = status
+        return out
+
     def close(self):
         if getattr(self, "kv", None):
             _lib.lib().glacier_cuda_kv_destroy(self.kv)

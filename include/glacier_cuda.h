@@ -254,6 +254,19 @@ int glacier_cuda_decode_step(glacier_cuda_model *model, glacier_cuda_kv *kv, siz
                              size_t max_pages, const uint64_t *eligible, size_t eligible_words,
                              int32_t *tokens_out, int32_t *status_out, float *logits_out, void *stream);
 
+/* Prompt prefill of one request: the batched counterpart of the reference's prompt loop
+ * (runPackedBatchPrefill, src/generate.zig:3397-3548; for g32 the reference feeds prompt tokens
+ * one at a time, :2377).  tokens[0..count) (device) go in at positions start..start+count-1 of
+ * block_table[0..max_pages) (device), in chunks of up to the reserved lane count; each chunk is one
+ * batched pass whose rows attend causally to every earlier position, and every position's K/V rows
+ * are written.  The greedy token after the last prompt position goes to token_out[0] (device),
+ * its status to status_out[0] (may be NULL) and its logits to logits_out[vocab] (may be NULL).
+ * Requires glacier_cuda_model_reserve. */
+int glacier_cuda_prefill(glacier_cuda_model *model, glacier_cuda_kv *kv, const int32_t *tokens, size_t count,
+                         int32_t start, const int32_t *block_table, size_t max_pages, const uint64_t *eligible,
+                         size_t eligible_words, int32_t *token_out, int32_t *status_out, float *logits_out,
+                         void *stream);
+
 /* Diagnostics, no reference counterpart: per kernel class device time of decode steps.
  * glacier_cuda_model_profile(model, 1) makes later decode steps record CUDA events on their
  * stream between the step's kernel classes (no synchronisation inside the step); 0 stops.

@@ -117,3 +117,58 @@ def test_step_profile_counts_every_kernel_class():
     assert list(regions) == [0] * n
     sess.close()
     dm.close()
+
+
+def _prefill_parity(cfg, reserve_lanes, prompt_len, new_tokens, seed=11):
+    """Chunked prefill of one prompt, then greedy decode steps, against the oracle's
+    token-at-a-time prompt loop (the reference's path for g32)."""
+    from glacier_b200.model import DecodeSession, DeviceModel, SyntheticModel
+    m = SyntheticModel(cfg, seed=seed)
+    max_pages = -(-(prompt_len + new_tokens) // 16)
+    dm = DeviceModel(m, max_positions=max_pages * 16)
+    sess = DecodeSession(dm, 1, max_pages, reserve_lanes=reserve_lanes)
+    om = oracle.OracleModel(m, rope_positions=max_pages * 16, threads=4)
+    pool = np.zeros(max_pages * om.page_floats(), np.float32)
+    bt = np.arange(max_pages, dtype=np.int32)
+    rng = np.random.default_rng(seed)
+    prompt = rng.integers(0, cfg.vocab, size=prompt_len).astype(np.int32)
+    for pos in range(prompt_len):
+        ol, _ = om.decode_token(pool, bt, pos, int(prompt[pos]))
+    logits_dev = torch.empty(cfg.vocab, dtype=torch.float32, device="cuda")
+    tok = int(sess.prefill(prompt, logits=logits_dev).cpu()[0])
+    assert int(sess.last_status.cpu()[0]) == 0
+    assert max_rel_err(logits_dev.cpu().numpy(), ol) <= REL_TOL
+    ref = oracle.argmax(ol)
+    if tok != ref:
+        assert near_tie(ol)
+        return 0
+    compared = 1
+    cur, pos = tok, prompt_len
+    step_logits = torch.empty((1, cfg.vocab), dtype=torch.float32, device="cuda")
+    for _ in range(new_tokens - 1):
+        out = int(sess.step(tokens=[cur], positions=[pos], logits=step_logits).cpu()[0])
+        ol, _ = om.decode_token(pool, bt, pos, cur)
+        assert max_rel_err(step_logits.cpu().numpy()[0], ol) <= REL_TOL, pos
+        ref = oracle.argmax(ol)
+        if out != ref:
+            assert near_tie(ol)
+            break
+        compared += 1
+        cur, pos = out, pos + 1
+    sess.close()
+    dm.close()
+    return compared
+
+
+def test_prefill_chunks_on_tensor_cores_then_decode():
+    from glacier_b200.model import ModelConfig
+    # 16 reserved lanes: tensor-core projections; 40 prompt tokens = chunks of 16, 16 and 8
+    cfg = ModelConfig(num_layers=2, dim=512, hidden=1024, num_heads=28, num_kv_heads=4, head_dim=128, vocab=2048)
+    assert _prefill_parity(cfg, reserve_lanes=16, prompt_len=40, new_tokens=4) >= 2
+
+
+def test_prefill_chunks_on_gemv_path():
+    from glacier_b200.model import ModelConfig
+    # 4 reserved lanes: GEMV projections; 19 prompt tokens = chunks of 4 (x4) and 3
+    cfg = ModelConfig(num_layers=2, dim=256, hidden=512, num_heads=8, num_kv_heads=2, head_dim=64, vocab=1000)
+    assert _prefill_parity(cfg, reserve_lanes=4, prompt_len=19, new_tokens=3) >= 2
