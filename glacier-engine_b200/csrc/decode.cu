@@ -54,6 +54,11 @@ int argmax_rows(const float* logits, size_t ld, size_t batch, size_t n, const ui
                 glacier_argmax_result* out, int32_t* tokens, int32_t* status, void* workspace, size_t ws_bytes,
                 cudaStream_t stream);
 
+int tp_unique_id(void* out);
+int tp_comm_create(void** comm, int rank, int world, const void* id_bytes);
+void tp_comm_destroy(void* comm);
+int tp_all_reduce(void* comm, float* buf, size_t count, cudaStream_t stream);
+
 size_t gemm_split_bytes(size_t np, size_t K);
 bool gemm_tc_supported(const Int4Weight& w);
 int split_activation(const float* x, size_t ldx, size_t n, size_t K, size_t np, __half* xs, float* xscale,
@@ -254,6 +259,10 @@ struct glacier_cuda_model {
   CUtensorMap map_d, map_q, map_f;
   int split_qkv = 1, split_o = 1, split_d = 1;
   DevBuf pf_pos, pf_bt;  // prompt-chunk positions and per-row block tables (prefill)
+  // Tensor parallelism: this rank's NCCL communicator (nullptr: one GPU).
+  void* tp_comm = nullptr;
+  int tp_rank = 0, tp_world = 1;
+  ~glacier_cuda_model() { tp_comm_destroy(tp_comm); }
   StepProfiler prof;  // optional per-kernel-class timing of decode steps
 };
 
@@ -633,6 +642,8 @@ static int step_impl(glacier_cuda_model* m, glacier_cuda_kv* kv, size_t lanes, c
       return rc;
     mark(GLACIER_CUDA_STEP_PROJ_O);
     if ((rc = project(L.o.w, m->attn.as<float>(), m->q_dim, so_q, m->map_q, m->proj.as<float>(), D, so_))) return rc;
+    // Tensor parallel: every split-K partial of o summed over the ranks' head slices.
+    if (m->tp_comm && (rc = tp_all_reduce(m->tp_comm, m->proj.as<float>(), (size_t)so_ * B * D, st))) return rc;
     mark(GLACIER_CUDA_STEP_NORM);
     if ((rc = add_rmsnorm(x, D, m->proj.as<float>(), D, B * D, so_, x, D, L.post_norm.as<float>(), c.rms_eps,
                           m->gemm ? nullptr : hn, D, B, D, st, so_d)))
@@ -645,6 +656,8 @@ static int step_impl(glacier_cuda_model* m, glacier_cuda_kv* kv, size_t lanes, c
       return rc;
     mark(GLACIER_CUDA_STEP_PROJ_DOWN);
     if ((rc = project(L.d.w, m->act.as<float>(), F, so_f, m->map_f, m->down.as<float>(), D, sd))) return rc;
+    // Tensor parallel: every split-K partial of down summed over the ranks' FFN slices.
+    if (m->tp_comm && (rc = tp_all_reduce(m->tp_comm, m->down.as<float>(), (size_t)sd * B * D, st))) return rc;
   }
   if (head == kHeadNone) {
     mark(-1);
@@ -724,6 +737,22 @@ int glacier_cuda_prefill(glacier_cuda_model* m, glacier_cuda_kv* kv, const int32
                    logits_out, st, last ? kHeadLastRow : kHeadNone);
     if (rc) return rc;
   }
+  return GLACIER_CUDA_OK;
+}
+
+int glacier_cuda_tp_unique_id(void* id_out) { return tp_unique_id(id_out); }
+
+int glacier_cuda_model_tp_init(glacier_cuda_model* m, int rank, int world, const void* id) {
+  GLC_REQUIRE(m && m->finalized, "model_tp_init: model not finalized");
+  GLC_REQUIRE(!m->tp_comm, "model_tp_init: tensor parallelism already set up");
+  const int rc = bind_device(m);
+  if (rc) return rc;
+  void* comm = nullptr;
+  const int r = tp_comm_create(&comm, rank, world, id);
+  if (r) return r;
+  m->tp_comm = comm;
+  m->tp_rank = rank;
+  m->tp_world = world;
   return GLACIER_CUDA_OK;
 }
 

@@ -67,6 +67,8 @@ SIGNATURES = {
     "glacier_cuda_kv_page_floats": ([vp], sz),
     "glacier_cuda_decode_step": ([vp, vp, sz, vp, vp, vp, sz, vp, sz, vp, vp, vp, vp], i32),
     "glacier_cuda_prefill": ([vp, vp, vp, sz, i32, vp, sz, vp, sz, vp, vp, vp, vp], i32),
+    "glacier_cuda_tp_unique_id": ([vp], i32),
+    "glacier_cuda_model_tp_init": ([vp, C.c_int, C.c_int, vp], i32),
     "glacier_cuda_model_profile": ([vp, C.c_int], i32),
     "glacier_cuda_model_profile_read": ([vp, vp, vp, sz], i32),
 }

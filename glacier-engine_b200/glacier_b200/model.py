@@ -113,6 +113,62 @@ class SyntheticModel:
         self.lm_head = random_int4(rng, cfg.vocab, cfg.dim, cfg.group)
 
 
+def _rows(w, out_f: int, in_f: int, r0: int, r1: int, group: int = 32):
+    """Rows [r0, r1) of an INT4 matrix given as (packed [out_f*in_f/2], scales [out_f*in_f/group])."""
+    packed, scales = w
+    return (np.ascontiguousarray(packed.reshape(out_f, in_f // 2)[r0:r1]).ravel(),
+            np.ascontiguousarray(scales.reshape(out_f, in_f // group)[r0:r1]).ravel())
+
+
+def _cols(w, out_f: int, in_f: int, c0: int, c1: int, group: int = 32):
+    """Input columns [c0, c1) (whole scale groups) of an INT4 matrix."""
+    assert c0 % group == 0 and c1 % group == 0
+    packed, scales = w
+    return (np.ascontiguousarray(packed.reshape(out_f, in_f // 2)[:, c0 // 2:c1 // 2]).ravel(),
+            np.ascontiguousarray(scales.reshape(out_f, in_f // group)[:, c0 // group:c1 // group]).ravel())
+
+
+class TensorParallelShard:
+    """Rank `rank`'s share of a model split over `world` GPUs (Megatron split).
+
+    q/k/v rows of this rank's heads (whole GQA groups), gate/up rows of its FFN
+    slice, the matching input columns of o and down; norms, biases of its heads,
+    embedding and LM head as in the full model.  Its config carries the local
+    head counts and FFN width, so the device model is self-consistent; the
+    decode step all-reduces the o and down projections over the ranks."""
+
+    def __init__(self, m: SyntheticModel, rank: int, world: int):
+        c = dict(m.cfg)
+        H, Hkv, hd, F, D, g = c["num_heads"], c["num_kv_heads"], c["head_dim"], c["hidden"], c["dim"], c["group"]
+        if H % world or Hkv % world or F % (world * g) or (H // world * hd) % g:
+            raise ValueError(f"a {H}/{Hkv}-head, {F}-wide model does not split over {world} GPUs")
+        hl, kl, fl = H // world, Hkv // world, F // world
+        q0, q1 = rank * hl * hd, (rank + 1) * hl * hd
+        k0, k1 = rank * kl * hd, (rank + 1) * kl * hd
+        f0, f1 = rank * fl, (rank + 1) * fl
+        self.cfg = dict(c, num_heads=hl, num_kv_heads=kl, hidden=fl)
+        self.config = m.config
+        self.rank, self.world = rank, world
+        self.layers = []
+        for L in m.layers:
+            self.layers.append({
+                "wq": _rows(L["wq"], H * hd, D, q0, q1, g), "wk": _rows(L["wk"], Hkv * hd, D, k0, k1, g),
+                "wv": _rows(L["wv"], Hkv * hd, D, k0, k1, g), "wo": _cols(L["wo"], D, H * hd, q0, q1, g),
+                "wg": _rows(L["wg"], F, D, f0, f1, g), "wu": _rows(L["wu"], F, D, f0, f1, g),
+                "wd": _cols(L["wd"], D, F, f0, f1, g),
+                "bq": L["bq"][q0:q1].copy(), "bk": L["bk"][k0:k1].copy(), "bv": L["bv"][k0:k1].copy(),
+                "input_norm": L["input_norm"], "post_attn_norm": L["post_attn_norm"],
+            })
+        self.embedding, self.final_norm, self.lm_head = m.embedding, m.final_norm, m.lm_head
+
+
+def tp_unique_id() -> bytes:
+    """NCCL unique id for a tensor-parallel group (made on rank 0, handed to every rank)."""
+    buf = (C.c_uint8 * 128)()
+    _lib.call("glacier_cuda_tp_unique_id", buf)
+    return bytes(buf)
+
+
 def _p(a: np.ndarray):
     return a.ctypes.data
 
@@ -147,6 +203,11 @@ class DeviceModel:
         except Exception:
             self.close()
             raise
+
+    def enable_tensor_parallel(self, rank: int, world: int, unique_id: bytes):
+        """Joins the tensor-parallel group (blocks until every rank has joined)."""
+        buf = (C.c_uint8 * 128).from_buffer_copy(unique_id)
+        _lib.call("glacier_cuda_model_tp_init", self.h, rank, world, buf)
 
     def _int4(self, layer, kind, packed, scales):
         packed = np.ascontiguousarray(packed, np.uint8)

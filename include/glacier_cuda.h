@@ -267,6 +267,18 @@ int glacier_cuda_prefill(glacier_cuda_model *model, glacier_cuda_kv *kv, const i
                          size_t eligible_words, int32_t *token_out, int32_t *status_out, float *logits_out,
                          void *stream);
 
+/* Tensor parallelism over G GPUs, one process per GPU (no reference counterpart: the reference
+ * runs on one device).  Each rank creates its model with its local geometry: num_heads/G and
+ * num_kv_heads/G heads and hidden/G FFN rows.  It loads the q/k/v, gate and up rows of its slice
+ * and the matching input columns of o and down; norms, embedding and LM head are replicated.
+ * After glacier_cuda_model_tp_init, decode steps and prefill all-reduce the o and down
+ * projections over the ranks with NCCL on the step's stream, so every rank produces the same
+ * tokens.  Rank 0 makes the id with glacier_cuda_tp_unique_id and the caller hands it to every
+ * rank; tp_init blocks until all ranks have joined. */
+#define GLACIER_CUDA_TP_ID_BYTES 128
+int glacier_cuda_tp_unique_id(void *id_out);
+int glacier_cuda_model_tp_init(glacier_cuda_model *model, int rank, int world, const void *id);
+
 /* Diagnostics, no reference counterpart: per kernel class device time of decode steps.
  * glacier_cuda_model_profile(model, 1) makes later decode steps record CUDA events on their
  * stream between the step's kernel classes (no synchronisation inside the step); 0 stops.
