@@ -52,6 +52,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=None,
                     help="build only this many decoder layers (small cases for ncu captures; not a bench number)")
+    ap.add_argument("--tp", type=int, default=1,
+                    help="tensor-parallel degree: with --tp N under torchrun (N ranks) the ranks share one model "
+                         "and one set of lanes (strong scaling); default 1 = lane partition (weak scaling)")
     ap.add_argument("--workload", choices=["decode", "prefill"], default="decode",
                     help="decode: the headline 64-lane step; prefill: one prompt of --tokens tokens (config 4)")
     ap.add_argument("--tokens", type=int, default=2048, help="prompt length for --workload prefill")
@@ -232,7 +235,8 @@ def run_reference(args):
 def run_glacier(args):
     import torch
     from glacier_b200 import _lib
-    from glacier_b200.model import PRESETS, DecodeSession, DeviceModel, SyntheticModel
+    from glacier_b200.model import (PRESETS, DecodeSession, DeviceModel, SyntheticModel, TensorParallelShard,
+                                    tp_unique_id)
 
     ws, rank, local = dist_setup()
     torch.cuda.set_device(local)
@@ -240,15 +244,25 @@ def run_glacier(args):
         import datetime
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    tp = args.tp
+    if tp > 1 and tp != ws:
+        raise SystemExit(f"--tp {tp} needs {tp} ranks (got {ws})")
     cfg = PRESETS[args.model]
     lanes = args.lanes
-    ctxs = lane_contexts(args, lanes, rank)
+    # Tensor parallel: every rank serves the same lanes; lane partition: each rank its own.
+    ctxs = lane_contexts(args, lanes, 0 if tp > 1 else rank)
     total_steps = args.warmup + 2 * args.steps + args.profile_steps + 4
     max_pages = -(-(int(ctxs.max()) + total_steps + 1) // 16)
 
     t0 = time.time()
     model = SyntheticModel(cfg, seed=args.seed, layers=args.layers)
-    dm = DeviceModel(model, max_positions=max_pages * 16)
+    if tp > 1:
+        dm = DeviceModel(TensorParallelShard(model, rank, tp), max_positions=max_pages * 16)
+        uid = [tp_unique_id() if rank == 0 else None]
+        torch.distributed.broadcast_object_list(uid, src=0)
+        dm.enable_tensor_parallel(rank, tp, uid[0])
+    else:
+        dm = DeviceModel(model, max_positions=max_pages * 16)
     sess = DecodeSession(dm, lanes, max_pages)
     # KV: every lane's pages filled with random FP32 rows (equivalent to having
     # prefilled its context; decode cost depends only on the context length).
@@ -325,7 +339,7 @@ def run_glacier(args):
     dom["kernels"].update(gemv_batch1_timing(torch, cfg, stream))
 
     dev_ms, e2e_ms = max_over_ranks([dev_ms, e2e_s * 1e3], ws, dev)
-    tokens_total = lanes * args.steps * ws
+    tokens_total = lanes * args.steps * (1 if tp > 1 else ws)
     value = tokens_total / (dev_ms / 1e3)
     e2e_value = tokens_total / (e2e_ms / 1e3)
 
@@ -339,11 +353,15 @@ def run_glacier(args):
         peaks = load_peaks()
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": dev_ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "ms_per_step": dev_ms / args.steps, "higher_is_better": True,
+            "scaling": "strong" if tp > 1 else "weak", "vs_baseline": None,
             "dtype": "f32 activations / int4 g32 weights (fp16 scales) / f32 KV", "data": "synthetic",
-            "config": {"workload": "7B decode, 64 lanes per GPU, ctx U[256,4096], greedy (BASELINE config 5)",
-                       "model": args.model, "lanes_per_gpu": lanes, "mean_ctx": float(np.mean(ctxs)),
-                       "parallelism": f"lane partition x{ws} (weights replicated, no collective)",
+            "config": {"workload": (f"7B decode, {lanes} lanes over {tp} tensor-parallel GPUs" if tp > 1 else
+                                    "7B decode, 64 lanes per GPU") + ", ctx U[256,4096], greedy (BASELINE config 5)",
+                       "model": args.model, "lanes_per_gpu": lanes if tp == 1 else lanes / tp,
+                       "mean_ctx": float(np.mean(ctxs)),
+                       "parallelism": (f"tensor parallel x{tp} (Megatron split, NCCL all-reduce of o and down)"
+                                       if tp > 1 else f"lane partition x{ws} (weights replicated, no collective)"),
                        "l2": "working set (weights 4.0 GB + KV) >> 126 MB L2; no flush needed",
                        "setup_seconds": round(setup_s, 1)},
             "achieved_step_gbs": step_bytes / (dev_ms / args.steps / 1e3) / 1e9,

@@ -58,6 +58,7 @@ int tp_unique_id(void* out);
 int tp_comm_create(void** comm, int rank, int world, const void* id_bytes);
 void tp_comm_destroy(void* comm);
 int tp_all_reduce(void* comm, float* buf, size_t count, cudaStream_t stream);
+int reduce_splits(const float* part, size_t split_stride, int nsplit, float* y, size_t n, cudaStream_t stream);
 
 size_t gemm_split_bytes(size_t np, size_t K);
 bool gemm_tc_supported(const Int4Weight& w);
@@ -618,7 +619,15 @@ static int step_impl(glacier_cuda_model* m, glacier_cuda_kv* kv, size_t lanes, c
     if (!m->gemm) return int4_linear(w, xin, K, B, nullptr, y, ldy, st);
     return gemm_int4_tc(w, map, so.xscale, B, m->np, y, ldy, nsplit, B * ldy, nullptr, st);
   };
-  const int sq = m->gemm ? m->split_qkv : 1, so_ = m->gemm ? m->split_o : 1, sd = m->gemm ? m->split_d : 1;
+  const int sq = m->gemm ? m->split_qkv : 1, so_gemm = m->gemm ? m->split_o : 1, sd_gemm = m->gemm ? m->split_d : 1;
+  // Partials the o / down consumers sum: with tensor parallelism the split-K
+  // partials are summed locally and all-reduced as one buffer.
+  const int so_ = m->tp_comm ? 1 : so_gemm, sd = m->tp_comm ? 1 : sd_gemm;
+  auto tp_reduce = [&](float* buf, int nsplit) -> int {
+    int r;
+    if (nsplit > 1 && (r = reduce_splits(buf, B * D, nsplit, buf, B * D, st))) return r;
+    return tp_all_reduce(m->tp_comm, buf, B * D, st);
+  };
   for (size_t l = 0; l < c.num_layers; ++l) {
     Layer& L = *m->layers[l];
     // x (+ previous layer's down projection, its split-K partials summed in order) -> x, normed hn
@@ -641,9 +650,10 @@ static int step_impl(glacier_cuda_model* m, glacier_cuda_kv* kv, size_t lanes, c
                               m->att_chunk, st, so_q, prof, GLACIER_CUDA_STEP_ATTN_COMBINE)))
       return rc;
     mark(GLACIER_CUDA_STEP_PROJ_O);
-    if ((rc = project(L.o.w, m->attn.as<float>(), m->q_dim, so_q, m->map_q, m->proj.as<float>(), D, so_))) return rc;
-    // Tensor parallel: every split-K partial of o summed over the ranks' head slices.
-    if (m->tp_comm && (rc = tp_all_reduce(m->tp_comm, m->proj.as<float>(), (size_t)so_ * B * D, st))) return rc;
+    if ((rc = project(L.o.w, m->attn.as<float>(), m->q_dim, so_q, m->map_q, m->proj.as<float>(), D, so_gemm)))
+      return rc;
+    // Tensor parallel: o summed over the ranks' head slices.
+    if (m->tp_comm && (rc = tp_reduce(m->proj.as<float>(), so_gemm))) return rc;
     mark(GLACIER_CUDA_STEP_NORM);
     if ((rc = add_rmsnorm(x, D, m->proj.as<float>(), D, B * D, so_, x, D, L.post_norm.as<float>(), c.rms_eps,
                           m->gemm ? nullptr : hn, D, B, D, st, so_d)))
@@ -655,9 +665,9 @@ static int step_impl(glacier_cuda_model* m, glacier_cuda_kv* kv, size_t lanes, c
                        F, st, so_f)))
       return rc;
     mark(GLACIER_CUDA_STEP_PROJ_DOWN);
-    if ((rc = project(L.d.w, m->act.as<float>(), F, so_f, m->map_f, m->down.as<float>(), D, sd))) return rc;
-    // Tensor parallel: every split-K partial of down summed over the ranks' FFN slices.
-    if (m->tp_comm && (rc = tp_all_reduce(m->tp_comm, m->down.as<float>(), (size_t)sd * B * D, st))) return rc;
+    if ((rc = project(L.d.w, m->act.as<float>(), F, so_f, m->map_f, m->down.as<float>(), D, sd_gemm))) return rc;
+    // Tensor parallel: down summed over the ranks' FFN slices.
+    if (m->tp_comm && (rc = tp_reduce(m->down.as<float>(), sd_gemm))) return rc;
   }
   if (head == kHeadNone) {
     mark(-1);
