@@ -252,6 +252,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   }
 }
 
+// True in exactly one lane of a converged warp.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t p;
+  asm volatile("{\n\t.reg .pred P;\n\telect.sync _|P, 0xffffffff;\n\tselp.u32 %0, 1, 0, P;\n\t}" : "=r"(p));
+  return p != 0;
+}
+
 // Non-blocking probe of a phase (no suspension), for the one thread on a
 // pipeline's critical path: a satisfied try_wait costs it hundreds of cycles.
 __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {

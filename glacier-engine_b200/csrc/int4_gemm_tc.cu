@@ -23,7 +23,8 @@
 //   warp 0      TMA producer: 128 x 256-code nibble tiles (SWIZZLE_128B) plus the
 //               matching 128 x 8 fp16 scale tiles, into a ring of super-stages
 //   warp 1      TMA producer: 64-K activation tiles [Xhi | Xlo] (SWIZZLE_128B)
-//   warp 2      allocates TMEM; one thread issues tcgen05.mma
+//   warp 2      allocates TMEM; runs the MMA loop converged, one elected lane
+//               issues every tcgen05.mma and commit
 //   warps 3-10  converters (two per 32-row TMEM lane quarter): nibbles + scales
 //               -> -Whi / Wlo fp16 pairs written straight into TMEM with
 //               tcgen05.st; the MMA reads A from TMEM (the descriptor's negate
@@ -278,51 +279,61 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     }
   } else if (warp == 2) {
     // ---- MMA issuer ----
-    if (lane == 0) {
-      // A holds -Whi (negated back by the descriptor) and Wlo.
-      const uint32_t id_hl = idesc_f16(2 * p.np, true), id_h = idesc_f16(p.np);
-      const uint64_t bdesc0 = sdesc(smem_u32(btile));
-      const uint64_t bbox = (uint64_t)(bbytes >> 4);  // descriptor address units per B box
-      uint32_t ch = 0, acc_i = 0;
-      uint32_t as = 0, a_ph = 0, bs = 0, b_ph = 0;  // ring positions and phases, advanced per chunk
-      for (int u = blockIdx.x; u < p.units && !s_abort; u += gridDim.x) {
-        const Unit w = unit_of(p, u);
-        if (w.nch == 0) continue;
-        const int ab = acc_i % p.acc_bufs;
-        const uint32_t use = acc_i / p.acc_bufs;
-        if (!mbar_wait(&acc_empty[ab], (use & 1) ^ 1, p.err)) { s_abort = 1; break; }
+    // The whole warp runs this loop so that descriptors and TMEM addresses stay
+    // warp-uniform; one lane, elected once, issues every MMA and every commit (a
+    // commit tracks the MMAs of the thread that issues it).  Issuing from a
+    // diverged single lane instead costs about 47 cycles per tcgen05.mma, which
+    // is longer than an M128 x N64 x K16 MMA takes on the tensor pipe.
+    const bool leader = elect_one();
+    // A holds -Whi (negated back by the descriptor) and Wlo.
+    const uint32_t id_hl = idesc_f16(2 * p.np, true), id_h = idesc_f16(p.np);
+    const uint64_t bdesc0 = sdesc(smem_u32(btile));
+    const uint64_t bbox = (uint64_t)(bbytes >> 4);  // descriptor address units per B box
+    uint32_t ch = 0, acc_i = 0;
+    uint32_t as = 0, a_ph = 0, bs = 0, b_ph = 0;  // ring positions and phases, advanced per chunk
+    for (int u = blockIdx.x; u < p.units && !s_abort; u += gridDim.x) {
+      const Unit w = unit_of(p, u);
+      if (w.nch == 0) continue;
+      const int ab = acc_i % p.acc_bufs;
+      const uint32_t use = acc_i / p.acc_bufs;
+      if (!__all_sync(0xffffffffu, mbar_wait(&acc_empty[ab], (use & 1) ^ 1, p.err))) { s_abort = 1; break; }
+      tc_fence_after();
+      const uint32_t d = tmem + (uint32_t)(ab * p.acc_cols);
+      bool ok = true;
+      for (int i = 0; i < w.nch; ++i, ++ch) {
+        if (!__all_sync(0xffffffffu,
+                        mbar_wait_poll(&b_full[bs], b_ph, p.err) && mbar_wait_poll(&a_full[as], a_ph, p.err))) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
-        const uint32_t d = tmem + (uint32_t)(ab * p.acc_cols);
-        bool ok = true;
-        for (int i = 0; i < w.nch; ++i, ++ch) {
-          if (!mbar_wait_poll(&b_full[bs], b_ph, p.err) || !mbar_wait_poll(&a_full[as], a_ph, p.err)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t ahi = tmem + a_base + (uint32_t)as * kAColsPerSlot;
-          const uint32_t alo = ahi + kAColsPerSlot / 2;
-          const uint64_t bd = bdesc0 + (uint64_t)bs * kSub * bbox;  // +2 per 16-K step (32 bytes)
-          umma_f16_ts(d, ahi, bd, id_hl, i > 0 ? 1u : 0u);     // Whi x [Xhi | Xlo]
-          umma_f16_ts(d, alo, bd, id_h, 1u);                   // Wlo x Xhi
+        const uint32_t ahi = tmem + a_base + (uint32_t)as * kAColsPerSlot;
+        const uint32_t alo = ahi + kAColsPerSlot / 2;
+        const uint64_t bd = bdesc0 + (uint64_t)bs * kSub * bbox;  // +2 per 16-K step (32 bytes)
+        if (leader) {
+          umma_f16_ts(d, ahi, bd, id_hl, i > 0 ? 1u : 0u);  // Whi x [Xhi | Xlo]
+          umma_f16_ts(d, alo, bd, id_h, 1u);                // Wlo x Xhi
 #pragma unroll
           for (int kk = 1; kk < kPipeK / 16; ++kk) {
-            const uint32_t ac = (uint32_t)(kk * 8);                       // 8 columns per 16 K
+            const uint32_t ac = (uint32_t)(kk * 8);                           // 8 columns per 16 K
             const uint64_t bk = (uint64_t)((kk >> 2) * bbox + 2 * (kk & 3));  // box, then 32 B steps
             umma_f16_ts(d, ahi + ac, bd + bk, id_hl, 1u);
             umma_f16_ts(d, alo + ac, bd + bk, id_h, 1u);
           }
           umma_commit(&done[ch % kDoneRing]);  // frees A slot ch % kASlots and B slot ch % BS
-          if (++as == (uint32_t)kASlots) { as = 0; a_ph ^= 1; }
-          if (++bs == (uint32_t)BS) { bs = 0; b_ph ^= 1; }
         }
-        if (!ok) { s_abort = 1; break; }
-        umma_commit(&acc_full[ab]);  // fires when every MMA of this unit has completed
-        ++acc_i;
+        __syncwarp();
+        if (++as == (uint32_t)kASlots) { as = 0; a_ph ^= 1; }
+        if (++bs == (uint32_t)BS) { bs = 0; b_ph ^= 1; }
       }
-      umma_commit(mma_done);  // fires once every MMA issued above has completed
-      mbar_wait(mma_done, 0, p.err);
+      if (!ok) { s_abort = 1; break; }
+      if (leader) umma_commit(&acc_full[ab]);  // fires when every MMA of this unit has completed
+      __syncwarp();
+      ++acc_i;
     }
+    if (leader) umma_commit(mma_done);  // fires once every MMA issued above has completed
+    __syncwarp();
+    mbar_wait(mma_done, 0, p.err);
   } else if (warp < 3 + kConvWarps) {
     // ---- converters: thread = weight row (its TMEM lane); per chunk, one 32-code scale group
     //      of each 64-K MMA group ----
@@ -337,7 +348,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
       bool ok = true;
       for (int i = 0; i < w.nch; ++i, ++ch) {
         const int sub = i % kChunksPerSuper;
-        if (sub == 0 && !__all_sync(0xffffffffu, mbar_wait(&nib_full[ns], ns_ph, p.err))) {
+        if (sub == 0 && !__all_sync(0xffffffffu, mbar_wait_poll(&nib_full[ns], ns_ph, p.err))) {
           ok = false;
           break;
         }
@@ -367,7 +378,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
         // The A slot last held chunk ch - kASlots; wait until its MMAs completed.
         if (ch >= (uint32_t)kASlots) {
           const uint32_t prev = ch - kASlots;
-          if (!__all_sync(0xffffffffu, mbar_wait(&done[prev % kDoneRing], (prev / kDoneRing) & 1, p.err))) {
+          if (!__all_sync(0xffffffffu, mbar_wait_poll(&done[prev % kDoneRing], (prev / kDoneRing) & 1, p.err))) {
             ok = false;
             break;
           }
