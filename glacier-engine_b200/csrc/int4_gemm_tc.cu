@@ -25,7 +25,7 @@
 //   warp 1      TMA producer: 64-K activation tiles [Xhi | Xlo] (SWIZZLE_128B)
 //   warp 2      allocates TMEM; runs the MMA loop converged, one elected lane
 //               issues every tcgen05.mma and commit
-//   warps 3-10  converters (two per 32-row TMEM lane quarter): nibbles + scales
+//   warps 3-10  converters (two per 32-row TMEM lane quarter, alternate chunks): nibbles + scales
 //               -> -Whi / Wlo fp16 pairs written straight into TMEM with
 //               tcgen05.st; the MMA reads A from TMEM (the descriptor's negate
 //               bit restores the sign of Whi), so shared memory carries only
@@ -206,7 +206,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     }
     for (int i = 0; i < BS; ++i) mbar_init(&b_full[i], 1);
     for (int i = 0; i < kDoneRing; ++i) mbar_init(&done[i], 1);
-    for (int i = 0; i < kASlots; ++i) mbar_init(&a_full[i], kConvWarps);
+    for (int i = 0; i < kASlots; ++i) mbar_init(&a_full[i], kConvWarps / 2);  // one warp per lane quarter
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], kEpiWarps);
@@ -335,69 +335,82 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     __syncwarp();
     mbar_wait(mma_done, 0, p.err);
   } else if (warp < 3 + kConvWarps) {
-    // ---- converters: thread = weight row (its TMEM lane); per chunk, one 32-code scale group
-    //      of each 64-K MMA group ----
+    // ---- converters: thread = weight row (its TMEM lane).  The two warps of a TMEM
+    //      lane quarter take alternate chunks of each unit (cw = 0 the even ones,
+    //      cw = 1 the odd ones), so one converts while the other waits on a
+    //      barrier; each converts all four 32-code scale groups of its chunk and
+    //      hands every group to TMEM (asynchronous tcgen05.st) as soon as it is done ----
     const int quarter = warp & 3;
-    const int hf = (warp - 3) >> 2;  // which 32-code half of each 64-code group
+    const int cw = (warp - 3) >> 2;
     const int rrow = quarter * 32 + lane;
     const uint32_t swz = (uint32_t)(rrow & 7);
-    const uint32_t tlane = tmem + ((uint32_t)(quarter * 32) << 16) + a_base + (uint32_t)(16 * hf);
+    const uint32_t tlane = tmem + ((uint32_t)(quarter * 32) << 16) + a_base;
     uint32_t ch = 0, ns = 0, ns_ph = 0;  // chunk counter; nibble slot and phase
     for (int u = blockIdx.x; u < p.units && !s_abort; u += gridDim.x) {
       const Unit w = unit_of(p, u);
       bool ok = true;
       for (int i = 0; i < w.nch; ++i, ++ch) {
         const int sub = i % kChunksPerSuper;
-        if (sub == 0 && !__all_sync(0xffffffffu, mbar_wait_poll(&nib_full[ns], ns_ph, p.err))) {
-          ok = false;
-          break;
-        }
-        const int as = ch % kASlots;
-        const uint8_t* nrow = nib + ns * (kNibBytes + kSclBytes) + rrow * 128;
-        const uint8_t* srow = nib + ns * (kNibBytes + kSclBytes) + kNibBytes + rrow * 16;
-        uint32_t hi[kSub][16], lo[kSub][16];
-#pragma unroll
-        for (int gsub = 0; gsub < kSub; ++gsub) {
-          const int grp = (sub * kSub + gsub) * 2 + hf;  // 32-code group within the 256-code super stage
-          const uint4 g = *reinterpret_cast<const uint4*>(nrow + (((uint32_t)grp ^ swz) << 4));
-          const uint32_t sh = *reinterpret_cast<const uint16_t*>(srow + 2 * grp);
-          const uint32_t s2 = sh * 0x10001u;      // {s, s}
-          const uint32_t ns2 = s2 ^ 0x80008000u;  // {-s, -s}
-          const uint32_t words[4] = {g.x, g.y, g.z, g.w};
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            uint32_t q[4];
-            unpack8(words[j], q);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              hi[gsub][4 * j + e] = hmul2_u32(q[e], ns2);                      // -RN(q*s)
-              lo[gsub][4 * j + e] = hfma2_u32(q[e], s2, hi[gsub][4 * j + e]);  // q*s - RN(q*s), exact
-            }
-          }
-        }
-        // The A slot last held chunk ch - kASlots; wait until its MMAs completed.
-        if (ch >= (uint32_t)kASlots) {
-          const uint32_t prev = ch - kASlots;
-          if (!__all_sync(0xffffffffu, mbar_wait_poll(&done[prev % kDoneRing], (prev / kDoneRing) & 1, p.err))) {
+        const bool stage_end = sub == kChunksPerSuper - 1 || i == w.nch - 1;
+        if (sub == cw) {
+          if (!__all_sync(0xffffffffu, mbar_wait_poll(&nib_full[ns], ns_ph, p.err))) {
             ok = false;
             break;
           }
-        }
-        tc_fence_after();
-        const uint32_t ta = tlane + (uint32_t)as * kAColsPerSlot;
+          const int as = ch % kASlots;
+          const uint8_t* nrow = nib + ns * (kNibBytes + kSclBytes) + rrow * 128;
+          const uint8_t* srow = nib + ns * (kNibBytes + kSclBytes) + kNibBytes + rrow * 16;
+          const uint32_t ta = tlane + (uint32_t)as * kAColsPerSlot;
 #pragma unroll
-        for (int gsub = 0; gsub < kSub; ++gsub) {
-          tmem_st16(ta + 32 * gsub, hi[gsub]);
-          tmem_st16(ta + kAColsPerSlot / 2 + 32 * gsub, lo[gsub]);
+          for (int gi = 0; gi < 2 * kSub; ++gi) {
+            const int grp = sub * 2 * kSub + gi;  // 32-code group within the 256-code super stage
+            const uint4 g = *reinterpret_cast<const uint4*>(nrow + (((uint32_t)grp ^ swz) << 4));
+            const uint32_t sh = *reinterpret_cast<const uint16_t*>(srow + 2 * grp);
+            const uint32_t s2 = sh * 0x10001u;      // {s, s}
+            const uint32_t ns2 = s2 ^ 0x80008000u;  // {-s, -s}
+            const uint32_t words[4] = {g.x, g.y, g.z, g.w};
+            uint32_t hi[16], lo[16];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              uint32_t q[4];
+              unpack8(words[j], q);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                hi[4 * j + e] = hmul2_u32(q[e], ns2);                // -RN(q*s)
+                lo[4 * j + e] = hfma2_u32(q[e], s2, hi[4 * j + e]);  // q*s - RN(q*s), exact
+              }
+            }
+            if (gi == 0) {
+              // The A slot last held chunk ch - kASlots; wait until its MMAs completed.
+              if (ch >= (uint32_t)kASlots) {
+                const uint32_t prev = ch - kASlots;
+                if (!__all_sync(0xffffffffu,
+                                mbar_wait_poll(&done[prev % kDoneRing], (prev / kDoneRing) & 1, p.err))) {
+                  ok = false;
+                  break;
+                }
+              }
+              tc_fence_after();
+            }
+            // Group (gsub, half) of the chunk: 16 columns at 32 * gsub + 16 * half.
+            const uint32_t col = (uint32_t)(32 * (gi >> 1) + 16 * (gi & 1));
+            tmem_st16(ta + col, hi);
+            tmem_st16(ta + kAColsPerSlot / 2 + col, lo);
+          }
+          if (!ok) break;
+          tmem_st_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(&a_full[as]);
+            mbar_arrive(&nib_empty[ns]);
+          }
+        } else if (stage_end && sub < cw) {
+          // The stage ended before this warp's chunk (odd chunk count): release its share.
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&nib_empty[ns]);
         }
-        tmem_st_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&a_full[as]);
-          if (sub == kChunksPerSuper - 1 || i == w.nch - 1) mbar_arrive(&nib_empty[ns]);
-        }
-        if (sub == kChunksPerSuper - 1 || i == w.nch - 1) {
+        if (stage_end) {
           if (++ns == (uint32_t)NS) { ns = 0; ns_ph ^= 1; }
         }
       }
