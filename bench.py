@@ -336,7 +336,7 @@ def run_glacier(args):
     # Per-kernel-class pass: the library records CUDA events on the step's stream
     # between its kernel classes for a few more steps of the same decode.
     dom = step_kernel_timing(torch, dm, sess, cfg, lanes, stream, args.profile_steps, device_step)
-    dom["kernels"].update(gemv_batch1_timing(torch, cfg, stream))
+    b1 = batch1_decode(torch, model, cfg, args, rank, stream)
 
     dev_ms, e2e_ms = max_over_ranks([dev_ms, e2e_s * 1e3], ws, dev)
     tokens_total = lanes * args.steps * (1 if tp > 1 else ws)
@@ -367,6 +367,7 @@ def run_glacier(args):
             "achieved_step_gbs": step_bytes / (dev_ms / args.steps / 1e3) / 1e9,
             "roofline": dom["roofline"],
             "kernels": dom["kernels"],
+            "batch1": b1,
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 2 * lanes * 4,
                     "d2h_bytes_per_step": lanes * 4},
@@ -466,32 +467,53 @@ def step_kernel_timing(torch, dm, sess, cfg, lanes, stream, steps, device_step) 
     return {"kernels": kernels, "roofline": roof}
 
 
-def gemv_batch1_timing(torch, cfg, stream) -> dict:
-    """The batch-1 INT4 GEMV (row (a)) on the fused gate+up matrix, timed in isolation with CUDA
-    events on rotating weight copies larger than L2."""
-    from glacier_b200 import ops
-    from glacier_b200.model import random_int4
-    rng = np.random.default_rng(5)
-    M, K = 2 * cfg.hidden, cfg.dim
-    packed, scales = random_int4(rng, M, K, 32)
-    copies = 4
-    Ws = [torch.from_numpy(packed).cuda() for _ in range(copies)]
-    Ss = [torch.from_numpy(scales.astype(np.float16)).cuda() for _ in range(copies)]
-    x = torch.randn(1, K, device="cuda")
-    y = torch.empty(1, M, device="cuda")
-    for i in range(3):
-        ops.linear_int4_on_the_fly(x, Ws[i % copies], Ss[i % copies], M, K, 32, out=y, stream=stream)
-    n = 12
-    e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+def batch1_decode(torch, model, cfg, args, rank, stream) -> dict:
+    """Batch-1 half of the metric: one lane of the same 7B model decoding alone, on a DeviceModel
+    reserved for one lane (GEMV path: 4 lanes or fewer never take the batched GEMM).  Context
+    drawn like config 5's lanes; KV rows random.  Timed on the device with CUDA events over
+    `steps` greedy steps; then one profiled pass gives the per-class kernel times at batch 1.
+    Algorithmic bytes per token: all INT4 weights with their fp16 scales (LM head included)
+    + the lane's K and V rows."""
+    from glacier_b200.model import DecodeSession, DeviceModel
+    ctx = int(lane_contexts(args, 1, rank)[0])
+    steps, warm = 20, 3
+    max_pages = -(-(ctx + steps + warm + args.profile_steps + 4) // 16)
+    dm = DeviceModel(model, max_positions=max_pages * 16)
+    sess = DecodeSession(dm, 1, max_pages)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(args.seed + 1000 + rank)
+    pages = sess.pages()
+    for i in range(0, pages.shape[0], 256):
+        pages[i:i + 256].normal_(generator=g)
+    sess.tokens.fill_(1)
+    sess.positions.fill_(ctx)
+
+    def step():
+        out = sess.step()
+        sess.tokens.copy_(out)
+        sess.positions.add_(1)
+
+    for _ in range(warm):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for i in range(n):
-        ops.linear_int4_on_the_fly(x, Ws[i % copies], Ss[i % copies], M, K, 32, out=y, stream=stream)
+    for _ in range(steps):
+        step()
     e1.record(stream)
     torch.cuda.synchronize()
-    t = e0.elapsed_time(e1) / n / 1e3
-    byt = M * K // 2 + M * K // 32 * 2 + K * 4 + M * 4
-    return {f"int4_gemv_{M}x{K}_b1_isolated": {"us_per_launch": t * 1e6, "algorithmic_bytes": byt,
-                                               "gbs": byt / t / 1e9}}
+    ms = e0.elapsed_time(e1) / steps
+    assert (sess.status.cpu().numpy() == 0).all()
+    kv = (ctx + warm + steps // 2) * cfg.num_layers * 2 * cfg.kv_dim * 4
+    byt = cfg.int4_bytes_per_token() + kv
+    hbm = float(load_peaks()["hbm_gbs"])
+    prof = step_kernel_timing(torch, dm, sess, cfg, 1, stream, args.profile_steps, step)
+    sess.close()
+    dm.close()
+    return {"tok_s": 1e3 / ms, "ms_per_token": ms, "ctx": ctx, "algorithmic_bytes_per_token": int(byt),
+            "achieved_gbs": byt / (ms * 1e-3) / 1e9, "frac_of_hbm_peak": byt / (ms * 1e-3) / 1e9 / hbm,
+            "timing": f"CUDA events over {steps} device steps after {warm} warm-up steps",
+            "kernels": prof["kernels"]}
 
 
 def run_prefill(args):

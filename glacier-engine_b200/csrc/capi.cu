@@ -115,7 +115,7 @@ int qkv_rope_append(const float* qkv, size_t ld, size_t split_stride, int nsplit
                     size_t page_floats, const int32_t* block_tables, size_t max_pages, size_t layer,
                     cudaStream_t stream);
 size_t attention_workspace_floats(size_t lanes, size_t num_heads, size_t head_dim, size_t nsplit);
-int attention_chunk(size_t lanes, size_t num_kv_heads, size_t max_ctx);
+int attention_chunk(size_t lanes, size_t num_heads, size_t num_kv_heads, size_t max_ctx);
 int paged_attention(const float* q, size_t ldq, const float* pool, size_t page_floats, const int32_t* block_tables,
                     size_t max_pages, const int32_t* ctx_lens, size_t max_ctx, size_t lanes, size_t layer,
                     size_t num_heads, size_t num_kv_heads, size_t head_dim, float* out, size_t ldo, float* workspace,
@@ -266,7 +266,7 @@ int glacier_cuda_qkv_rope_append_f32(const float* qkv, size_t ld, const float* b
 size_t glacier_cuda_paged_attention_workspace(size_t lanes, size_t num_heads, size_t num_kv_heads, size_t head_dim,
                                               size_t max_ctx) {
   if (!lanes || !num_kv_heads || !max_ctx) return 0;
-  const int chunk = attention_chunk(lanes, num_kv_heads, max_ctx);
+  const int chunk = attention_chunk(lanes, num_heads, num_kv_heads, max_ctx);
   return attention_workspace_floats(lanes, num_heads, head_dim, ceil_div(max_ctx, (size_t)chunk));
 }
 
@@ -276,13 +276,13 @@ int glacier_cuda_paged_attention_f32(const float* q, const float* kv_pages, size
                                      size_t head_dim, float* out, float* workspace, size_t workspace_floats,
                                      void* stream) {
   GLC_REQUIRE(lanes > 0 && num_kv_heads > 0, "paged_attention: empty batch");
-  // The kernel's work counters sit at the end of the workspace and must start at zero.
+  // The kernel's two work counters sit at the start of the workspace and must start at zero.
   const size_t need = glacier_cuda_paged_attention_workspace(lanes, num_heads, num_kv_heads, head_dim, max_ctx);
   GLC_REQUIRE(workspace && workspace_floats >= need, "paged_attention: workspace of %zu floats needed", need);
   GLC_CHECK_CUDA(cudaMemsetAsync(workspace, 0, 4 * sizeof(float), (cudaStream_t)stream));
   return paged_attention(q, num_heads * head_dim, kv_pages, page_floats, block_tables, max_pages, ctx_lens, max_ctx,
                          lanes, layer, num_heads, num_kv_heads, head_dim, out, num_heads * head_dim, workspace,
-                         workspace_floats, attention_chunk(lanes, num_kv_heads, max_ctx), (cudaStream_t)stream);
+                         workspace_floats, attention_chunk(lanes, num_heads, num_kv_heads, max_ctx), (cudaStream_t)stream);
 }
 
 size_t glacier_cuda_argmax_workspace(size_t batch, size_t n) { return argmax_workspace_bytes(batch, n); }

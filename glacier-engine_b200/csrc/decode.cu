@@ -43,7 +43,7 @@ int qkv_rope_append(const float* qkv, size_t ld, size_t split_stride, int nsplit
                     size_t page_floats, const int32_t* block_tables, size_t max_pages, size_t layer,
                     cudaStream_t stream);
 size_t attention_workspace_floats(size_t lanes, size_t num_heads, size_t head_dim, size_t nsplit);
-int attention_chunk(size_t lanes, size_t num_kv_heads, size_t max_ctx);
+int attention_chunk(size_t lanes, size_t num_heads, size_t num_kv_heads, size_t max_ctx);
 int paged_attention(const float* q, size_t ldq, const float* pool, size_t page_floats, const int32_t* block_tables,
                     size_t max_pages, const int32_t* ctx_lens, size_t max_ctx, size_t lanes, size_t layer,
                     size_t num_heads, size_t num_kv_heads, size_t head_dim, float* out, size_t ldo, float* workspace,
@@ -507,7 +507,7 @@ int glacier_cuda_model_reserve(glacier_cuda_model* m, size_t max_lanes, size_t m
   if (rc) return rc;
   const auto& c = m->cfg;
   const size_t L = max_lanes;
-  m->att_chunk = attention_chunk(L, c.num_kv_heads, max_pages * 16);
+  m->att_chunk = attention_chunk(L, c.num_heads, c.num_kv_heads, max_pages * 16);
   const size_t nsplit = ceil_div(max_pages * 16, (size_t)m->att_chunk);
   m->att_floats = attention_workspace_floats(L, c.num_heads, c.head_dim, nsplit);
   m->arg_bytes = argmax_workspace_bytes(L, c.vocab);

@@ -130,8 +130,10 @@ template <typename ScaleT>
 __global__ void __launch_bounds__(kThreads, 2) gemv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w,
                                                               const __grid_constant__ CUtensorMap tmap_s,
                                                               const GemvParams p) {
+  // Weights do not depend on the previous kernel: the producer streams them at
+  // once; the consumers wait for its writes (griddep_wait) before reading x, and
+  // every thread waits before the stores of y.
   griddep_launch();
-  griddep_wait();
   constexpr int kScaleBytes = kRows * 8 * (int)sizeof(ScaleT);  // 8 groups per row per stage
   constexpr int kStageBytes = kNibBytes + kScaleBytes;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -187,6 +189,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_tc_kernel(const __grid_const
     }
   } else {
     // ---------------- consumers ----------------
+    griddep_wait();
     // 1) B fragments (activation hi/lo columns) for this CTA's K-slice.
     const int nblk = nst * kBlocksPerStage;
     for (int idx = threadIdx.x; idx < nblk * flanes; idx += kWarps * 32) {
@@ -263,6 +266,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_tc_kernel(const __grid_const
   }
 
   // Cross-CTA K reduction through distributed shared memory, in rank order.
+  griddep_wait();
   cluster_sync_all();
   if (crank == 0) {
     for (int idx = threadIdx.x; idx < p.batch * kRows; idx += kThreads) {

@@ -352,26 +352,29 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
 }
 
 // out[lane, h, :] = sum_s o_s * e^(m_s - M) / sum_s l_s * e^(m_s - M), in chunk
-// order.  One CTA per lane: a warp per head computes the chunk weights once,
-// then each thread combines 8 consecutive values of one head from registers
-// and writes them as fp32 or, for the o-projection GEMM, in split form with the
-// lane's row max from one block reduction.
+// order.  One CTA per (lane, block of heads): a warp per head computes the chunk
+// weights once, then each thread combines 8 consecutive values of one head from
+// registers and writes them as fp32 or, for the o-projection GEMM, in split form
+// with the lane's row max from one block reduction (one block of all heads).
 __global__ void __launch_bounds__(1024) attn_combine_kernel(const float* __restrict__ part_o,
                                                             const float* __restrict__ part_ml, int nsplit,
                                                             int head_dim, int num_heads, float* __restrict__ out,
                                                             size_t ldo, SplitOut so,
-                                                            const int32_t* __restrict__ ctx_lens, int chunk) {
+                                                            const int32_t* __restrict__ ctx_lens, int chunk,
+                                                            int heads_per_block) {
   griddep_launch();
   griddep_wait();
   extern __shared__ float wts[];  // [num_heads][nsplit] chunk weights
   __shared__ float2 sh[32];
   __shared__ __align__(8) float2 xch;
   const int lane_id = blockIdx.x;
+  const int head0 = blockIdx.y * heads_per_block;
+  const int nh = min(heads_per_block, num_heads - head0);
   // Only the chunks that hold part of this lane's context have partials.
   const int nsplit_lane = min(nsplit, (ctx_lens[lane_id] + chunk - 1) / chunk);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
-  for (int t = warp; t < num_heads; t += nwarps) {
-    const size_t base = ((size_t)lane_id * num_heads + t) * nsplit;
+  for (int t = warp; t < nh; t += nwarps) {
+    const size_t base = ((size_t)lane_id * num_heads + head0 + t) * nsplit;
     if (nsplit_lane <= 32) {  // one chunk per lane of the warp: one load of (max, sum)
       const float2 ml = lane < nsplit_lane ? *reinterpret_cast<const float2*>(part_ml + (base + lane) * 2)
                                            : make_float2(-INFINITY, 0.f);
@@ -397,12 +400,12 @@ __global__ void __launch_bounds__(1024) attn_combine_kernel(const float* __restr
   }
   __syncthreads();
   const int e0 = 8 * threadIdx.x;
-  const bool active = e0 < num_heads * head_dim;
+  const bool active = e0 < nh * head_dim;
   float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   float mx = 0.f;
   if (active) {
     const int t = e0 / head_dim, d = e0 - t * head_dim;
-    const float* po = part_o + ((size_t)lane_id * num_heads + t) * nsplit * head_dim + d;
+    const float* po = part_o + ((size_t)lane_id * num_heads + head0 + t) * nsplit * head_dim + d;
     const float* wt = wts + t * nsplit;
 #pragma unroll 4
     for (int s = 0; s < nsplit_lane; ++s) {
@@ -421,7 +424,7 @@ __global__ void __launch_bounds__(1024) attn_combine_kernel(const float* __restr
     if (active) store_split8(so, lane_id, (size_t)num_heads * head_dim, (size_t)e0, acc, 1.0f / scale);
     if (threadIdx.x == 0) so.xscale[lane_id] = scale;
   } else if (active) {
-    float4* dst = reinterpret_cast<float4*>(out + lane_id * ldo + e0);
+    float4* dst = reinterpret_cast<float4*>(out + lane_id * ldo + (size_t)head0 * head_dim + e0);
     dst[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
     dst[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
   }
@@ -435,11 +438,17 @@ size_t attention_workspace_floats(size_t lanes, size_t num_heads, size_t head_di
 }
 
 // Positions per work item: 512 (32 pages) unless that leaves fewer than two
-// items per warp of the persistent grid, then halved down to 64.
-int attention_chunk(size_t lanes, size_t num_kv_heads, size_t max_ctx) {
+// items per warp of the persistent grid, then halved down to 32 (few lanes:
+// short items spread one context over many SMs).  The combine keeps one weight
+// per (head, chunk) in 48 KB of shared memory, which bounds the chunk count.
+int attention_chunk(size_t lanes, size_t num_heads, size_t num_kv_heads, size_t max_ctx) {
   const size_t warps = (size_t)sm_count() * kAttnWarps;
+  const size_t max_split = (48 * 1024) / (sizeof(float) * num_heads);
   size_t chunk = 512;
-  while (chunk > 64 && lanes * num_kv_heads * ceil_div(max_ctx, chunk) < 2 * warps) chunk /= 2;
+  while (ceil_div(max_ctx, chunk) > max_split) chunk *= 2;
+  while (chunk > 32 && lanes * num_kv_heads * ceil_div(max_ctx, chunk) < 2 * warps &&
+         ceil_div(max_ctx, chunk / 2) <= max_split)
+    chunk /= 2;
   return (int)chunk;
 }
 
@@ -497,7 +506,7 @@ int paged_attention(const float* q, size_t ldq, const float* pool, size_t page_f
               "paged_attention: group %zu / head_dim %zu outside the kernel contract", group, head_dim);
   GLC_REQUIRE(max_ctx > 0 && max_ctx <= max_pages * 16, "paged_attention: context %zu exceeds the block table",
               max_ctx);
-  if (chunk <= 0) chunk = attention_chunk(lanes, num_kv_heads, max_ctx);
+  if (chunk <= 0) chunk = attention_chunk(lanes, num_heads, num_kv_heads, max_ctx);
   GLC_REQUIRE(chunk % 16 == 0, "paged_attention: chunk must be whole pages");
   const int nsplit = (int)ceil_div(max_ctx, (size_t)chunk);
   GLC_REQUIRE(workspace_floats >= attention_workspace_floats(lanes, num_heads, head_dim, nsplit),
@@ -555,7 +564,9 @@ int paged_attention(const float* q, size_t ldq, const float* pool, size_t page_f
   int* err = device_symbol_address(g_attn_error);
   GLC_REQUIRE(err != nullptr, "paged_attention: device status word unavailable");
   const size_t items = lanes * num_kv_heads * (size_t)nsplit;
-  const int grid = (int)std::min<size_t>((size_t)sm_count(), ceil_div(items, (size_t)kAttnWarps));
+  // Up to one CTA per item: with few items (few lanes) their K/V streams still
+  // spread over as many SMs as there are items.
+  const int grid = (int)std::min<size_t>((size_t)sm_count(), items);
   // The two work counters at the start of the workspace start at zero (the
   // caller clears them once) and the kernel leaves them at zero.
   int* counter = reinterpret_cast<int*>(workspace);
@@ -568,12 +579,16 @@ int paged_attention(const float* q, size_t ldq, const float* pool, size_t page_f
                 "paged_attention: combine geometry %zu x %zu unsupported", num_heads, head_dim);
     const size_t csmem = num_heads * (size_t)nsplit * sizeof(float);
     GLC_REQUIRE(csmem <= 48 * 1024, "paged_attention: %d chunks per lane exceed the combine's shared memory", nsplit);
+    // The split output needs the lane's row max over all heads (one block per
+    // lane); fp32 output takes a block per (lane, head) when there are few lanes.
+    const size_t hpb = (so.xs || lanes * num_heads >= (size_t)sm_count()) ? num_heads : 1;
     // One warp per head for the weights (up to 32 warps), enough threads for 8 values each.
-    const size_t vals = ceil_div(num_heads * head_dim / 8, (size_t)32) * 32;
-    const unsigned threads = (unsigned)std::min<size_t>(1024, std::max(vals, num_heads * (size_t)32));
-    if ((rc = launch_pdl(attn_combine_kernel, dim3((unsigned)lanes), dim3(threads), csmem, stream, 1,
+    const size_t vals = ceil_div(hpb * head_dim / 8, (size_t)32) * 32;
+    const unsigned threads = (unsigned)std::min<size_t>(1024, std::max(vals, hpb * (size_t)32));
+    const dim3 cgrid((unsigned)lanes, (unsigned)ceil_div(num_heads, hpb));
+    if ((rc = launch_pdl(attn_combine_kernel, cgrid, dim3(threads), hpb * (size_t)nsplit * sizeof(float), stream, 1,
                          (const float*)prm.part_o, (const float*)prm.part_ml, nsplit, (int)head_dim, (int)num_heads,
-                         out, ldo, so, ctx_lens, chunk)))
+                         out, ldo, so, ctx_lens, chunk, (int)hpb)))
       return rc;
   }
   return GLACIER_CUDA_OK;
