@@ -67,6 +67,61 @@ __device__ __forceinline__ float block_max(float v, float* sh) {
   return sh[0];
 }
 
+// Few rows (GEMV decode): one CTA per row, each thread holding up to two float4
+// of it in registers, so one block reduction and no cluster exchange are
+// needed.  Same arithmetic as add_rmsnorm_kernel with fp32 output.
+__global__ void __launch_bounds__(1024) add_rmsnorm_row_kernel(
+    const float* __restrict__ a, size_t lda, const float* __restrict__ b, size_t ldb, size_t b_split_stride,
+    int nb, float* __restrict__ residual, size_t ldr, const float* __restrict__ w, float eps, float* __restrict__ out,
+    size_t ldo, int dim) {
+  griddep_launch();
+  griddep_wait();
+  __shared__ float sh[32];
+  const int r = blockIdx.x, n4 = dim / 4;
+  float4 v[2];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int i = threadIdx.x + j * blockDim.x;
+    v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (i < n4) {
+      float4 x = reinterpret_cast<const float4*>(a + r * lda)[i];
+      if (nb > 0) {
+        // addInto (generate.zig:3642): dst = a + b, split-K partials summed first.
+        float4 bv = reinterpret_cast<const float4*>(b + r * ldb)[i];
+        for (int sp = 1; sp < nb; ++sp) {
+          const float4 t = reinterpret_cast<const float4*>(b + sp * b_split_stride + r * ldb)[i];
+          bv.x += t.x;
+          bv.y += t.y;
+          bv.z += t.z;
+          bv.w += t.w;
+        }
+        x.x = x.x + bv.x;
+        x.y = x.y + bv.y;
+        x.z = x.z + bv.z;
+        x.w = x.w + bv.w;
+      }
+      v[j] = x;
+      ss = fmaf(x.x, x.x, ss);
+      ss = fmaf(x.y, x.y, ss);
+      ss = fmaf(x.z, x.z, ss);
+      ss = fmaf(x.w, x.w, ss);
+    }
+  }
+  ss = block_sum(ss, sh);
+  const float inv = 1.0f / sqrtf(ss / (float)dim + eps);
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int i = threadIdx.x + j * blockDim.x;
+    if (i < n4) {
+      if (residual) reinterpret_cast<float4*>(residual + r * ldr)[i] = v[j];
+      const float4 wv = reinterpret_cast<const float4*>(w)[i];
+      reinterpret_cast<float4*>(out + r * ldo)[i] =
+          make_float4(v[j].x * inv * wv.x, v[j].y * inv * wv.y, v[j].z * inv * wv.z, v[j].w * inv * wv.w);
+    }
+  }
+}
+
 // A cluster of CTAs per row (blockIdx.y = row, cluster rank = slice of the row):
 // x = a (+ the nb split-K partial rows of b, summed in split order); the sum
 // goes to `residual` when given; out = x * (1/sqrt(mean(x^2)+eps)) * w, written
@@ -472,6 +527,14 @@ int add_rmsnorm(const float* a, size_t lda, const float* b, size_t ldb, size_t b
     split8_shape(dim, &threads, &cl);
     return launch_pdl(add_rmsnorm_split8_kernel, dim3((unsigned)cl, (unsigned)batch), dim3(threads), 0, stream, cl,
                       a, lda, b, ldb, b_split_stride, nb, residual, ldr, w, eps, so, (int)dim);
+  }
+  const bool vec = dim % 4 == 0 && lda % 4 == 0 && (!b || (ldb % 4 == 0 && b_split_stride % 4 == 0)) &&
+                   (!residual || ldr % 4 == 0) && ldo % 4 == 0 && ((uintptr_t)a | (uintptr_t)b | (uintptr_t)w |
+                                                                 (uintptr_t)out | (uintptr_t)residual) % 16 == 0;
+  if (!so.xs && vec && batch <= 8 && dim <= 8 * 1024) {
+    const unsigned threads = (unsigned)std::min<size_t>(1024, ceil_div(ceil_div(dim / 4, (size_t)2), (size_t)32) * 32);
+    return launch_pdl(add_rmsnorm_row_kernel, dim3((unsigned)batch), dim3(threads), 0, stream, 1, a, lda, b, ldb,
+                      b_split_stride, nb, residual, ldr, w, eps, out, ldo, (int)dim);
   }
   const int cl = row_cluster(dim);
   const size_t slice = ((ceil_div(dim, (size_t)cl)) + 7) & ~(size_t)7;

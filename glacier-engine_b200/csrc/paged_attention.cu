@@ -430,6 +430,67 @@ __global__ void __launch_bounds__(1024) attn_combine_kernel(const float* __restr
   }
 }
 
+// fp32 output of one (lane, head) per CTA, for few lanes: warp 0 computes the
+// chunk weights, then the 8 warps take chunks s = warp, warp + 8, ... (each lane
+// 4 consecutive dims) and warp 0 adds the 8 partial sums in warp order.
+__global__ void __launch_bounds__(256) attn_combine_head_kernel(const float* __restrict__ part_o,
+                                                                const float* __restrict__ part_ml, int nsplit,
+                                                                int head_dim, int num_heads, float* __restrict__ out,
+                                                                size_t ldo, const int32_t* __restrict__ ctx_lens,
+                                                                int chunk) {
+  griddep_launch();
+  griddep_wait();
+  extern __shared__ float wts[];  // [nsplit]
+  __shared__ float4 part[8][32];
+  const int lane_id = blockIdx.x, head = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nsplit_lane = min(nsplit, (ctx_lens[lane_id] + chunk - 1) / chunk);
+  const size_t base = ((size_t)lane_id * num_heads + head) * nsplit;
+  if (warp == 0) {
+    float M = -INFINITY;
+    for (int s = lane; s < nsplit_lane; s += 32) M = fmaxf(M, part_ml[(base + s) * 2]);
+    M = warp_max(M);
+    float L = 0.f;
+    for (int s = lane; s < nsplit_lane; s += 32) {
+      const float m = part_ml[(base + s) * 2];
+      const float e = m == -INFINITY ? 0.f : expf(m - M);
+      wts[s] = e;
+      L += part_ml[(base + s) * 2 + 1] * e;
+    }
+    L = warp_sum(L);
+    const float inv = 1.0f / L;
+    for (int s = lane; s < nsplit_lane; s += 32) wts[s] *= inv;
+  }
+  __syncthreads();
+  const bool active = 4 * lane < head_dim;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (active) {
+    const float* po = part_o + base * head_dim + 4 * lane;
+    for (int s = warp; s < nsplit_lane; s += 8) {
+      const float4 v = *reinterpret_cast<const float4*>(po + (size_t)s * head_dim);
+      const float w = wts[s];
+      acc.x = fmaf(v.x, w, acc.x);
+      acc.y = fmaf(v.y, w, acc.y);
+      acc.z = fmaf(v.z, w, acc.z);
+      acc.w = fmaf(v.w, w, acc.w);
+    }
+  }
+  part[warp][lane] = acc;
+  __syncthreads();
+  if (warp == 0 && active) {
+    float4 t = part[0][lane];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) {
+      const float4 q = part[w][lane];
+      t.x += q.x;
+      t.y += q.y;
+      t.z += q.z;
+      t.w += q.w;
+    }
+    *reinterpret_cast<float4*>(out + lane_id * ldo + (size_t)head * head_dim + 4 * lane) = t;
+  }
+}
+
 }  // namespace
 
 // Workspace floats needed by paged_attention for the given split count.
@@ -580,8 +641,14 @@ int paged_attention(const float* q, size_t ldq, const float* pool, size_t page_f
     const size_t csmem = num_heads * (size_t)nsplit * sizeof(float);
     GLC_REQUIRE(csmem <= 48 * 1024, "paged_attention: %d chunks per lane exceed the combine's shared memory", nsplit);
     // The split output needs the lane's row max over all heads (one block per
-    // lane); fp32 output takes a block per (lane, head) when there are few lanes.
-    const size_t hpb = (so.xs || lanes * num_heads >= (size_t)sm_count()) ? num_heads : 1;
+    // lane); fp32 output with few lanes takes a block per (lane, head).
+    if (!so.xs && lanes * num_heads < (size_t)sm_count()) {
+      GLC_REQUIRE(head_dim <= 128 && head_dim % 4 == 0 && ldo % 4 == 0, "paged_attention: head_dim %zu", head_dim);
+      return launch_pdl(attn_combine_head_kernel, dim3((unsigned)lanes, (unsigned)num_heads), dim3(256),
+                        (size_t)nsplit * sizeof(float), stream, 1, (const float*)prm.part_o,
+                        (const float*)prm.part_ml, nsplit, (int)head_dim, (int)num_heads, out, ldo, ctx_lens, chunk);
+    }
+    const size_t hpb = num_heads;
     // One warp per head for the weights (up to 32 warps), enough threads for 8 values each.
     const size_t vals = ceil_div(hpb * head_dim / 8, (size_t)32) * 32;
     const unsigned threads = (unsigned)std::min<size_t>(1024, std::max(vals, hpb * (size_t)32));
