@@ -235,7 +235,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_tc_kernel(const __grid_const
         sc[t][1].load(sstg + (rho + 8) * 8 * sizeof(ScaleT));
       }
       const uint8_t* rowbase = stg + (16 * kTilesPerWarp * warp + r) * 128 + 4 * c;
-#pragma unroll 2
+#pragma unroll
       for (int bl = 0; bl < kBlocksPerStage; ++bl) {
         const uint32_t off = ((uint32_t)bl ^ swz) << 4;
         uint4 bf = make_uint4(0, 0, 0, 0);
