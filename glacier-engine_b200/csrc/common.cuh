@@ -140,6 +140,12 @@ int int4_weight_prepare(Int4Weight& w);
 int int4_linear(const Int4Weight& w, const float* x, size_t ldx, size_t batch, const float* bias, float* y,
                 size_t ldy, cudaStream_t stream);
 
+// y[b, :] = (silu(gate[b, :]) * up[b, :]) * dequant(W)^T + bias on the tensor-core
+// GEMV with the SwiGLU folded into its activation loads (gate and up share the
+// row stride ld); GLACIER_CUDA_EUNSUPPORTED when that kernel does not apply.
+int int4_linear_swiglu(const Int4Weight& w, const float* gate, const float* up, size_t ld, size_t batch,
+                       const float* bias, float* y, size_t ldy, cudaStream_t stream);
+
 // Destination of an activation block that feeds the tensor-core GEMM: rows of
 // fp16 hi / lo parts ([2*np, K]: hi rows 0..np-1, lo rows np..2np-1) in the
 // per-8 code order (0,4,1,5,2,6,3,7), plus one power-of-two scale per row

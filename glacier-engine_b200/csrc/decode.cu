@@ -660,12 +660,24 @@ static int step_impl(glacier_cuda_model* m, glacier_cuda_kv* kv, size_t lanes, c
       return rc;
     mark(GLACIER_CUDA_STEP_PROJ_GATE_UP);
     if ((rc = project(L.gu.w, hn, D, so_d, m->map_d, m->gu.as<float>(), 2 * F, 1))) return rc;
-    mark(GLACIER_CUDA_STEP_SILU);
-    if ((rc = silu_mul(m->gu.as<float>(), m->gu.as<float>() + F, 2 * F, m->gemm ? nullptr : m->act.as<float>(), F, B,
-                       F, st, so_f)))
-      return rc;
-    mark(GLACIER_CUDA_STEP_PROJ_DOWN);
-    if ((rc = project(L.d.w, m->act.as<float>(), F, so_f, m->map_f, m->down.as<float>(), D, sd_gemm))) return rc;
+    // GEMV mode: the down projection's activation loads compute silu(gate) * up
+    // themselves (no SiLU launch); otherwise the SiLU kernel writes the split
+    // (GEMM) or fp32 activations first.
+    rc = m->gemm ? GLACIER_CUDA_EUNSUPPORTED : GLACIER_CUDA_OK;
+    if (!m->gemm) {
+      mark(GLACIER_CUDA_STEP_PROJ_DOWN);
+      rc = int4_linear_swiglu(L.d.w, m->gu.as<float>(), m->gu.as<float>() + F, 2 * F, B, nullptr,
+                              m->down.as<float>(), D, st);
+      if (rc && rc != GLACIER_CUDA_EUNSUPPORTED) return rc;
+    }
+    if (rc == GLACIER_CUDA_EUNSUPPORTED) {
+      mark(GLACIER_CUDA_STEP_SILU);
+      if ((rc = silu_mul(m->gu.as<float>(), m->gu.as<float>() + F, 2 * F, m->gemm ? nullptr : m->act.as<float>(), F,
+                         B, F, st, so_f)))
+        return rc;
+      mark(GLACIER_CUDA_STEP_PROJ_DOWN);
+      if ((rc = project(L.d.w, m->act.as<float>(), F, so_f, m->map_f, m->down.as<float>(), D, sd_gemm))) return rc;
+    }
     // Tensor parallel: down summed over the ranks' FFN slices.
     if (m->tp_comm && (rc = tp_reduce(m->down.as<float>(), sd_gemm))) return rc;
   }

@@ -261,7 +261,23 @@ bool gemv_fast_layout(size_t K, size_t group) {
 }
 
 int gemv_int4_tc(const Int4Weight& w, const float* x, size_t ldx, size_t batch, const float* bias, float* y,
-                 size_t ldy, cudaStream_t stream);
+                 size_t ldy, cudaStream_t stream, const float* xu = nullptr);
+
+// y = W (silu(gate) * up) on the tensor-core GEMV, the SwiGLU folded into the
+// activation loads; GLACIER_CUDA_EUNSUPPORTED when the weight or operands do not
+// fit that kernel (the caller then runs silu_mul and int4_linear).
+int int4_linear_swiglu(const Int4Weight& w, const float* gate, const float* up, size_t ld, size_t batch,
+                       const float* bias, float* y, size_t ldy, cudaStream_t stream) {
+  GLC_REQUIRE(gate && up && y && batch > 0, "int4 linear swiglu: empty or null argument");
+  const bool aligned = ((uintptr_t)gate % 16 == 0) && ((uintptr_t)up % 16 == 0) && (ld % 4 == 0);
+  if (!w.tc || !aligned) return GLACIER_CUDA_EUNSUPPORTED;
+  for (size_t b = 0; b < batch; b += 4) {
+    const size_t nb = batch - b < 4 ? batch - b : 4;
+    const int rc = gemv_int4_tc(w, gate + b * ld, ld, nb, bias, y + b * ldy, ldy, stream, up + b * ld);
+    if (rc) return rc;
+  }
+  return GLACIER_CUDA_OK;
+}
 
 int int4_linear(const Int4Weight& w, const float* x, size_t ldx, size_t batch, const float* bias, float* y,
                 size_t ldy, cudaStream_t stream) {

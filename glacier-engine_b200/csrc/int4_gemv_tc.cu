@@ -50,6 +50,7 @@ struct GemvParams {
   int stages_total;    // ceil(K / 256)
   int stages_per_cta;  // K-slice length in stages
   int* err;
+  const float* xu;     // SwiGLU input: x = silu(x) * xu elementwise (same leading dimension), or null
 };
 
 __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
@@ -202,6 +203,14 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_tc_kernel(const __grid_const
         const float4* xp = reinterpret_cast<const float4*>(p.x + b * p.ldx + k0);
         const float4 a = __ldg(xp), bq = __ldg(xp + 1);
         v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = bq.x; v[5] = bq.y; v[6] = bq.z; v[7] = bq.w;
+        if (p.xu) {
+          // SwiGLU (kernels.zig:465): silu(gate) * up, the same expression as silu_mul_kernel.
+          const float4* up = reinterpret_cast<const float4*>(p.xu + b * p.ldx + k0);
+          const float4 ua = __ldg(up), ub = __ldg(up + 1);
+          const float u[8] = {ua.x, ua.y, ua.z, ua.w, ub.x, ub.y, ub.z, ub.w};
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[j] = v[j] * (1.0f / (1.0f + expf(-v[j]))) * u[j];
+        }
       }
       __half h[8];
 #pragma unroll
@@ -284,8 +293,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_tc_kernel(const __grid_const
 }
 
 template <typename ScaleT>
-int launch_gemv_tc(const Int4Weight& w, const float* x, size_t ldx, size_t batch, const float* bias, float* y,
-                   size_t ldy, cudaStream_t stream) {
+int launch_gemv_tc(const Int4Weight& w, const float* x, const float* xu, size_t ldx, size_t batch, const float* bias,
+                   float* y, size_t ldy, cudaStream_t stream) {
   const size_t M = w.M, K = w.K;
   int rc = 0;
   const int tiles = (int)ceil_div(M, kRows);
@@ -313,7 +322,7 @@ int launch_gemv_tc(const Int4Weight& w, const float* x, size_t ldx, size_t batch
   }
   int* err = nullptr;
   GLC_CHECK_CUDA(cudaGetSymbolAddress((void**)&err, g_gemv_error));
-  GemvParams prm{x, ldx, bias, y, ldy, (int)M, (int)K, (int)batch, stages, spc, err};
+  GemvParams prm{x, ldx, bias, y, ldy, (int)M, (int)K, (int)batch, stages, spc, err, xu};
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(tiles * cs);
   cfg.blockDim = dim3(kThreads);
@@ -355,9 +364,9 @@ int int4_weight_prepare(Int4Weight& w) {
 }
 
 int gemv_int4_tc(const Int4Weight& w, const float* x, size_t ldx, size_t batch, const float* bias, float* y,
-                 size_t ldy, cudaStream_t stream) {
-  return w.f16 ? launch_gemv_tc<__half>(w, x, ldx, batch, bias, y, ldy, stream)
-               : launch_gemv_tc<float>(w, x, ldx, batch, bias, y, ldy, stream);
+                 size_t ldy, cudaStream_t stream, const float* xu) {
+  return w.f16 ? launch_gemv_tc<__half>(w, x, xu, ldx, batch, bias, y, ldy, stream)
+               : launch_gemv_tc<float>(w, x, xu, ldx, batch, bias, y, ldy, stream);
 }
 
 int gemv_device_error(int clear) {

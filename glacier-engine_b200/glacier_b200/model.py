@@ -271,6 +271,25 @@ class DecodeSession:
                   self.status.data_ptr(), None if logits is None else logits.data_ptr(), s.cuda_stream)
         return self.out
 
+    def capture_greedy_step(self, stream=None):
+        """Records one greedy continuation step as a CUDA graph: decode_step on self.tokens and
+        self.positions, then tokens <- the new token ids and positions += 1.  replay_greedy_step()
+        runs it again; all of its inputs live in device memory, so a replay is the same step as a
+        fresh launch sequence, minus the host launch work and inter-launch gaps."""
+        torch = self.torch
+        s = stream if stream is not None else torch.cuda.current_stream()
+        self._graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self._graph, stream=s):
+            out = self.step(stream=s)
+            self.tokens.copy_(out)
+            self.positions.add_(1)
+        return self._graph
+
+    def replay_greedy_step(self):
+        """One replay of the graph recorded by capture_greedy_step (on its capture stream)."""
+        self._graph.replay()
+        return self.out
+
     def prefill(self, prompt, lane: int = 0, start: int = 0, eligible=None, logits=None, stream=None):
         """Feeds prompt tokens (host sequence or device int32 tensor) of one request at positions
         start.. through lane `lane`'s block table; returns the device int32 tensor [1] holding
@@ -290,6 +309,7 @@ class DecodeSession:
         return out
 
     def close(self):
+        self._graph = None  # a recorded step references this session's buffers
         if getattr(self, "kv", None):
             _lib.lib().glacier_cuda_kv_destroy(self.kv)
             self.kv = None
