@@ -23,6 +23,8 @@
 //  * Every mbarrier wait is bounded; on timeout the kernel raises a device
 //    error word, drains its own TMA copies and leaves through the cluster
 //    barriers so no CTA is left waiting.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace glacier {
@@ -299,15 +301,18 @@ int launch_gemv_tc(const Int4Weight& w, const float* x, const float* xu, size_t 
   int rc = 0;
   const int tiles = (int)ceil_div(M, kRows);
   const int stages = (int)ceil_div(K, 256);
-  // Cluster size: enough CTAs for two per SM, K-slices short enough that the
-  // B fragments leave room for two CTAs per SM; at most 8 CTAs per cluster.
-  int cs = 1;
+  // Cluster size (the K split): as many CTAs per row tile as keep the grid within
+  // one wave of two CTAs per SM (at most 8 per cluster: 10-CTA non-portable
+  // clusters measured slower), then as few as give every CTA the same number of
+  // stages; K-slices short enough that the B fragments leave room for two CTAs
+  // per SM.
   auto frag_bytes = [&](int c) { return (size_t)ceil_div(stages, c) * kBlocksPerStage * 8 * batch * 16; };
-  while (cs < 8 && cs * 2 <= stages &&
-         ((int)ceil_div(stages, cs) > kMaxStagesPerCta || frag_bytes(cs) > 24 * 1024 ||
-          tiles * cs < 2 * sm_count()))
-    cs *= 2;
+  int cs = std::max(1, std::min({8, stages, 2 * sm_count() / tiles}));
+  while (cs < std::min(8, stages) &&
+         ((int)ceil_div(stages, cs) > kMaxStagesPerCta || frag_bytes(cs) > 24 * 1024))
+    ++cs;
   const int spc = (int)ceil_div(stages, cs);
+  cs = (int)ceil_div(stages, spc);
   const size_t stage_bytes = kNibBytes + (size_t)kRows * 8 * sizeof(ScaleT);
   const size_t smem = 1024 + (size_t)kStages * stage_bytes + (size_t)spc * kBlocksPerStage * 8 * batch * 16 +
                       4 * kRows * sizeof(float) + 2 * kStages * sizeof(uint64_t);
