@@ -338,6 +338,98 @@ GOR_EXPORT int gor_linear_int4_f32_mt(const float *x, size_t batch, const uint8_
 }
 
 /* ------------------------------------------------------------------------ */
+/* int4_matmul.zig: Q8 activations (the reference's default decode numerics) */
+/* ------------------------------------------------------------------------ */
+
+/* Activation block of the Q8 path: 32 for group 8, else the weight group
+ * (int4_matmul.zig:361, :535-538 q8ActivationScaleCount). */
+GOR_EXPORT size_t gor_q8_activation_group(size_t group) { return group == 8 ? 32 : group; }
+
+/* One row of the Q8 activation quantizer of linearInt4Q8OnTheFly
+ * (int4_matmul.zig:365-394): per activation block, scale = max|x| / 127 and
+ * q = clamp(round(x * (1/scale)), -127, 127), rounding half away from zero
+ * (Zig @round); an all-zero block has scale 0 and q = 0. */
+GOR_EXPORT void gor_q8_quantize_row(const float *x, size_t in_f, size_t group, int8_t *q, float *a_scales)
+{
+    const size_t ag = gor_q8_activation_group(group);
+    const size_t ngroups = ceil_div(in_f, ag);
+    for (size_t g = 0; g < ngroups; ++g) {
+        const size_t start = g * ag, end = start + ag < in_f ? start + ag : in_f;
+        float max_abs = 0.0f;
+        for (size_t i = start; i < end; ++i) max_abs = fmaxf(max_abs, fabsf(x[i]));
+        const float scale = max_abs / 127.0f;
+        a_scales[g] = scale;
+        if (scale == 0.0f) {
+            memset(q + start, 0, end - start);
+            continue;
+        }
+        const float inv = 1.0f / scale;
+        for (size_t i = start; i < end; ++i) {
+            long qi = (long)roundf(x[i] * inv);
+            if (qi < -127) qi = -127;
+            if (qi > 127) qi = 127;
+            q[i] = (int8_t)qi;
+        }
+    }
+}
+
+/* int4_matmul.zig:335-418 linearInt4Q8OnTheFly.  Each batch row is quantized
+ * independently; per output row acc starts at the bias and adds, group by
+ * group in order, (float)(sum (u - 7) * q) * w_scale * a_scale.  Inputs longer
+ * than 16384 or with more than 2048 activation blocks take the FP32 path
+ * (:369-371).  Returns 0, or -1 on a shape error. */
+GOR_EXPORT int gor_linear_int4_q8(const float *x, size_t batch, const uint8_t *packed, const float *scales,
+                                  const float *bias, float *out, size_t out_f, size_t in_f, size_t group)
+{
+    if (group == 0 || in_f % group != 0) return -1;
+    const size_t ag = gor_q8_activation_group(group);
+    if (in_f > 16384 || ceil_div(in_f, ag) > 2048)
+        return gor_linear_int4_f32(x, batch, packed, scales, bias, out, out_f, in_f, group);
+    int8_t *q = (int8_t *)malloc(in_f);
+    float *as = (float *)malloc(ceil_div(in_f, ag) * sizeof(float));
+    if (!q || !as) {
+        free(q);
+        free(as);
+        return -1;
+    }
+    const size_t groups = in_f / group;
+    for (size_t b = 0; b < batch; ++b) {
+        gor_q8_quantize_row(x + b * in_f, in_f, group, q, as);
+        for (size_t row = 0; row < out_f; ++row) {
+            float acc = bias ? bias[row] : 0.0f;
+            const size_t row_start = row * in_f;
+            for (size_t og = 0; og < groups; ++og) {
+                const size_t start = og * group, end = start + group;
+                int32_t dot = 0;
+                for (size_t col = start; col < end; ++col) {
+                    const size_t idx = row_start + col;
+                    const uint8_t byte = packed[idx / 2];
+                    const int32_t nib = (idx & 1) == 0 ? (byte & 0x0F) : (byte >> 4);
+                    dot += (nib - 7) * (int32_t)q[col];
+                }
+                float t = (float)dot * scales[(row_start + start) / group];
+                t = t * as[start / ag];
+                acc = acc + t;
+            }
+            out[b * out_f + row] = acc;
+        }
+    }
+    free(q);
+    free(as);
+    return 0;
+}
+
+/* int4_matmul.zig:422-532 linearInt4WeightQ8 as it dispatches on a non-AArch64
+ * host: an LM-head-sized output (out_f > 65536) takes the FP32 path
+ * (linearInt4Weight, :460-462), everything else linearInt4Q8OnTheFly. */
+GOR_EXPORT int gor_linear_int4_weight_q8(const float *x, size_t batch, const uint8_t *packed, const float *scales,
+                                         const float *bias, float *out, size_t out_f, size_t in_f, size_t group)
+{
+    if (out_f > 65536) return gor_linear_int4_f32(x, batch, packed, scales, bias, out, out_f, in_f, group);
+    return gor_linear_int4_q8(x, batch, packed, scales, bias, out, out_f, in_f, group);
+}
+
+/* ------------------------------------------------------------------------ */
 /* kernels.zig: RMSNorm, fused residual RMSNorm, SwiGLU                      */
 /* ------------------------------------------------------------------------ */
 

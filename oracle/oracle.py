@@ -42,6 +42,12 @@ def lib():
                                      C.POINTER(C.c_int), vp]
         L.gor_linear_int4_f32.argtypes = [vp, sz, vp, vp, vp, vp, sz, sz, sz]
         L.gor_linear_int4_f32_mt.argtypes = [vp, sz, vp, vp, vp, vp, sz, sz, sz, sz]
+        L.gor_q8_activation_group.argtypes = [sz]
+        L.gor_q8_activation_group.restype = sz
+        L.gor_q8_quantize_row.argtypes = [vp, sz, sz, vp, vp]
+        L.gor_q8_quantize_row.restype = None
+        L.gor_linear_int4_q8.argtypes = [vp, sz, vp, vp, vp, vp, sz, sz, sz]
+        L.gor_linear_int4_weight_q8.argtypes = [vp, sz, vp, vp, vp, vp, sz, sz, sz]
         L.gor_rmsnorm_f32.argtypes = [vp, sz, sz, vp, C.c_float, vp]
         L.gor_rmsnorm_f32.restype = None
         L.gor_add_rmsnorm_f32.argtypes = [vp, vp, vp, sz, sz, vp, C.c_float, vp]
@@ -143,6 +149,30 @@ def linear_int4(x, packed, scales, out_f: int, in_f: int, group: int, bias=None,
         rc = lib().gor_linear_int4_f32(_p(x), x.shape[0], _p(packed), _p(scales), _p(bias),
                                        _p(out), out_f, in_f, group)
     if rc:
+        raise ValueError("ShapeMismatch")
+    return out
+
+
+def q8_quantize(x, group: int):
+    """int4_matmul.zig:365-394: one row's Q8 activation codes and per-block scales."""
+    x = _f32(x).reshape(-1)
+    ag = lib().gor_q8_activation_group(group)
+    q = np.zeros(x.size, np.int8)
+    scales = np.zeros(-(-x.size // ag), np.float32)
+    lib().gor_q8_quantize_row(_p(x), x.size, group, _p(q), _p(scales))
+    return q, scales
+
+
+def linear_int4_q8(x, packed, scales, out_f: int, in_f: int, group: int, bias=None, weight_dispatch: bool = False):
+    """int4_matmul.zig:335 linearInt4Q8OnTheFly (weight_dispatch: :422 linearInt4WeightQ8 on a
+    non-AArch64 host, which sends out_f > 65536 to the FP32 path)."""
+    x = _f32(x).reshape(-1, in_f)
+    packed = np.ascontiguousarray(packed, np.uint8)
+    scales = _f32(scales)
+    bias = None if bias is None else _f32(bias)
+    out = np.zeros((x.shape[0], out_f), np.float32)
+    fn = lib().gor_linear_int4_weight_q8 if weight_dispatch else lib().gor_linear_int4_q8
+    if fn(_p(x), x.shape[0], _p(packed), _p(scales), _p(bias), _p(out), out_f, in_f, group):
         raise ValueError("ShapeMismatch")
     return out
 
