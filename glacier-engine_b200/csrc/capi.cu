@@ -101,6 +101,7 @@ int gemv_int4(const float* x, size_t ldx, size_t batch, const uint8_t* packed, c
               size_t group, cudaStream_t stream);
 
 int gemv_device_error(int clear);
+int q8_device_error(int clear);
 int ops_device_error(int clear);
 int add_rmsnorm(const float* a, size_t lda, const float* b, size_t ldb, size_t b_split_stride, int nb,
                 float* residual, size_t ldr, const float* w, float eps, float* out, size_t ldo, size_t batch,
@@ -153,9 +154,9 @@ unsigned long long glacier_cuda_launch_count(void) { return g_launches.load(std:
 int glacier_cuda_device_status(int clear) {
   GLC_CHECK_CUDA(cudaDeviceSynchronize());
   const int v = gemv_device_error(clear), w = ops_device_error(clear), g = gemm_device_error(clear),
-            a = attn_device_error(clear);
-  if (v < 0 || w < 0 || g < 0 || a < 0) return set_error(GLACIER_CUDA_ECUDA, "device status read failed");
-  return (v || g || a) ? 1 : (w ? 2 : 0);
+            a = attn_device_error(clear), q = q8_device_error(clear);
+  if (v < 0 || w < 0 || g < 0 || a < 0 || q < 0) return set_error(GLACIER_CUDA_ECUDA, "device status read failed");
+  return (v || g || a || q) ? 1 : (w ? 2 : 0);
 }
 
 int glacier_cuda_int4_matvec_f32(const float* x, const uint8_t* packed, const float* scales,
@@ -183,6 +184,22 @@ int glacier_cuda_int4_linear(const float* x, size_t batch, const uint8_t* packed
                              out_features, out_features, in_features, group_size, (cudaStream_t)stream);
   return gemv_int4<float>(x, in_features, batch, packed, static_cast<const float*>(scales), 0, bias, y,
                           out_features, out_features, in_features, group_size, (cudaStream_t)stream);
+}
+
+int glacier_cuda_int4_linear_q8(const float* x, size_t batch, const uint8_t* packed, const void* scales,
+                                int scale_is_f16, const float* bias, float* y, size_t out_features,
+                                size_t in_features, size_t group_size, void* stream) {
+  GLC_REQUIRE(x && packed && scales && y, "int4_linear_q8: null pointer");
+  Int4Weight w;
+  w.packed = packed;
+  w.scales = scales;
+  w.f16 = scale_is_f16 != 0;
+  w.M = out_features;
+  w.K = in_features;
+  w.group = group_size;
+  const int rc = int4_weight_prepare(w);
+  if (rc) return rc;
+  return int4_linear_q8(w, x, in_features, batch, bias, y, out_features, (cudaStream_t)stream);
 }
 
 static size_t matmul_ws_bytes(size_t batch, size_t in_features, size_t out_features) {

@@ -140,6 +140,11 @@ int int4_weight_prepare(Int4Weight& w);
 int int4_linear(const Int4Weight& w, const float* x, size_t ldx, size_t batch, const float* bias, float* y,
                 size_t ldy, cudaStream_t stream);
 
+// The Q8-activation form (linearInt4WeightQ8 on a non-AArch64 host): bit-identical
+// to the reference's portable path; LM-head-sized outputs and long inputs run int4_linear.
+int int4_linear_q8(const Int4Weight& w, const float* x, size_t ldx, size_t batch, const float* bias, float* y,
+                   size_t ldy, cudaStream_t stream);
+
 // y[b, :] = (silu(gate[b, :]) * up[b, :]) * dequant(W)^T + bias on the tensor-core
 // GEMV with the SwiGLU folded into its activation loads (gate and up share the
 // row stride ld); GLACIER_CUDA_EUNSUPPORTED when that kernel does not apply.

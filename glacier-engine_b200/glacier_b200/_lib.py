@@ -40,6 +40,7 @@ SIGNATURES = {
     "glacier_cuda_int4_matvec_f32": ([vp, vp, vp, vp, vp, sz, sz, sz, vp], i32),
     "glacier_cuda_int4_matvec_f16scale": ([vp, vp, vp, vp, vp, sz, sz, sz, vp], i32),
     "glacier_cuda_int4_linear": ([vp, sz, vp, vp, i32, vp, vp, sz, sz, sz, vp], i32),
+    "glacier_cuda_int4_linear_q8": ([vp, sz, vp, vp, i32, vp, vp, sz, sz, sz, vp], i32),
     "glacier_cuda_int4_matmul_workspace": ([sz, sz, sz], sz),
     "glacier_cuda_int4_matmul_f16scale": ([vp, sz, vp, vp, vp, vp, sz, sz, sz, vp, sz, vp], i32),
     "glacier_cuda_rmsnorm_f32": ([vp, vp, f32, vp, sz, sz, vp], i32),

@@ -92,6 +92,20 @@ int glacier_cuda_int4_linear(const float *x, size_t batch, const uint8_t *packed
                              size_t out_features, size_t in_features, size_t group_size,
                              void *stream);
 
+/* Q8-activation form, the reference's default decode numerics: linearInt4WeightQ8
+ * (src/backends/cpu/int4_matmul.zig:422-532) as it dispatches on a non-AArch64 host, i.e.
+ * linearInt4Q8OnTheFly (:335-418).  Each x row is quantized per activation block (32 codes
+ * for group 8, else group): scale = max|x| / 127, q = clamp(round(x / scale), -127, 127);
+ * then acc = bias and, weight group by weight group,
+ * acc += (float)(sum (u - 7) * q) * w_scale * a_scale.  Bit-identical to that portable
+ * path.  Outputs longer than 65536 and inputs longer than 16384 (or with more than 2048
+ * activation blocks) take the FP32-activation path, as in the reference.  Same arguments
+ * as glacier_cuda_int4_linear. */
+int glacier_cuda_int4_linear_q8(const float *x, size_t batch, const uint8_t *packed,
+                                const void *scales, int scale_is_f16, const float *bias, float *y,
+                                size_t out_features, size_t in_features, size_t group_size,
+                                void *stream);
+
 /* (b) Batched form on the tensor cores (tcgen05/TMEM dequant GEMM): x [batch, in_f] fp32,
  * y [batch, out_f]; the reference's M4 weight-stationary GEMM
  * (glacier_int4_gemm_neon_q8_prequant_f16scale_rows4_k16_m4, src/decode_lane4.zig:221-264,

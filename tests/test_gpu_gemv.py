@@ -83,3 +83,61 @@ def test_gemv_rejects_zero_group_without_writing():
 def test_device_status_clean_after_gemv():
     from glacier_b200 import _lib
     assert _lib.lib().glacier_cuda_device_status(1) == 0
+
+
+# ---------------------------------------------------------------------------
+# Q8-activation form (linearInt4WeightQ8 / linearInt4Q8OnTheFly): bit-identical
+# ---------------------------------------------------------------------------
+
+def _run_q8(x, packed, scales, out_f, in_f, group, bias=None):
+    from glacier_b200 import _lib
+    xd, pd, sd = _dev(x), _dev(packed), _dev(scales)
+    bd = None if bias is None else _dev(bias)
+    y = torch.empty((x.shape[0], out_f), dtype=torch.float32, device="cuda")
+    _lib.call("glacier_cuda_int4_linear_q8", xd.data_ptr(), x.shape[0], pd.data_ptr(), sd.data_ptr(),
+              int(scales.dtype == np.float16), None if bd is None else bd.data_ptr(), y.data_ptr(), out_f, in_f,
+              group, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    from glacier_b200 import _lib as L
+    assert L.lib().glacier_cuda_device_status(0) == 0
+    return y.cpu().numpy()
+
+
+@pytest.mark.parametrize("out_f,in_f,group,batch", [
+    (512, 3584, 32, 1),     # 32-row CTAs (tensor-core Q8 path)
+    (9600, 3584, 32, 1),    # 64-row CTAs
+    (19200, 3584, 32, 1),   # 128-row CTAs
+    (4608, 3584, 32, 3),    # 7B QKV, batch 3
+    (3584, 3584, 32, 5),    # 7B O, batch 5 = 4 + 1 rows
+    (1000, 256, 32, 2),     # row tail
+    (4864, 896, 32, 1),     # config 1 (K % 256 != 0: generic kernel)
+    (1000, 256, 16, 2),     # group 16: activation blocks of 16
+    (1000, 256, 8, 1),      # group 8: activation blocks of 32 over four weight groups
+    (512, 512, 64, 1),
+])
+@pytest.mark.parametrize("scale_dtype", ["f16", "f32"])
+def test_q8_gemv_bit_identical_to_oracle(out_f, in_f, group, batch, scale_dtype):
+    rng = np.random.default_rng(out_f + 3 * in_f + group)
+    packed, s32, s16 = synthetic_int4(rng, out_f, in_f, group)
+    x = rng.standard_normal((batch, in_f), dtype=np.float32)
+    x[0, 32:64] = 0  # an all-zero activation block (scale 0)
+    bias = rng.standard_normal(out_f, dtype=np.float32) * 0.1
+    ref = oracle.linear_int4_q8(x, packed, s32, out_f, in_f, group, bias=bias, weight_dispatch=True)
+    y = _run_q8(x, packed, s16 if scale_dtype == "f16" else s32, out_f, in_f, group, bias)
+    assert np.array_equal(y.view(np.uint32), ref.view(np.uint32)), max_rel_err(y, ref)
+
+
+def test_q8_gemv_without_bias_and_reference_fallbacks():
+    rng = np.random.default_rng(11)
+    # no bias
+    packed, s32, s16 = synthetic_int4(rng, 768, 2048, 32)
+    x = rng.standard_normal((2, 2048), dtype=np.float32)
+    ref = oracle.linear_int4_q8(x, packed, s32, 768, 2048, 32, weight_dispatch=True)
+    assert np.array_equal(_run_q8(x, packed, s16, 768, 2048, 32).view(np.uint32), ref.view(np.uint32))
+    # inputs longer than 16384 and LM-head-sized outputs take the FP32 path (oracle within tolerance)
+    for out_f, in_f in ((64, 16640), (65600, 256)):
+        packed, s32, s16 = synthetic_int4(rng, out_f, in_f, 32)
+        x = rng.standard_normal((1, in_f), dtype=np.float32)
+        ref = oracle.linear_int4_q8(x, packed, s32, out_f, in_f, 32, weight_dispatch=True)
+        assert np.array_equal(ref, oracle.linear_int4(x, packed, s32, out_f, in_f, 32))
+        assert max_rel_err(_run_q8(x, packed, s16, out_f, in_f, 32), ref) <= REL_TOL
