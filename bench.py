@@ -337,6 +337,7 @@ def run_glacier(args):
     # between its kernel classes for a few more steps of the same decode.
     dom = step_kernel_timing(torch, dm, sess, cfg, lanes, stream, args.profile_steps, device_step)
     b1 = batch1_decode(torch, model, cfg, args, rank, stream)
+    b1["gemv_activation_modes"] = gemv_modes_timing(torch, cfg)
 
     dev_ms, e2e_ms = max_over_ranks([dev_ms, e2e_s * 1e3], ws, dev)
     tokens_total = lanes * args.steps * (1 if tp > 1 else ws)
@@ -521,6 +522,52 @@ def batch1_decode(torch, model, cfg, args, rank, stream) -> dict:
             "achieved_gbs": byt / (ms * 1e-3) / 1e9, "frac_of_hbm_peak": byt / (ms * 1e-3) / 1e9 / hbm,
             "timing": f"CUDA events over {steps} CUDA-graph replays of the greedy step after {warm} warm-up steps",
             "kernels": prof["kernels"]}
+
+
+def gemv_modes_timing(torch, cfg) -> dict:
+    """The batch-1 INT4 GEMV on the 7B projection shapes in both activation modes: FP32
+    activations (glacier_cuda_int4_linear, the parity mode of the decode step) and Q8
+    activations (glacier_cuda_int4_linear_q8, the reference's default decode numerics,
+    bit-identical to its portable path).  Each figure is one replay of a CUDA graph of 20
+    back-to-back calls on rotating weight copies (more than L2 in total), timed with CUDA events
+    on the capture stream; bytes are the INT4 codes plus fp16 scales."""
+    from glacier_b200 import _lib
+    L = _lib.lib()
+    out = {}
+    shapes = {"qkv": (cfg.q_dim + 2 * cfg.kv_dim, cfg.dim), "o": (cfg.dim, cfg.q_dim), "gate_up": (2 * cfg.hidden, cfg.dim)}
+    st = torch.cuda.Stream()
+    for name, (M, K) in shapes.items():
+        n = M * K
+        copies = max(2, min(8, int(4 * 126e6 // (n * 0.5625)) + 1))
+        Ws = [torch.randint(0, 256, (n // 2,), dtype=torch.uint8, device="cuda") for _ in range(copies)]
+        Ss = [(torch.rand(n // 32, device="cuda") * 0.02).half() for _ in range(copies)]
+        x = torch.randn(1, K, device="cuda")
+        y = torch.empty(1, M, device="cuda")
+        byt = n // 2 + n // 32 * 2
+        e = {}
+        for mode, fn in (("fp32", L.glacier_cuda_int4_linear), ("q8", L.glacier_cuda_int4_linear_q8)):
+            def call(i):
+                assert fn(x.data_ptr(), 1, Ws[i % copies].data_ptr(), Ss[i % copies].data_ptr(), 1, None, y.data_ptr(),
+                          M, K, 32, st.cuda_stream) == 0
+            with torch.cuda.stream(st):
+                for i in range(3):
+                    call(i)
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=st):
+                    for i in range(20):
+                        call(i)
+                g.replay()
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(st)
+                g.replay()
+                e1.record(st)
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) / 20 * 1e3
+            e[mode] = {"us": us, "gbs": byt / (us * 1e-6) / 1e9}
+            del g
+        out[f"{name}_{M}x{K}"] = e
+    return out
 
 
 def run_prefill(args):
