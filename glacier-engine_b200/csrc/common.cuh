@@ -129,7 +129,8 @@ struct Int4Weight {
   bool f16 = true;
   size_t scale_stride = 0;          // elements per scale row; 0 = flat reference array
   size_t M = 0, K = 0, group = 0;
-  bool tc = false;                  // tensor-core GEMV eligible (maps valid)
+  bool tc = false;                  // tensor-core GEMV eligible (group 32, maps valid)
+  bool tcg = false;                 // tensor-core GEMM maps valid (group 8, 16 or 32)
   CUtensorMap tmap_w, tmap_s;
 };
 

@@ -59,7 +59,8 @@ constexpr int kDoneRing = 8;                    // chunk-completion barriers (>=
 constexpr uint32_t kAColsPerSlot = 128;         // 64 columns of -Whi + 64 of Wlo (2 fp16 per column)
 constexpr uint32_t kTmemCols = 512;             // the whole TMEM of the SM (one CTA per SM)
 constexpr int kNibBytes = kRowsTile * 128;      // 128 rows x 256 codes
-constexpr int kSclBytes = kRowsTile * 16;       // 128 rows x 8 fp16 scales
+// Scale tile of a super-stage: 128 rows x 256/group fp16 scales (16, 32 or 64 bytes a row).
+__host__ __device__ constexpr int scl_bytes(int per32) { return kRowsTile * 16 * per32; }
 constexpr int kThreads = (3 + kConvWarps + kEpiWarps) * 32;
 constexpr int kMinSmem = 120 * 1024;            // keeps a second CTA (and its TMEM request) off the SM
 
@@ -153,6 +154,7 @@ struct GemmParams {
   int nsplit, tiles, units;
   int nib_slots, b_slots;
   int acc_cols, acc_bufs;  // TMEM columns per accumulator buffer, number of buffers
+  int sc_x;                // scale-tile x coordinate per super-stage (256 / group)
   int* err;
 };
 
@@ -170,6 +172,8 @@ __device__ __forceinline__ Unit unit_of(const GemmParams& p, int u) {
   return w;
 }
 
+// S = scale groups per 32 codes: 1 (group 32), 2 (group 16) or 4 (group 8).
+template <int S>
 __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_w,
                                                               const __grid_constant__ CUtensorMap tmap_s,
                                                               const __grid_constant__ CUtensorMap tmap_x,
@@ -179,6 +183,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
   const int bbytes = 2 * p.np * 128;  // [Xhi | Xlo] box: 2*Np rows x 64 fp16; a B stage holds kSub boxes
   const int NS = p.nib_slots, BS = p.b_slots;
   uint8_t* nib = smem;                                 // NS x (nibbles + scales)
+  constexpr int kSclBytes = scl_bytes(S);
   uint8_t* btile = nib + NS * (kNibBytes + kSclBytes);  // BS x kSub x bbytes
   uint64_t* bars = reinterpret_cast<uint64_t*>(btile + BS * kSub * bbytes);
   uint64_t* nib_full = bars;
@@ -242,7 +247,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
           mbar_arrive_expect_tx(&nib_full[slot], kNibBytes + kSclBytes);
           const int ks = w.c0 / kChunksPerSuper + i;  // super-stage index along K
           tma_load_2d(dst, &tmap_w, ks * 128, w.row0, &nib_full[slot], pol);
-          tma_load_2d(dst + kNibBytes, &tmap_s, ks * 8, w.row0, &nib_full[slot], pol);
+          tma_load_2d(dst + kNibBytes, &tmap_s, ks * p.sc_x, w.row0, &nib_full[slot], pol);
           if (++slot == (uint32_t)NS) { slot = 0; ph ^= 1; }
         }
       }
@@ -359,19 +364,23 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
           }
           const int as = ch % kASlots;
           const uint8_t* nrow = nib + ns * (kNibBytes + kSclBytes) + rrow * 128;
-          const uint8_t* srow = nib + ns * (kNibBytes + kSclBytes) + kNibBytes + rrow * 16;
+          const uint8_t* srow = nib + ns * (kNibBytes + kSclBytes) + kNibBytes + rrow * 16 * S;
           const uint32_t ta = tlane + (uint32_t)as * kAColsPerSlot;
 #pragma unroll
           for (int gi = 0; gi < 2 * kSub; ++gi) {
             const int grp = sub * 2 * kSub + gi;  // 32-code group within the 256-code super stage
             const uint4 g = *reinterpret_cast<const uint4*>(nrow + (((uint32_t)grp ^ swz) << 4));
-            const uint32_t sh = *reinterpret_cast<const uint16_t*>(srow + 2 * grp);
-            const uint32_t s2 = sh * 0x10001u;      // {s, s}
-            const uint32_t ns2 = s2 ^ 0x80008000u;  // {-s, -s}
+            // Word j (codes 8j..8j+7) uses scale grp*S + j*S/4 of the super-stage.
+            uint32_t s2w[S];
+#pragma unroll
+            for (int k = 0; k < S; ++k)
+              s2w[k] = (uint32_t)reinterpret_cast<const uint16_t*>(srow)[grp * S + k] * 0x10001u;  // {s, s}
             const uint32_t words[4] = {g.x, g.y, g.z, g.w};
             uint32_t hi[16], lo[16];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
+              const uint32_t s2 = s2w[j * S / 4];
+              const uint32_t ns2 = s2 ^ 0x80008000u;  // {-s, -s}
               uint32_t q[4];
               unpack8(words[j], q);
 #pragma unroll
@@ -514,7 +523,9 @@ __global__ void split_activation_kernel(const float* __restrict__ x, size_t ldx,
 
 size_t gemm_split_bytes(size_t np, size_t K) { return 2 * np * K * sizeof(__half) + np * sizeof(float) + 256; }
 
-bool gemm_tc_supported(const Int4Weight& w) { return w.tc && w.f16 && w.K % kPipeK == 0; }
+// Groups 8, 16 and 32 (the maps int4_weight_prepare encodes), fp16 scales, K a
+// multiple of the 128-K pipeline chunk.
+bool gemm_tc_supported(const Int4Weight& w) { return w.tcg && w.f16 && w.K % kPipeK == 0; }
 
 // Activations in split form for the GEMM: xs [2*np, K] fp16 + xscale [np].
 int split_activation(const float* x, size_t ldx, size_t n, size_t K, size_t np, __half* xs, float* xscale,
@@ -533,21 +544,22 @@ int encode_split_map(CUtensorMap* map, const __half* xs, size_t np, size_t K) {
 // (1024 K of HBM reads in flight) and as many 64-K activation tiles as fit,
 // at most eight; the footprint never drops below kMinSmem so that exactly one
 // CTA (which takes the whole TMEM) runs per SM.
-static void gemm_slots(size_t np, int* nib, int* b) {
+static void gemm_slots(size_t np, int per32, int* nib, int* b) {
   *nib = 4;
   *b = kMaxSlots;
   const size_t fixed = 1024 + (size_t)(3 * kMaxSlots + kDoneRing + kASlots + 5) * 8 + 16;
-  auto bytes = [&]() { return fixed + (size_t)*nib * (kNibBytes + kSclBytes) + (size_t)*b * kSub * 2 * np * 128; };
+  const size_t stage = (size_t)(kNibBytes + scl_bytes(per32));
+  auto bytes = [&]() { return fixed + (size_t)*nib * stage + (size_t)*b * kSub * 2 * np * 128; };
   while (bytes() > 227 * 1024 && *b > 3) --*b;
   while (bytes() > 227 * 1024 && *nib > 2) --*nib;
   while (bytes() > 227 * 1024 && *b > 2) --*b;
 }
 
-size_t gemm_smem_bytes(size_t np) {
+size_t gemm_smem_bytes(size_t np, int per32) {
   int nib, b;
-  gemm_slots(np, &nib, &b);
+  gemm_slots(np, per32, &nib, &b);
   const size_t bytes = 1024 + (size_t)(3 * kMaxSlots + kDoneRing + kASlots + 5) * 8 + 16 +
-                       (size_t)nib * (kNibBytes + kSclBytes) + (size_t)b * kSub * 2 * np * 128;
+                       (size_t)nib * (kNibBytes + scl_bytes(per32)) + (size_t)b * kSub * 2 * np * 128;
   return bytes < (size_t)kMinSmem ? (size_t)kMinSmem : bytes;
 }
 
@@ -610,18 +622,22 @@ int gemm_int4_tc(const Int4Weight& w, const CUtensorMap& xmap, const float* xsca
   const int sup = (int)ceil_div(w.K, kSuperK);
   const int per = (int)ceil_div(sup, nsplit) * kChunksPerSuper;
   const int tiles = (int)ceil_div(w.M, kRowsTile);
-  const size_t smem = gemm_smem_bytes(np);
+  const int per32 = (int)(32 / w.group);  // scale groups per 32 codes
+  const size_t smem = gemm_smem_bytes(np, per32);
   GLC_REQUIRE(smem <= 227 * 1024, "int4 gemm: %zu bytes of shared memory", smem);
-  static size_t attr = 0;
-  if (attr < smem) {
-    const int rc = allow_dynamic_smem((const void*)gemm_tc_kernel, (int)smem);
+  const void* kern = per32 == 1 ? (const void*)gemm_tc_kernel<1>
+                     : per32 == 2 ? (const void*)gemm_tc_kernel<2> : (const void*)gemm_tc_kernel<4>;
+  static size_t attr[3] = {0, 0, 0};
+  size_t& done = attr[per32 == 1 ? 0 : per32 == 2 ? 1 : 2];
+  if (done < smem) {
+    const int rc = allow_dynamic_smem(kern, (int)smem);
     if (rc) return rc;
-    attr = smem;
+    done = smem;
   }
   int* err = device_symbol_address(g_gemm_error);
   GLC_REQUIRE(err != nullptr, "int4 gemm: device status word unavailable");
   int nib_slots, b_slots;
-  gemm_slots(np, &nib_slots, &b_slots);
+  gemm_slots(np, per32, &nib_slots, &b_slots);
   // Accumulator columns: 2*np (hi | lo products), a power of two >= 32; two
   // buffers when they fit beside the A ring in the 512 TMEM columns.
   int acc_cols = 32;
@@ -647,9 +663,14 @@ int gemm_int4_tc(const Int4Weight& w, const CUtensorMap& xmap, const float* xsca
   prm.b_slots = b_slots;
   prm.acc_cols = acc_cols;
   prm.acc_bufs = acc_bufs;
+  prm.sc_x = 8 * per32;
   prm.err = err;
   const int grid = std::min(prm.units, sm_count());
-  return launch_pdl(gemm_tc_kernel, dim3(grid), dim3(kThreads), smem, stream, 1, w.tmap_w, w.tmap_s, xmap, prm);
+  if (per32 == 2)
+    return launch_pdl(gemm_tc_kernel<2>, dim3(grid), dim3(kThreads), smem, stream, 1, w.tmap_w, w.tmap_s, xmap, prm);
+  if (per32 == 4)
+    return launch_pdl(gemm_tc_kernel<4>, dim3(grid), dim3(kThreads), smem, stream, 1, w.tmap_w, w.tmap_s, xmap, prm);
+  return launch_pdl(gemm_tc_kernel<1>, dim3(grid), dim3(kThreads), smem, stream, 1, w.tmap_w, w.tmap_s, xmap, prm);
   return GLACIER_CUDA_OK;
 }
 

@@ -356,15 +356,20 @@ int int4_weight_prepare(Int4Weight& w) {
   GLC_REQUIRE(w.M < (1u << 31) && w.K < (1u << 31), "int4 weight: dimension too large");
   const size_t esz = w.f16 ? 2 : 4;
   const size_t stride = w.scale_stride ? w.scale_stride : (w.K % w.group == 0 ? w.K / w.group : 0);
-  w.tc = w.group == 32 && w.K % 32 == 0 && stride != 0 && (stride * esz) % 16 == 0 &&
-         (uintptr_t)w.packed % 16 == 0 && (uintptr_t)w.scales % 16 == 0;
-  if (!w.tc) return GLACIER_CUDA_OK;
+  // Maps for 128-row x 256-code tiles and their 256/group scales: the GEMV takes
+  // group 32, the tcgen05 GEMM groups 8, 16 and 32 (one scale row of 16, 32 or 64
+  // bytes per tile row and super-stage).
+  w.tcg = (w.group == 8 || w.group == 16 || w.group == 32) && w.K % 32 == 0 && stride != 0 &&
+          (stride * esz) % 16 == 0 && (uintptr_t)w.packed % 16 == 0 && (uintptr_t)w.scales % 16 == 0;
+  w.tc = w.tcg && w.group == 32;
+  if (!w.tcg) return GLACIER_CUDA_OK;
   w.scale_stride = stride;
   int rc = encode_tmap_2d(&w.tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.packed, w.K / 2, w.M, w.K / 2, 128, kRows,
                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
   if (rc) return rc;
   rc = encode_tmap_2d(&w.tmap_s, w.f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, w.scales,
-                      w.K / 32, w.M, stride * esz, 8, kRows, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE);
+                      w.K / w.group, w.M, stride * esz, (uint32_t)(256 / w.group), kRows, CU_TENSOR_MAP_SWIZZLE_NONE,
+                      CU_TENSOR_MAP_L2_PROMOTION_NONE);
   return rc;
 }
 

@@ -110,8 +110,9 @@ int glacier_cuda_int4_linear_q8(const float *x, size_t batch, const uint8_t *pac
  * y [batch, out_f]; the reference's M4 weight-stationary GEMM
  * (glacier_int4_gemm_neon_q8_prequant_f16scale_rows4_k16_m4, src/decode_lane4.zig:221-264,
  * int4_neon.c:1439-1621) generalised to batch <= 128 with FP32-activation numerics.
- * scales: fp16 bit patterns [out_f, in_f/32]; group_size must be 32 and in_f a multiple
- * of 256 for the tensor-core path (other shapes run the GEMV kernels).
+ * scales: fp16 bit patterns [out_f, in_f/group]; group_size 8, 16 or 32 (the reference's
+ * production g8/g16 layouts and g32) and in_f a multiple of 128 for the tensor-core path
+ * (other shapes run the GEMV kernels).
  * workspace: glacier_cuda_int4_matmul_workspace(batch, in_f, out_f) bytes of device memory. */
 size_t glacier_cuda_int4_matmul_workspace(size_t batch, size_t in_features, size_t out_features);
 int glacier_cuda_int4_matmul_f16scale(const float *x, size_t batch, const uint8_t *packed,

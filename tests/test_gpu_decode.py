@@ -3,13 +3,15 @@
 Greedy token ids must match the oracle exactly except at near-ties: a step whose
 oracle top-2 logit gap is below 1e-3 * max(1, |top1|) is exempt, and the lane
 stops being compared after such a step (its continuation legitimately differs).
-Logits must match within the dequant-matvec tolerance.
+Logits must match within DECODE_LOGIT_TOL of the row's largest |logit| (the
+kernels' own per-element 1e-3 bound is checked by their tests; through several
+layers their rounding compounds onto logits near zero).
 """
 import numpy as np
 import pytest
 
 import oracle
-from helpers import REL_TOL, max_rel_err
+from helpers import DECODE_LOGIT_TOL, max_err_vs_row_max
 
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
@@ -45,7 +47,7 @@ def run_parity(cfg, lanes, prompt_len, new_tokens, seed=7):
             ol, _ = om.decode_token(pools[b], bt, pos, int(cur[b]))
             if not live[b]:
                 continue
-            assert max_rel_err(gl[b], ol) <= REL_TOL, (b, pos)
+            assert max_err_vs_row_max(gl[b], ol) <= DECODE_LOGIT_TOL, (b, pos)
             if pos >= prompt_len - 1:
                 ref_tok = oracle.argmax(ol)
                 if gpu_tok[b] != ref_tok:
@@ -123,6 +125,14 @@ def test_greedy_step_graph_replay_matches_stream_steps(lanes):
     dm.close()
 
 
+def test_decode_tensor_core_mode_group16_model():
+    from glacier_b200.model import ModelConfig
+    # the reference's production g16 layout on the tcgen05 GEMM (16 lanes)
+    cfg = ModelConfig(num_layers=2, dim=512, hidden=1024, num_heads=28, num_kv_heads=4, head_dim=128, vocab=2048,
+                      group=16)
+    assert run_parity(cfg, lanes=16, prompt_len=4, new_tokens=3) >= 30
+
+
 def test_step_profile_counts_every_kernel_class():
     """The per-class event timing sees each class the expected number of times per step and
     leaves the step's results unchanged."""
@@ -173,7 +183,7 @@ def _prefill_parity(cfg, reserve_lanes, prompt_len, new_tokens, seed=11):
     logits_dev = torch.empty(cfg.vocab, dtype=torch.float32, device="cuda")
     tok = int(sess.prefill(prompt, logits=logits_dev).cpu()[0])
     assert int(sess.last_status.cpu()[0]) == 0
-    assert max_rel_err(logits_dev.cpu().numpy(), ol) <= REL_TOL
+    assert max_err_vs_row_max(logits_dev.cpu().numpy(), ol) <= DECODE_LOGIT_TOL
     ref = oracle.argmax(ol)
     if tok != ref:
         assert near_tie(ol)
@@ -184,7 +194,7 @@ def _prefill_parity(cfg, reserve_lanes, prompt_len, new_tokens, seed=11):
     for _ in range(new_tokens - 1):
         out = int(sess.step(tokens=[cur], positions=[pos], logits=step_logits).cpu()[0])
         ol, _ = om.decode_token(pool, bt, pos, cur)
-        assert max_rel_err(step_logits.cpu().numpy()[0], ol) <= REL_TOL, pos
+        assert max_err_vs_row_max(step_logits.cpu().numpy()[0], ol) <= DECODE_LOGIT_TOL, pos
         ref = oracle.argmax(ol)
         if out != ref:
             assert near_tie(ol)

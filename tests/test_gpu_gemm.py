@@ -36,3 +36,27 @@ def test_gemm_matches_oracle(out_f, in_f, batch):
     y = y.cpu().numpy()
     for b in range(batch):
         assert max_rel_err(y[b], ref[b]) <= REL_TOL, b
+
+
+
+@pytest.mark.parametrize("group,out_f,in_f,batch", [
+    (16, 1000, 2048, 17),   # two scales per 32 codes
+    (8, 512, 1024, 64),     # four scales per 32 codes
+    (16, 4608, 3584, 64),   # 7B QKV shape in the reference's production g16 layout
+    (8, 256, 512, 128),
+])
+def test_gemm_groups_8_and_16_match_oracle(group, out_f, in_f, batch):
+    """The tcgen05 GEMM with the reference's production group sizes (g8 / g16): the converters
+    pick the scale of every 8-code word from 256/group scales per row and super-stage."""
+    from glacier_b200 import _lib, ops
+    rng = np.random.default_rng(out_f + in_f + batch + group)
+    packed, s32, s16 = synthetic_int4(rng, out_f, in_f, group)
+    x = rng.standard_normal((batch, in_f), dtype=np.float32)
+    bias = rng.standard_normal(out_f, dtype=np.float32) * 0.1
+    y = ops.linear_int4_tensor_core(dev(x), dev(packed), dev(s16.view(np.int16)), out_f, in_f, group, bias=dev(bias))
+    torch.cuda.synchronize()
+    assert _lib.lib().glacier_cuda_device_status(1) == 0
+    ref = oracle.linear_int4(x, packed, s32, out_f, in_f, group, bias=bias, threads=8)
+    y = y.cpu().numpy()
+    for b in range(batch):
+        assert max_rel_err(y[b], ref[b]) <= REL_TOL, b

@@ -14,7 +14,7 @@ import numpy as np
 import pytest
 
 import oracle
-from helpers import REL_TOL, max_rel_err
+from helpers import DECODE_LOGIT_TOL, REL_TOL, max_err_vs_row_max, max_rel_err
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
@@ -126,7 +126,7 @@ def test_tp2_decode_matches_oracle():
             ol, _ = om.decode_token(pools[b], bt, pos, int(cur[b]))
             if not live[b]:
                 continue
-            assert max_rel_err(lg0[b], ol) <= REL_TOL, (b, pos)
+            assert max_err_vs_row_max(lg0[b], ol) <= DECODE_LOGIT_TOL, (b, pos)
             if pos >= prompt_len - 1 and tok0[b] != oracle.argmax(ol):
                 top2 = np.sort(ol)[-2:]
                 assert (top2[1] - top2[0]) < 1e-3 * max(1.0, abs(float(top2[1])))
