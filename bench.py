@@ -336,8 +336,12 @@ def run_glacier(args):
     # Per-kernel-class pass: the library records CUDA events on the step's stream
     # between its kernel classes for a few more steps of the same decode.
     dom = step_kernel_timing(torch, dm, sess, cfg, lanes, stream, args.profile_steps, device_step)
-    b1 = batch1_decode(torch, model, cfg, args, rank, stream)
-    b1["gemv_activation_modes"] = gemv_modes_timing(torch, cfg)
+    # The batch-1 half of the metric is a single-GPU measurement: rank 0 takes it,
+    # with no collective in it, while the other ranks go on to the final max-over-ranks.
+    b1 = None
+    if rank == 0:
+        b1 = batch1_decode(torch, model, cfg, args, rank, stream)
+        b1["gemv_activation_modes"] = gemv_modes_timing(torch, cfg)
 
     dev_ms, e2e_ms = max_over_ranks([dev_ms, e2e_s * 1e3], ws, dev)
     tokens_total = lanes * args.steps * (1 if tp > 1 else ws)
