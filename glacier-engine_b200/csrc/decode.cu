@@ -37,6 +37,8 @@ int silu_mul(const float* gate, const float* up, size_t ld_in, float* out, size_
              cudaStream_t stream, SplitOut so = SplitOut());
 int embed_gather(const __half* table, size_t vocab, size_t dim, const int32_t* tokens, size_t batch, float* out,
                  size_t ldo, cudaStream_t stream);
+int embed_gather(const float* table, size_t vocab, size_t dim, const int32_t* tokens, size_t batch, float* out,
+                 size_t ldo, cudaStream_t stream);
 int qkv_rope_append(const float* qkv, size_t ld, size_t split_stride, int nsplit, const float* bias,
                     const float* cos_t, const float* sin_t, size_t positions, const int32_t* pos, size_t batch,
                     size_t num_heads, size_t num_kv_heads, size_t head_dim, float* q_out, size_t ldq, float* pool,
@@ -247,7 +249,7 @@ struct glacier_cuda_model {
   std::vector<std::unique_ptr<Layer>> layers;
   FusedWeight lm;
   DevBuf embedding, final_norm, rope_cos, rope_sin;
-  bool emb_loaded = false, final_loaded = false, finalized = false;
+  bool emb_loaded = false, emb_f32 = false, final_loaded = false, finalized = false;
   // Reserved step workspace.
   size_t max_lanes = 0, max_pages = 0;
   DevBuf x, hn, qkv, q, attn, proj, gu, act, down, logits, ctx, att_ws, arg_ws, status;
@@ -379,8 +381,7 @@ glacier_cuda_model* glacier_cuda_model_create(const glacier_cuda_model_config* c
     }
     m->layers.push_back(std::move(L));
   }
-  if (m->lm.init({c.vocab}, c.dim, c.group_size, f16) || m->embedding.alloc((size_t)c.vocab * c.dim * 2) ||
-      m->final_norm.alloc((size_t)c.dim * 4))
+  if (m->lm.init({c.vocab}, c.dim, c.group_size, f16) || m->final_norm.alloc((size_t)c.dim * 4))
     return nullptr;
   // RoPE table (generate.zig:791-808): angle = pos / theta^(2i/hd) in f32.
   const size_t half = c.head_dim / 2, P = c.max_positions;
@@ -472,10 +473,27 @@ int glacier_cuda_model_load_embedding_f16(glacier_cuda_model* m, const uint16_t*
   GLC_REQUIRE(m && table, "model_load_embedding: null argument");
   GLC_REQUIRE(count == (size_t)m->cfg.vocab * m->cfg.dim, "model_load_embedding: %zu values, expected %zu", count,
               (size_t)m->cfg.vocab * m->cfg.dim);
-  const int rc = bind_device(m);
+  GLC_REQUIRE(!m->finalized, "model_load_embedding: model already finalized");
+  int rc = bind_device(m);
   if (rc) return rc;
+  if (m->embedding.bytes != count * 2 && (rc = m->embedding.alloc(count * 2))) return rc;
   GLC_CHECK_CUDA(cudaMemcpy(m->embedding.p, table, count * 2, cudaMemcpyHostToDevice));
   m->emb_loaded = true;
+  m->emb_f32 = false;
+  return GLACIER_CUDA_OK;
+}
+
+int glacier_cuda_model_load_embedding_f32(glacier_cuda_model* m, const float* table, size_t count) {
+  GLC_REQUIRE(m && table, "model_load_embedding_f32: null argument");
+  GLC_REQUIRE(!m->finalized, "model_load_embedding_f32: model already finalized");
+  GLC_REQUIRE(count == (size_t)m->cfg.vocab * m->cfg.dim, "model_load_embedding_f32: %zu values, expected %zu",
+              count, (size_t)m->cfg.vocab * m->cfg.dim);
+  int rc = bind_device(m);
+  if (rc) return rc;
+  if (m->embedding.bytes != count * 4 && (rc = m->embedding.alloc(count * 4))) return rc;
+  GLC_CHECK_CUDA(cudaMemcpy(m->embedding.p, table, count * 4, cudaMemcpyHostToDevice));
+  m->emb_loaded = true;
+  m->emb_f32 = true;
   return GLACIER_CUDA_OK;
 }
 
@@ -600,7 +618,9 @@ static int step_impl(glacier_cuda_model* m, glacier_cuda_kv* kv, size_t lanes, c
   if ((rc = launch_pdl(ctx_from_pos_kernel, dim3((unsigned)ceil_div(B, 128)), dim3(128), 0, st, 1, positions,
                        m->ctx.as<int32_t>(), (int)B)))
     return rc;
-  if ((rc = embed_gather(m->embedding.as<__half>(), c.vocab, D, tokens, B, x, D, st))) return rc;
+  if ((rc = m->emb_f32 ? embed_gather(m->embedding.as<float>(), c.vocab, D, tokens, B, x, D, st)
+                       : embed_gather(m->embedding.as<__half>(), c.vocab, D, tokens, B, x, D, st)))
+    return rc;
   // Split-form destinations of the GEMM inputs (tensor-core mode only).
   auto split_of = [&](DevBuf& xs, size_t K) {
     SplitOut so;
@@ -792,3 +812,8 @@ int glacier_cuda_model_profile_read(glacier_cuda_model* m, double* ms, uint64_t*
 }
 
 }  // extern "C"
+
+namespace glacier {
+const glacier_cuda_model_config* model_config(const glacier_cuda_model* m) { return &m->cfg; }
+}  // namespace glacier
+

@@ -401,7 +401,11 @@ __global__ void silu_mul_kernel(const float* __restrict__ gate, const float* __r
 }
 
 // x[b, :] = float(table[token[b], :])
-__global__ void embed_kernel(const __half* __restrict__ table, const int32_t* __restrict__ tokens, int vocab, int dim,
+__device__ __forceinline__ float embed_value(__half v) { return __half2float(v); }
+__device__ __forceinline__ float embed_value(float v) { return v; }
+
+template <typename T>
+__global__ void embed_kernel(const T* __restrict__ table, const int32_t* __restrict__ tokens, int vocab, int dim,
                              float* __restrict__ out, size_t ldo, int* __restrict__ bad) {
   griddep_launch();
   griddep_wait();
@@ -412,7 +416,7 @@ __global__ void embed_kernel(const __half* __restrict__ table, const int32_t* __
     return;
   }
   for (int k = blockIdx.x * blockDim.x + threadIdx.x; k < dim; k += gridDim.x * blockDim.x)
-    out[b * ldo + k] = __half2float(table[(size_t)tok * dim + k]);
+    out[b * ldo + k] = embed_value(table[(size_t)tok * dim + k]);
 }
 
 // One CTA per lane: adds the q/k/v biases to the fused projection row (summing
@@ -583,12 +587,23 @@ int silu_mul(const float* gate, const float* up, size_t ld_in, float* out, size_
   return launch_row_cluster((const void*)silu_mul_split_kernel, args, batch, cl, smem, stream);
 }
 
-int embed_gather(const __half* table, size_t vocab, size_t dim, const int32_t* tokens, size_t batch, float* out,
-                 size_t ldo, cudaStream_t stream) {
+template <typename T>
+int embed_gather_t(const T* table, size_t vocab, size_t dim, const int32_t* tokens, size_t batch, float* out,
+                   size_t ldo, cudaStream_t stream) {
   GLC_REQUIRE(table && tokens && out && batch > 0 && dim > 0, "embedding: empty or null argument");
   dim3 grid((unsigned)std::min<size_t>(ceil_div(dim, 256), 16), (unsigned)batch);
-  return launch_pdl(embed_kernel, grid, dim3(256), 0, stream, 1, table, tokens, (int)vocab, (int)dim, out, ldo,
+  return launch_pdl(embed_kernel<T>, grid, dim3(256), 0, stream, 1, table, tokens, (int)vocab, (int)dim, out, ldo,
                     ops_err_ptr());
+}
+
+int embed_gather(const __half* table, size_t vocab, size_t dim, const int32_t* tokens, size_t batch, float* out,
+                 size_t ldo, cudaStream_t stream) {
+  return embed_gather_t(table, vocab, dim, tokens, batch, out, ldo, stream);
+}
+
+int embed_gather(const float* table, size_t vocab, size_t dim, const int32_t* tokens, size_t batch, float* out,
+                 size_t ldo, cudaStream_t stream) {
+  return embed_gather_t(table, vocab, dim, tokens, batch, out, ldo, stream);
 }
 
 int qkv_rope_append(const float* qkv, size_t ld, size_t split_stride, int nsplit, const float* bias,

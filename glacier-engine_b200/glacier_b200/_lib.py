@@ -16,12 +16,13 @@ _lib = None
 
 
 class GlacierCudaError(RuntimeError):
-    def __init__(self, code: int, msg: str):
+    def __init__(self, code: int, msg: str, reason: int = 0):
         super().__init__(f"glacier_cuda error {code}: {msg}")
         self.code = code
+        self.reason = reason  # enum glacier_cuda_format_reason when code is EFORMAT
 
 
-EINVAL, ECUDA, ENOMEM, EMASK, ENAN, EUNSUPPORTED = -1, -2, -3, -4, -5, -6
+EINVAL, ECUDA, ENOMEM, EMASK, ENAN, EUNSUPPORTED, EFORMAT = -1, -2, -3, -4, -5, -6, -7
 
 vp, sz, i32, u32, f32 = C.c_void_p, C.c_size_t, C.c_int, C.c_uint32, C.c_float
 
@@ -60,6 +61,15 @@ SIGNATURES = {
     "glacier_cuda_model_load_qio": ([vp, i32, i32, vp, sz], i32),
     "glacier_cuda_model_load_f32": ([vp, i32, i32, vp, sz], i32),
     "glacier_cuda_model_load_embedding_f16": ([vp, vp, sz], i32),
+    "glacier_cuda_model_load_embedding_f32": ([vp, vp, sz], i32),
+    "glacier_cuda_format_error": ([], C.c_int32),
+    "glacier_cuda_crc32": ([vp, sz], C.c_uint32),
+    "glacier_cuda_glacier_open": ([vp, C.c_uint64, vp], i32),
+    "glacier_cuda_glacier_validate_pages": ([vp, C.c_uint64], i32),
+    "glacier_cuda_glacier_page": ([vp, C.c_uint64, C.c_uint64, vp], i32),
+    "glacier_cuda_glacier_page_decode_f32": ([vp, C.c_uint64, C.c_uint64, vp, C.c_uint64], i32),
+    "glacier_cuda_glacier_geometry": ([vp, C.c_uint64, vp], i32),
+    "glacier_cuda_model_load_glacier": ([vp, vp, C.c_uint64, i32], i32),
     "glacier_cuda_model_finalize": ([vp], i32),
     "glacier_cuda_model_reserve": ([vp, sz, sz], i32),
     "glacier_cuda_kv_create": ([vp, sz], vp),
@@ -76,6 +86,26 @@ SIGNATURES = {
 
 # enum glacier_cuda_tensor_kind
 W_Q, W_K, W_V, W_O, W_GATE, W_UP, W_DOWN, W_LM_HEAD, B_Q, B_K, B_V, N_INPUT, N_POST_ATTN, N_FINAL = range(14)
+
+
+class FileInfo(C.Structure):
+    """glacier_cuda_file_info."""
+    _fields_ = [(n, C.c_uint64) for n in ("container_bytes", "meta_offset", "meta_len", "num_pages",
+                                          "page_index_offset", "page_data_offset")]
+
+
+class PageEntry(C.Structure):
+    """glacier_cuda_page_entry: one decoded 64-byte page index entry."""
+    _fields_ = [("page_id", C.c_uint64), ("layer_idx", C.c_uint32), ("tensor_kind", C.c_uint32),
+                ("row_start", C.c_uint64), ("row_end", C.c_uint64), ("precision", C.c_uint8),
+                ("quant_group", C.c_uint8), ("reserved", C.c_uint16), ("crc32", C.c_uint32),
+                ("data_offset", C.c_uint64), ("data_len", C.c_uint64)]
+
+
+class FileGeometry(C.Structure):
+    """glacier_cuda_file_geometry."""
+    _fields_ = [(n, C.c_uint32) for n in ("num_layers", "dim", "hidden", "vocab", "group_size", "has_lm_head",
+                                          "has_qkv_bias")]
 
 
 class ModelConfigC(C.Structure):
@@ -105,7 +135,8 @@ def lib():
 def check(rc: int) -> int:
     if rc != 0:
         msg = lib().glacier_cuda_last_error()
-        raise GlacierCudaError(rc, msg.decode() if msg else "")
+        reason = lib().glacier_cuda_format_error() if rc == EFORMAT else 0
+        raise GlacierCudaError(rc, msg.decode() if msg else "", reason)
     return rc
 
 

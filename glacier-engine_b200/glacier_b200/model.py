@@ -204,6 +204,26 @@ class DeviceModel:
             self.close()
             raise
 
+    @classmethod
+    def from_glacier(cls, gf, cfg: dict, max_positions: int, scales_f16: bool = True) -> "DeviceModel":
+        """Loads an admitted GlacierFile with a resolved config (see glacier_file.load_model)."""
+        self = cls.__new__(cls)
+        cfgc = _lib.ModelConfigC(cfg["num_layers"], cfg["dim"], cfg["hidden"], cfg["num_heads"],
+                                 cfg["num_kv_heads"], cfg["head_dim"], cfg["vocab"], cfg["group"], cfg["eps"],
+                                 cfg["theta"], max_positions, int(scales_f16))
+        self.cfg = {k: cfg[k] for k in ("num_layers", "dim", "hidden", "num_heads", "num_kv_heads", "head_dim",
+                                        "vocab", "group", "eps", "theta")}
+        self.max_positions = max_positions
+        self.h = _lib.handle(_lib.lib().glacier_cuda_model_create(C.byref(cfgc)))
+        try:
+            _lib.call("glacier_cuda_model_load_glacier", self.h, gf._ptr, gf.size,
+                      int(cfg.get("tie_word_embeddings", False)))
+            _lib.call("glacier_cuda_model_finalize", self.h)
+        except Exception:
+            self.close()
+            raise
+        return self
+
     def enable_tensor_parallel(self, rank: int, world: int, unique_id: bytes):
         """Joins the tensor-parallel group (blocks until every rank has joined)."""
         buf = (C.c_uint8 * 128).from_buffer_copy(unique_id)

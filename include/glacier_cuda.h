@@ -38,6 +38,7 @@ extern "C" {
 #define GLACIER_CUDA_EMASK (-4)        /* sampling.zig:40 InvalidEligibleMask */
 #define GLACIER_CUDA_ENAN (-5)         /* sampling.zig:41 EligibleLogitNaN */
 #define GLACIER_CUDA_EUNSUPPORTED (-6) /* shape outside the kernels' contract */
+#define GLACIER_CUDA_EFORMAT (-7)      /* .glacier container rejected; reason in glacier_cuda_format_error() */
 
 /* Greedy reduction result; same 24-byte layout as glacier_argmax_result
  * (src/backends/cpu/int4_neon.c:8-19). */
@@ -245,6 +246,11 @@ int glacier_cuda_model_load_f32(glacier_cuda_model *model, int layer, int kind, 
 /* Token embedding table [vocab, dim] as IEEE binary16 bit patterns. */
 int glacier_cuda_model_load_embedding_f16(glacier_cuda_model *model, const uint16_t *table, size_t count);
 
+/* Same as float32 values, for tables whose rows are not fp16-exact: an INT4
+ * embedding dequantized as int4_matmul.zig dequantizeRow (:3166-3196) does,
+ * or bf16 / fp32 pages.  The lookup then copies rows without rounding. */
+int glacier_cuda_model_load_embedding_f32(glacier_cuda_model *model, const float *table, size_t count);
+
 /* Checks that every tensor is present and prepares the kernels' descriptors. */
 int glacier_cuda_model_finalize(glacier_cuda_model *model);
 
@@ -318,6 +324,112 @@ enum glacier_cuda_step_kind {
 };
 int glacier_cuda_model_profile(glacier_cuda_model *model, int enable);
 int glacier_cuda_model_profile_read(glacier_cuda_model *model, double *ms, uint64_t *regions, size_t kinds);
+
+/* ------------------------------------------------------------------------
+ * The portable .glacier container (docs/FORMAT_SPEC.md; src/model/format.zig,
+ * src/model/qio.zig) read from a host image of the whole file (a read or an
+ * mmap).  Host-only: none of these touches a GPU except
+ * glacier_cuda_model_load_glacier's uploads.
+ *
+ * Every entry admits the image first, as FileReader.openFile does
+ * (format.zig:407-478).  A rejected image returns GLACIER_CUDA_EFORMAT, and
+ * glacier_cuda_format_error() then names the reference error it stands for.
+ * ---------------------------------------------------------------------- */
+
+enum glacier_cuda_format_reason {
+  GLACIER_CUDA_FMT_OK = 0,
+  GLACIER_CUDA_FMT_TRUNCATED_HEADER,       /* error.TruncatedHeader */
+  GLACIER_CUDA_FMT_BAD_MAGIC,              /* error.BadMagic */
+  GLACIER_CUDA_FMT_BAD_VERSION,            /* error.BadVersion */
+  GLACIER_CUDA_FMT_BAD_HEADER_SIZE,        /* error.BadHeaderSize */
+  GLACIER_CUDA_FMT_BAD_PAGE_SIZE,          /* error.BadPageSize */
+  GLACIER_CUDA_FMT_BAD_RESERVED_FIELD,     /* error.BadReservedField */
+  GLACIER_CUDA_FMT_BAD_LAYOUT,             /* error.BadLayout */
+  GLACIER_CUDA_FMT_METADATA_TOO_LARGE,     /* error.MetadataTooLarge */
+  GLACIER_CUDA_FMT_INDEX_TOO_LARGE,        /* error.IndexTooLarge */
+  GLACIER_CUDA_FMT_LAYOUT_OVERFLOW,        /* error.LayoutOverflow */
+  GLACIER_CUDA_FMT_TRUNCATED_META,         /* error.TruncatedMeta */
+  GLACIER_CUDA_FMT_TRUNCATED_INDEX,        /* error.TruncatedIndex */
+  GLACIER_CUDA_FMT_BAD_METADATA,           /* error.BadMetadata */
+  GLACIER_CUDA_FMT_BAD_TENSOR_KIND,        /* error.BadTensorKind */
+  GLACIER_CUDA_FMT_BAD_PRECISION,          /* error.BadPrecision */
+  GLACIER_CUDA_FMT_BAD_PAGE_ID,            /* error.BadPageId */
+  GLACIER_CUDA_FMT_BAD_ROW_RANGE,          /* error.BadRowRange */
+  GLACIER_CUDA_FMT_EMPTY_PAGE,             /* error.EmptyPage */
+  GLACIER_CUDA_FMT_BAD_QUANT_GROUP,        /* error.BadQuantGroup */
+  GLACIER_CUDA_FMT_PAGE_GEOMETRY_TOO_LARGE, /* error.PageGeometryTooLarge */
+  GLACIER_CUDA_FMT_UNSUPPORTED_PRECISION,  /* error.UnsupportedPrecision (INT2, ternary) */
+  GLACIER_CUDA_FMT_BAD_PAGE_GEOMETRY,      /* error.BadPageGeometry */
+  GLACIER_CUDA_FMT_NON_CONTIGUOUS_PAYLOAD, /* error.NonContiguousPayload */
+  GLACIER_CUDA_FMT_TRUNCATED_PAGE,         /* error.TruncatedPage */
+  GLACIER_CUDA_FMT_TRAILING_BYTES,         /* error.TrailingBytes */
+  GLACIER_CUDA_FMT_BAD_QUANT_PAYLOAD,      /* error.BadQuantPayload */
+  GLACIER_CUDA_FMT_CRC_MISMATCH,           /* error.CrcMismatch */
+  GLACIER_CUDA_FMT_SIZE_MISMATCH,          /* error.SizeMismatch (decode buffer) */
+  GLACIER_CUDA_FMT_NO_LAYERS,              /* LoaderError.NoLayers */
+  GLACIER_CUDA_FMT_MISSING_TENSOR,         /* LoaderError.MissingTensor */
+  GLACIER_CUDA_FMT_BAD_PAYLOAD             /* LoaderError.BadPayload */
+};
+
+/* Reason for this thread's last GLACIER_CUDA_EFORMAT (0 after a success). */
+int32_t glacier_cuda_format_error(void);
+
+/* CRC-32 as std.hash.Crc32 (IEEE reflected polynomial), the per-page checksum. */
+uint32_t glacier_cuda_crc32(const uint8_t *data, size_t len);
+
+typedef struct glacier_cuda_file_info {
+  uint64_t container_bytes, meta_offset, meta_len, num_pages, page_index_offset, page_data_offset;
+} glacier_cuda_file_info;
+
+/* One 64-byte page index entry, decoded (PageEntry, format.zig:141-202). */
+typedef struct glacier_cuda_page_entry {
+  uint64_t page_id;
+  uint32_t layer_idx, tensor_kind; /* TensorKind 0..15 or 255 */
+  uint64_t row_start, row_end;     /* flat element range of the tensor */
+  uint8_t precision;               /* 0 fp16, 1 bf16, 2 int8, 3 int4, 6 fp32 */
+  uint8_t quant_group;             /* 0 for raw pages */
+  uint16_t reserved;
+  uint32_t crc32;
+  uint64_t data_offset, data_len;
+} glacier_cuda_page_entry;
+
+/* Model geometry as loader.zig derives it from page metadata (:1224-1260):
+ * dim from the norms, hidden and vocab from the flat sizes of the MLP and
+ * vocabulary tensors, layers from the largest layer_idx. */
+typedef struct glacier_cuda_file_geometry {
+  uint32_t num_layers, dim, hidden, vocab, group_size;
+  uint32_t has_lm_head, has_qkv_bias;
+} glacier_cuda_file_geometry;
+
+/* Header, layout, metadata JSON and page index admission
+ * (FileReader.openFile, format.zig:407-478). */
+int glacier_cuda_glacier_open(const uint8_t *bytes, uint64_t len, glacier_cuda_file_info *info);
+
+/* Admission plus every page's quantized sub-header and CRC-32
+ * (FileReader.validateAllPageCrcs, format.zig:497-534), pages checked in
+ * parallel on the host; the first failing page in page order is reported. */
+int glacier_cuda_glacier_validate_pages(const uint8_t *bytes, uint64_t len);
+
+int glacier_cuda_glacier_page(const uint8_t *bytes, uint64_t len, uint64_t index, glacier_cuda_page_entry *out);
+
+/* One page's elements as f32 (FileReader.readPageDequant(f32), format.zig:638-662):
+ * CRC first, then the quantized sub-header, then the decode.  count must equal
+ * the page's element count. */
+int glacier_cuda_glacier_page_decode_f32(const uint8_t *bytes, uint64_t len, uint64_t index, float *out,
+                                         uint64_t count);
+
+int glacier_cuda_glacier_geometry(const uint8_t *bytes, uint64_t len, glacier_cuda_file_geometry *out);
+
+/* Loads every tensor of a .glacier image into a model created with the
+ * matching config (loader.zig loadWithOptions, :1214-1540, compact INT4):
+ * INT4 projection, LM head and embedding pages are concatenated in packed
+ * form (concatInt4Pages, :1633-1730), norms and biases decoded to f32, and a
+ * tied LM head reuses the INT4 embedding (:1521-1523).  Every page's CRC is
+ * checked before the first upload.  The caller then runs
+ * glacier_cuda_model_finalize.  Dense (non-INT4) projections and an attention
+ * output bias return GLACIER_CUDA_EUNSUPPORTED. */
+int glacier_cuda_model_load_glacier(glacier_cuda_model *model, const uint8_t *bytes, uint64_t len,
+                                    int tie_word_embeddings);
 
 #ifdef __cplusplus
 }
