@@ -722,6 +722,11 @@ int int4_kind_to_model(uint32_t kind) {
 }
 
 }  // namespace
+
+// Shared with the runtime-image reader: the CRC and this thread's format reason.
+uint32_t crc32_ieee(uint32_t crc, const uint8_t* p, size_t n) { return crc32_update(crc, p, n); }
+int32_t* format_error_slot() { return &g_format_error; }
+
 }  // namespace glacier
 
 using namespace glacier;

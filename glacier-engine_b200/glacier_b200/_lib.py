@@ -70,6 +70,13 @@ SIGNATURES = {
     "glacier_cuda_glacier_page_decode_f32": ([vp, C.c_uint64, C.c_uint64, vp, C.c_uint64], i32),
     "glacier_cuda_glacier_geometry": ([vp, C.c_uint64, vp], i32),
     "glacier_cuda_model_load_glacier": ([vp, vp, C.c_uint64, i32], i32),
+    "glacier_cuda_glrt_open": ([vp, C.c_uint64, vp, vp], i32),
+    "glacier_cuda_glrt_record": ([vp, C.c_uint64, C.c_uint64, vp], i32),
+    "glacier_cuda_glrt_model_info": ([vp, C.c_uint64, vp, vp], i32),
+    "glacier_cuda_model_load_glrt": ([vp, vp, C.c_uint64, vp], i32),
+    "glacier_cuda_rows4_k16_to_row_major": ([vp, vp, sz, sz], i32),
+    "glacier_cuda_rows4_scales_to_row_major": ([vp, vp, sz, sz], i32),
+    "glacier_cuda_pair_nibble_split": ([vp, vp, sz, sz, sz, vp, vp, vp, vp], i32),
     "glacier_cuda_model_finalize": ([vp], i32),
     "glacier_cuda_model_reserve": ([vp, sz, sz], i32),
     "glacier_cuda_kv_create": ([vp, sz], vp),
@@ -106,6 +113,33 @@ class FileGeometry(C.Structure):
     """glacier_cuda_file_geometry."""
     _fields_ = [(n, C.c_uint32) for n in ("num_layers", "dim", "hidden", "vocab", "group_size", "has_lm_head",
                                           "has_qkv_bias")]
+
+
+class GlrtOptions(C.Structure):
+    """glacier_cuda_glrt_options."""
+    _fields_ = [("skip_payload_crc", C.c_uint32), ("skip_payload_digest", C.c_uint32), ("reject_v1", C.c_uint32),
+                ("abi_policy", C.c_uint32), ("expected_source_fingerprint", C.c_void_p)]
+
+
+class GlrtInfo(C.Structure):
+    """glacier_cuda_glrt_info."""
+    _fields_ = [("version", C.c_uint32), ("abi_policy", C.c_uint32), ("record_count", C.c_uint64),
+                ("data_offset", C.c_uint64), ("file_size", C.c_uint64),
+                ("source_fingerprint", C.c_uint8 * 32), ("abi_fingerprint", C.c_uint8 * 32)] + \
+               [(n, C.c_uint32) for n in ("dim", "hidden", "num_layers", "vocab", "num_heads", "head_dim",
+                                          "num_kv_heads", "tie_embeddings")] + \
+               [("rms_eps", C.c_float), ("rope_theta", C.c_float), ("mlp_layout", C.c_uint32),
+                ("group_size", C.c_uint32)]
+
+
+class GlrtEntry(C.Structure):
+    """glacier_cuda_glrt_entry: one decoded runtime-image record."""
+    _fields_ = [("layer_idx", C.c_uint32), ("tensor_kind", C.c_uint32), ("encoding", C.c_uint16),
+                ("packed_layout", C.c_uint16), ("role", C.c_uint16), ("pair_nibble_layout", C.c_uint16),
+                ("group_size", C.c_uint32), ("out_f", C.c_uint32), ("in_f", C.c_uint32),
+                ("payload_crc32", C.c_uint32), ("num_elements", C.c_uint64),
+                ("stream_offset", C.c_uint64 * 5), ("stream_len", C.c_uint64 * 5),
+                ("payload_digest", C.c_uint8 * 32)]
 
 
 class ModelConfigC(C.Structure):

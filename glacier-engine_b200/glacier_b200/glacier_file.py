@@ -25,7 +25,11 @@ REASONS = ("Ok", "TruncatedHeader", "BadMagic", "BadVersion", "BadHeaderSize", "
            "BadMetadata", "BadTensorKind", "BadPrecision", "BadPageId", "BadRowRange", "EmptyPage", "BadQuantGroup",
            "PageGeometryTooLarge", "UnsupportedPrecision", "BadPageGeometry", "NonContiguousPayload",
            "TruncatedPage", "TrailingBytes", "BadQuantPayload", "CrcMismatch", "SizeMismatch", "NoLayers",
-           "MissingTensor", "BadPayload")
+           "MissingTensor", "BadPayload", "BadRecordSize", "BadAlignment", "BadConfig", "HeaderCrcMismatch",
+           "IndexCrcMismatch", "LegacyVersionDisabled", "BadHeader", "BadBounds", "SourceFingerprintMismatch",
+           "AbiFingerprintMismatch", "BadEncoding", "BadPackedLayout", "BadRole", "BadPairNibbleLayout", "BadFlags",
+           "BadVersionedRecord", "MissingDigest", "BadTensorShape", "MissingScales", "OverlappingPayload",
+           "DuplicateRecord", "DigestMismatch")
 
 # TensorKind (format.zig:44-62) and StoredPrecision (core/precision.zig:9-16).
 TENSOR_KINDS = {0: "embedding", 1: "attn_q", 2: "attn_k", 3: "attn_v", 4: "attn_o", 5: "mlp_up", 6: "mlp_down",

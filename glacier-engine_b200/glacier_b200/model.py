@@ -224,6 +224,28 @@ class DeviceModel:
             raise
         return self
 
+    @classmethod
+    def from_runtime_image(cls, img, max_positions: int, scales_f16: bool = True) -> "DeviceModel":
+        """Loads an admitted RuntimeImage with the config its header carries (see runtime_image.load_model)."""
+        info = img.model_info()
+        cfg = dict(num_layers=info.num_layers, dim=info.dim, hidden=info.hidden, num_heads=info.num_heads,
+                   num_kv_heads=info.num_kv_heads, head_dim=info.head_dim, vocab=info.vocab,
+                   group=info.group_size, eps=info.rms_eps, theta=info.rope_theta)
+        self = cls.__new__(cls)
+        cfgc = _lib.ModelConfigC(cfg["num_layers"], cfg["dim"], cfg["hidden"], cfg["num_heads"],
+                                 cfg["num_kv_heads"], cfg["head_dim"], cfg["vocab"], cfg["group"], cfg["eps"],
+                                 cfg["theta"], max_positions, int(scales_f16))
+        self.cfg = cfg
+        self.max_positions = max_positions
+        self.h = _lib.handle(_lib.lib().glacier_cuda_model_create(C.byref(cfgc)))
+        try:
+            _lib.call("glacier_cuda_model_load_glrt", self.h, img._ptr, img.size, C.byref(img.options))
+            _lib.call("glacier_cuda_model_finalize", self.h)
+        except Exception:
+            self.close()
+            raise
+        return self
+
     def enable_tensor_parallel(self, rank: int, world: int, unique_id: bytes):
         """Joins the tensor-parallel group (blocks until every rank has joined)."""
         buf = (C.c_uint8 * 128).from_buffer_copy(unique_id)

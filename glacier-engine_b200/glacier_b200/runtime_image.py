@@ -1,0 +1,110 @@
+"""The prepared runtime image (`.glrt`) through the C ABI.
+
+``RuntimeImage`` admits an image as the reference's
+``MappedImage.openWithOptions`` does (src/model/runtime_image.zig:805-850);
+``load_model`` builds a device-resident model from it as
+``loader.loadPreparedWithOptions`` does (src/loader.zig:200-385).  Parsing,
+checksums, digests and the layout transforms all run in the library
+(csrc/runtime_image.cu).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+from . import _lib
+
+ENCODINGS = {0: "raw_f32", 1: "int4", 2: "pair_nibble"}
+PACKED_LAYOUTS = {0: "row_major", 1: "rows4_k16", 0xFFFF: "none"}
+ROLES = {0: "tensor", 1: "mlp_gate_up_pair"}
+STREAMS = ("packed_weights", "scales_f32", "scales_f16", "scales_f16_rows4", "raw")
+GLOBAL_LAYER = 0xFFFFFFFF
+
+
+class RuntimeImage:
+    """An admitted `.glrt` image held in host memory."""
+
+    def __init__(self, source, verify_crc: bool = True, verify_digest: bool = True, allow_v1: bool = True,
+                 abi_policy: str | None = None, expected_source_fingerprint: bytes | None = None):
+        if isinstance(source, (str, os.PathLike)):
+            self._buf = np.fromfile(os.fspath(source), dtype=np.uint8)
+        else:
+            self._buf = np.frombuffer(memoryview(source), np.uint8)
+        self._fp = None
+        if expected_source_fingerprint is not None:
+            if len(expected_source_fingerprint) != 32:
+                raise ValueError("a source fingerprint is 32 bytes")
+            self._fp = np.frombuffer(bytes(expected_source_fingerprint), np.uint8).copy()
+        policy = {None: 0, "portable": 1, "aarch64": 2}[abi_policy]
+        self.options = _lib.GlrtOptions(int(not verify_crc), int(not verify_digest), int(not allow_v1), policy,
+                                        self._fp.ctypes.data if self._fp is not None else None)
+        self.info = _lib.GlrtInfo()
+        _lib.call("glacier_cuda_glrt_open", self._ptr, self.size, C.byref(self.options), C.byref(self.info))
+
+    @property
+    def _ptr(self):
+        return self._buf.ctypes.data if self._buf.size else None
+
+    @property
+    def size(self) -> int:
+        return int(self._buf.size)
+
+    @property
+    def num_records(self) -> int:
+        return int(self.info.record_count)
+
+    def record(self, index: int) -> _lib.GlrtEntry:
+        e = _lib.GlrtEntry()
+        _lib.call("glacier_cuda_glrt_record", self._ptr, self.size, index, C.byref(e))
+        return e
+
+    def records(self) -> list[_lib.GlrtEntry]:
+        return [self.record(i) for i in range(self.num_records)]
+
+    def stream(self, rec: _lib.GlrtEntry, name: str) -> np.ndarray:
+        """The bytes of one stream of a record (a view into the image)."""
+        s = STREAMS.index(name)
+        off, n = rec.stream_offset[s], rec.stream_len[s]
+        return self._buf[off:off + n]
+
+    def model_info(self) -> _lib.GlrtInfo:
+        """Header config plus the prepared-model schema checks: MLP form and INT4 group."""
+        info = _lib.GlrtInfo()
+        _lib.call("glacier_cuda_glrt_model_info", self._ptr, self.size, C.byref(self.options), C.byref(info))
+        return info
+
+
+def load_model(source, max_positions: int, scales_f16: bool = True, **open_options):
+    """A finalized DeviceModel built from a `.glrt` image on the current device."""
+    from .model import DeviceModel
+    img = source if isinstance(source, RuntimeImage) else RuntimeImage(source, **open_options)
+    return DeviceModel.from_runtime_image(img, max_positions, scales_f16)
+
+
+def rows4_k16_to_row_major(packed: np.ndarray, out_f: int, in_f: int) -> np.ndarray:
+    src = np.ascontiguousarray(packed, np.uint8)
+    dst = np.empty(out_f * in_f // 2, np.uint8)
+    _lib.call("glacier_cuda_rows4_k16_to_row_major", src.ctypes.data, dst.ctypes.data, out_f, in_f)
+    return dst
+
+
+def rows4_scales_to_row_major(scales_f16: np.ndarray, out_f: int, groups_per_row: int) -> np.ndarray:
+    src = np.ascontiguousarray(scales_f16, np.float16).view(np.uint16)
+    dst = np.empty(out_f * groups_per_row, np.float32)
+    _lib.call("glacier_cuda_rows4_scales_to_row_major", src.ctypes.data, dst.ctypes.data, out_f, groups_per_row)
+    return dst
+
+
+def pair_nibble_split(pairs: np.ndarray, pair_scales_f16: np.ndarray, out_f: int, in_f: int, group: int):
+    """(gate packed, up packed, gate scales f32, up scales f32), all row-major."""
+    p = np.ascontiguousarray(pairs, np.uint8)
+    s = np.ascontiguousarray(pair_scales_f16, np.float16).view(np.uint16)
+    gate = np.empty(out_f * in_f // 2, np.uint8)
+    up = np.empty_like(gate)
+    gs = np.empty(out_f * in_f // group, np.float32)
+    us = np.empty_like(gs)
+    _lib.call("glacier_cuda_pair_nibble_split", p.ctypes.data, s.ctypes.data, out_f, in_f, group, gate.ctypes.data,
+              up.ctypes.data, gs.ctypes.data, us.ctypes.data)
+    return gate, up, gs, us

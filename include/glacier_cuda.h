@@ -368,7 +368,30 @@ enum glacier_cuda_format_reason {
   GLACIER_CUDA_FMT_SIZE_MISMATCH,          /* error.SizeMismatch (decode buffer) */
   GLACIER_CUDA_FMT_NO_LAYERS,              /* LoaderError.NoLayers */
   GLACIER_CUDA_FMT_MISSING_TENSOR,         /* LoaderError.MissingTensor */
-  GLACIER_CUDA_FMT_BAD_PAYLOAD             /* LoaderError.BadPayload */
+  GLACIER_CUDA_FMT_BAD_PAYLOAD,            /* LoaderError.BadPayload */
+  /* Prepared runtime image (src/model/runtime_image.zig) */
+  GLACIER_CUDA_FMT_BAD_RECORD_SIZE,        /* error.BadRecordSize */
+  GLACIER_CUDA_FMT_BAD_ALIGNMENT,          /* error.BadAlignment */
+  GLACIER_CUDA_FMT_BAD_CONFIG,             /* error.BadConfig */
+  GLACIER_CUDA_FMT_HEADER_CRC_MISMATCH,    /* error.HeaderCrcMismatch */
+  GLACIER_CUDA_FMT_INDEX_CRC_MISMATCH,     /* error.IndexCrcMismatch */
+  GLACIER_CUDA_FMT_LEGACY_VERSION_DISABLED, /* error.LegacyVersionDisabled */
+  GLACIER_CUDA_FMT_BAD_HEADER,             /* error.BadHeader */
+  GLACIER_CUDA_FMT_BAD_BOUNDS,             /* error.BadBounds */
+  GLACIER_CUDA_FMT_SOURCE_FINGERPRINT_MISMATCH, /* error.SourceFingerprintMismatch */
+  GLACIER_CUDA_FMT_ABI_FINGERPRINT_MISMATCH,    /* error.AbiFingerprintMismatch */
+  GLACIER_CUDA_FMT_BAD_ENCODING,           /* error.BadEncoding */
+  GLACIER_CUDA_FMT_BAD_PACKED_LAYOUT,      /* error.BadPackedLayout */
+  GLACIER_CUDA_FMT_BAD_ROLE,               /* error.BadRole */
+  GLACIER_CUDA_FMT_BAD_PAIR_NIBBLE_LAYOUT, /* error.BadPairNibbleLayout */
+  GLACIER_CUDA_FMT_BAD_FLAGS,              /* error.BadFlags */
+  GLACIER_CUDA_FMT_BAD_VERSIONED_RECORD,   /* error.BadVersionedRecord */
+  GLACIER_CUDA_FMT_MISSING_DIGEST,         /* error.MissingDigest */
+  GLACIER_CUDA_FMT_BAD_TENSOR_SHAPE,       /* error.BadTensorShape */
+  GLACIER_CUDA_FMT_MISSING_SCALES,         /* error.MissingScales */
+  GLACIER_CUDA_FMT_OVERLAPPING_PAYLOAD,    /* error.OverlappingPayload */
+  GLACIER_CUDA_FMT_DUPLICATE_RECORD,       /* error.DuplicateRecord */
+  GLACIER_CUDA_FMT_DIGEST_MISMATCH         /* error.DigestMismatch */
 };
 
 /* Reason for this thread's last GLACIER_CUDA_EFORMAT (0 after a success). */
@@ -430,6 +453,81 @@ int glacier_cuda_glacier_geometry(const uint8_t *bytes, uint64_t len, glacier_cu
  * output bias return GLACIER_CUDA_EUNSUPPORTED. */
 int glacier_cuda_model_load_glacier(glacier_cuda_model *model, const uint8_t *bytes, uint64_t len,
                                     int tie_word_embeddings);
+
+/* ------------------------------------------------------------------------
+ * The prepared runtime image `.glrt` (docs/RUNTIME_IMAGE.md;
+ * src/model/runtime_image.zig), v1 read-only and v2, from a host image of the
+ * whole file.  Admission follows MappedImage.openOwnedFileWithOptionsV1
+ * (runtime_image.zig:828-850): header CRC, config, ABI fingerprint, index CRC,
+ * every record's descriptor, bounds, identity and overlap, then each record's
+ * payload CRC and v2 SHA-256 digest (checked on all host cores; the failure
+ * reported is the one the reference's sequential walk meets first).
+ * ---------------------------------------------------------------------- */
+
+typedef struct glacier_cuda_glrt_options {
+  uint32_t skip_payload_crc;    /* 0 (default): verify every record's payload CRC */
+  uint32_t skip_payload_digest; /* 0 (default): verify every v2 record's SHA-256 digest */
+  uint32_t reject_v1;           /* 0 (default): v1 images are read */
+  uint32_t abi_policy;          /* 0: either preparation policy; 1: portable only; 2: AArch64 only */
+  const uint8_t *expected_source_fingerprint; /* 32 bytes, or NULL */
+} glacier_cuda_glrt_options;
+
+typedef struct glacier_cuda_glrt_info {
+  uint32_t version, abi_policy; /* abi_policy 1 portable, 2 AArch64 */
+  uint64_t record_count, data_offset, file_size;
+  uint8_t source_fingerprint[32], abi_fingerprint[32];
+  uint32_t dim, hidden, num_layers, vocab, num_heads, head_dim, num_kv_heads, tie_embeddings;
+  float rms_eps, rope_theta;
+  /* Filled by glacier_cuda_glrt_model_info only: */
+  uint32_t mlp_layout; /* 1 separate gate/up records, 2 one PairNibble record per layer */
+  uint32_t group_size; /* the INT4 group every quantized record shares */
+} glacier_cuda_glrt_info;
+
+/* One decoded record (runtime_image.zig Record, :308-430).  Streams in the
+ * order packed_weights, scales_f32, scales_f16, scales_f16_rows4, raw. */
+typedef struct glacier_cuda_glrt_entry {
+  uint32_t layer_idx, tensor_kind; /* layer 0xffffffff: global tensor */
+  uint16_t encoding;               /* 0 raw f32, 1 INT4, 2 PairNibble */
+  uint16_t packed_layout;          /* 0 row-major, 1 rows4_k16, 0xffff none */
+  uint16_t role;                   /* 0 tensor, 1 MLP gate/up pair */
+  uint16_t pair_nibble_layout;     /* 0 rows4_k16, 0xffff none */
+  uint32_t group_size, out_f, in_f, payload_crc32;
+  uint64_t num_elements;
+  uint64_t stream_offset[5], stream_len[5];
+  uint8_t payload_digest[32];
+} glacier_cuda_glrt_entry;
+
+/* opts may be NULL (defaults).  info may be NULL. */
+int glacier_cuda_glrt_open(const uint8_t *bytes, uint64_t len, const glacier_cuda_glrt_options *opts,
+                           glacier_cuda_glrt_info *info);
+
+/* One record of a structurally admitted image (payload content not re-verified). */
+int glacier_cuda_glrt_record(const uint8_t *bytes, uint64_t len, uint64_t index, glacier_cuda_glrt_entry *out);
+
+/* Admission plus the prepared-model schema (loader.zig validatePreparedConfig
+ * :618-652, validatePreparedRecordSet :656-714): the config to create the model
+ * with, its MLP form and its INT4 group. */
+int glacier_cuda_glrt_model_info(const uint8_t *bytes, uint64_t len, const glacier_cuda_glrt_options *opts,
+                                 glacier_cuda_glrt_info *info);
+
+/* Loads a prepared image into a model created with its config
+ * (loader.zig loadPreparedOwnedFileWithOptionsV1, :216-385).  rows4_k16 codes,
+ * rows4 fp16 scale grids and PairNibble records are put back in row-major
+ * order on the host, bit for bit; the embedding becomes an f32 table
+ * dequantized as dequantizeRow does, and a tied head reuses its INT4 data.
+ * The caller then runs glacier_cuda_model_finalize.  An attention output bias
+ * or mixed INT4 group sizes return GLACIER_CUDA_EUNSUPPORTED. */
+int glacier_cuda_model_load_glrt(glacier_cuda_model *model, const uint8_t *bytes, uint64_t len,
+                                 const glacier_cuda_glrt_options *opts);
+
+/* Layout transforms (int4_weights.zig): rows4_k16 nibble order -> row-major
+ * (packedNibbleIndex, :153-170); the [tile][group][lane] fp16 scale grid ->
+ * row-major f32 (withRows4F16Scales, :362-386); a PairNibble record -> its gate
+ * and up branches, row-major, with f32 scales (pairRows4K16, :251-346). */
+int glacier_cuda_rows4_k16_to_row_major(const uint8_t *src, uint8_t *dst, size_t out_f, size_t in_f);
+int glacier_cuda_rows4_scales_to_row_major(const uint16_t *src, float *dst, size_t out_f, size_t groups_per_row);
+int glacier_cuda_pair_nibble_split(const uint8_t *pairs, const uint16_t *pair_scales, size_t out_f, size_t in_f,
+                                   size_t group, uint8_t *gate, uint8_t *up, float *gate_scales, float *up_scales);
 
 #ifdef __cplusplus
 }
