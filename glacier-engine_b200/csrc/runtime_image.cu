@@ -464,15 +464,8 @@ int admit(const uint8_t* b, uint64_t len, const glacier_cuda_glrt_options* opts,
 
 // ------------------------------------------------------------- layouts ----
 uint8_t nib(const uint8_t* p, uint64_t i) { return (p[i >> 1] >> ((i & 1) * 4)) & 15; }
-void set_nib(uint8_t* p, uint64_t i, uint8_t v) {
-  uint8_t& d = p[i >> 1];
-  d = (i & 1) ? (uint8_t)((d & 0x0F) | v << 4) : (uint8_t)((d & 0xF0) | v);
-}
-
-// Physical nibble index of (row, col) in a rows4_k16 stream (int4_weights.zig:153-170).
-uint64_t rows4_index(uint64_t row, uint64_t col, uint64_t in_f) {
-  return (row / 4) * (4 * in_f) + (col / 16) * 64 + ((col % 16) / 4) * 16 + (row % 4) * 4 + col % 4;
-}
+// Physical nibble of (row, col) in a rows4_k16 stream (int4_weights.zig:153-170):
+//   (row/4)*(4*in_f) + (col/16)*64 + ((col%16)/4)*16 + (row%4)*4 + col%4.
 
 float half_to_float(uint16_t h) {
   const uint32_t sign = (uint32_t)(h & 0x8000) << 16, exp = (h >> 10) & 0x1F, man = h & 0x3FF;
@@ -497,18 +490,50 @@ float half_to_float(uint16_t h) {
   return f;
 }
 
+// Runs f(tile) for every 4-row tile, spread over the host's cores for large tensors.
+template <typename F>
+void for_each_tile(uint64_t tiles, uint64_t bytes_per_tile, const F& f) {
+  unsigned nt = std::max(1u, std::min(std::thread::hardware_concurrency(), 32u));
+  if (tiles * bytes_per_tile < (8ull << 20)) nt = 1;
+  std::atomic<uint64_t> next{0};
+  auto work = [&] {
+    for (uint64_t t0; (t0 = next.fetch_add(64)) < tiles;)
+      for (uint64_t t = t0; t < std::min(tiles, t0 + 64); ++t) f(t);
+  };
+  std::vector<std::thread> pool;
+  for (unsigned i = 1; i < nt; ++i) pool.emplace_back(work);
+  work();
+  for (auto& th : pool) th.join();
+}
+
+// rows4_k16 -> row-major as a byte permutation.  Inside a 4-row tile, the
+// 16-column block b is 32 contiguous bytes ordered [chunk c][row lane l][pair p]
+// (nibbles c*16 + l*4 + 2p and 2p+1), and that byte is exactly row l's byte for
+// columns 16b + 4c + 2p and +1 in row-major order.
+void rows4_to_row_major(const uint8_t* src, uint8_t* dst, uint64_t out_f, uint64_t in_f) {
+  const uint64_t rb = in_f / 2;
+  for_each_tile(out_f / 4, 4 * rb, [&](uint64_t t) {
+    const uint8_t* s = src + t * 4 * rb;
+    uint8_t* d = dst + t * 4 * rb;
+    for (uint64_t b = 0; b < in_f / 16; ++b)
+      for (int c = 0; c < 4; ++c)
+        for (int l = 0; l < 4; ++l) {
+          d[l * rb + b * 8 + c * 2] = s[b * 32 + c * 8 + l * 2];
+          d[l * rb + b * 8 + c * 2 + 1] = s[b * 32 + c * 8 + l * 2 + 1];
+        }
+  });
+}
+
 // One INT4 record as row-major codes and row-major f32 scales.  Scale choice:
 // the f32 stream when present (the portable numerics), else the row-major
 // fp16 mirror, else the rows4 fp16 grid; fp16 widens to f32 exactly.
 void int4_row_major(const Image& im, const Rec& x, std::vector<uint8_t>* packed, std::vector<float>* scales) {
   const uint8_t* pk = im.b + x.s[S_PACKED].off;
-  packed->assign(x.n / 2 + x.n % 2, 0);
-  if (x.layout == LAY_ROW_MAJOR) {
+  packed->resize(x.n / 2 + x.n % 2);
+  if (x.layout == LAY_ROW_MAJOR)
     memcpy(packed->data(), pk, packed->size());
-  } else {
-    for (uint64_t r = 0; r < x.out_f; ++r)
-      for (uint64_t c = 0; c < x.in_f; ++c) set_nib(packed->data(), r * x.in_f + c, nib(pk, rows4_index(r, c, x.in_f)));
-  }
+  else
+    rows4_to_row_major(pk, packed->data(), x.out_f, x.in_f);
   const uint64_t groups = x.n / x.group + (x.n % x.group != 0);
   scales->resize(groups);
   if (x.s[S_F32].len) {
@@ -525,19 +550,26 @@ void int4_row_major(const Image& im, const Rec& x, std::vector<uint8_t>* packed,
   }
 }
 
-// A PairNibble record split into row-major gate and up tensors: byte
-// rows4_index(r, c) holds gate in its low nibble and up in its high nibble,
-// and the scale grid is [tile][group][branch][lane] (int4_weights.zig:42-54, :322-331).
+// A PairNibble record split into row-major gate and up tensors: the byte at
+// coefficient position of (r, c) in rows4_k16 order holds gate in its low nibble and up
+// in its high nibble, and the scale grid is [tile][group][branch][lane]
+// (int4_weights.zig:42-54, :322-331).  Columns 2j and 2j+1 of a row sit in
+// adjacent pair bytes, so each output byte comes from two input bytes.
 void pair_split(const uint8_t* pairs, const uint8_t* scale_bits, uint64_t out_f, uint64_t in_f, uint64_t group,
                 uint8_t* gate, uint8_t* up, float* gate_scales, float* up_scales) {
-  memset(gate, 0, out_f * in_f / 2);
-  memset(up, 0, out_f * in_f / 2);
-  for (uint64_t r = 0; r < out_f; ++r)
-    for (uint64_t c = 0; c < in_f; ++c) {
-      const uint8_t p = pairs[rows4_index(r, c, in_f)];
-      set_nib(gate, r * in_f + c, p & 15);
-      set_nib(up, r * in_f + c, p >> 4);
-    }
+  const uint64_t rb = in_f / 2;
+  for_each_tile(out_f / 4, 4 * in_f, [&](uint64_t t) {
+    const uint8_t* s = pairs + t * 4 * in_f;
+    for (uint64_t b = 0; b < in_f / 16; ++b)
+      for (int c = 0; c < 4; ++c)
+        for (int l = 0; l < 4; ++l)
+          for (int p = 0; p < 2; ++p) {
+            const uint8_t lo = s[b * 64 + c * 16 + l * 4 + 2 * p], hi = s[b * 64 + c * 16 + l * 4 + 2 * p + 1];
+            const uint64_t o = (t * 4 + l) * rb + b * 8 + c * 2 + p;
+            gate[o] = (uint8_t)((lo & 15) | (hi & 15) << 4);
+            up[o] = (uint8_t)((lo >> 4) | (hi & 0xF0));
+          }
+  });
   const uint64_t per_row = in_f / group;
   for (uint64_t t = 0; t < out_f / 4; ++t)
     for (uint64_t g = 0; g < per_row; ++g)
@@ -735,9 +767,7 @@ int glacier_cuda_glrt_model_info(const uint8_t* bytes, uint64_t len, const glaci
 
 int glacier_cuda_rows4_k16_to_row_major(const uint8_t* src, uint8_t* dst, size_t out_f, size_t in_f) {
   GLC_REQUIRE(src && dst && out_f % 4 == 0 && in_f % 16 == 0, "rows4_k16: bad arguments");
-  memset(dst, 0, out_f * in_f / 2);
-  for (uint64_t r = 0; r < out_f; ++r)
-    for (uint64_t c = 0; c < in_f; ++c) set_nib(dst, r * in_f + c, nib(src, rows4_index(r, c, in_f)));
+  rows4_to_row_major(src, dst, out_f, in_f);
   return GLACIER_CUDA_OK;
 }
 
