@@ -505,9 +505,19 @@ int check_crc(const uint8_t* b, const glacier_cuda_page_entry& p, uint64_t index
 }
 
 // Schema and CRC of every page, spread over the host's cores; the first
-// failing page in page order is the one reported (validateAllPageCrcs walks
-// pages in order).
-int check_all_pages(const uint8_t* b, const Container& c) {
+// failing page in page order is the one reported.  validateAllPageCrcs checks
+// each page's quantized sub-header, then its CRC (format.zig:503-534).  The
+// model loader reads pages through readPage, which checks the CRC first
+// (:488-495), and a sub-header it cannot use fails the load as BadPayload
+// (loader.zig:1697-1700); `loader` selects that order and naming.
+bool schema_ok(const uint8_t* b, const glacier_cuda_page_entry& p) {
+  if (p.precision != P_INT8 && p.precision != P_INT4) return true;
+  const uint8_t* q = b + p.data_offset;
+  return !q[13] && !q[14] && !q[15] && rd<uint32_t>(q) == kQioMagic && rd<uint32_t>(q + 4) == p.row_end - p.row_start &&
+         rd<uint32_t>(q + 8) == p.quant_group && q[12] == (p.precision == P_INT8 ? 0 : 1);
+}
+
+int check_all_pages(const uint8_t* b, const Container& c, bool loader) {
   const uint64_t n = c.pages.size();
   unsigned nt = std::max(1u, std::min(std::thread::hardware_concurrency(), 64u));
   uint64_t bytes = 0;
@@ -517,17 +527,9 @@ int check_all_pages(const uint8_t* b, const Container& c) {
   auto work = [&] {
     for (uint64_t i; (i = next.fetch_add(1)) < n;) {
       const auto& p = c.pages[i];
-      bool bad = false;
-      if (p.precision == P_INT8 || p.precision == P_INT4) {
-        const uint8_t* q = b + p.data_offset;
-        bad = q[13] || q[14] || q[15] || rd<uint32_t>(q) != kQioMagic || rd<uint32_t>(q + 4) != p.row_end - p.row_start ||
-              rd<uint32_t>(q + 8) != p.quant_group || q[12] != (p.precision == P_INT8 ? 0 : 1);
-      }
-      if (!bad) bad = crc32_update(0, b + p.data_offset, p.data_len) != p.crc32;
-      if (bad) {
-        uint64_t cur = first_bad.load();
-        while (i < cur && !first_bad.compare_exchange_weak(cur, i)) {
-        }
+      if (schema_ok(b, p) && crc32_update(0, b + p.data_offset, p.data_len) == p.crc32) continue;
+      uint64_t cur = first_bad.load();
+      while (i < cur && !first_bad.compare_exchange_weak(cur, i)) {
       }
     }
   };
@@ -537,8 +539,14 @@ int check_all_pages(const uint8_t* b, const Container& c) {
   for (auto& t : pool) t.join();
   const uint64_t bad = first_bad.load();
   if (bad == UINT64_MAX) return GLACIER_CUDA_OK;
-  int rc = check_schema(b, c.pages[bad], bad);
-  return rc ? rc : check_crc(b, c.pages[bad], bad);
+  const auto& p = c.pages[bad];
+  if (loader) {
+    const int rc = check_crc(b, p, bad);
+    return rc ? rc : fail(GLACIER_CUDA_FMT_BAD_PAYLOAD, "page %llu: quantized sub-header does not match the entry",
+                          (unsigned long long)bad);
+  }
+  const int rc = check_schema(b, p, bad);
+  return rc ? rc : check_crc(b, p, bad);
 }
 
 // IEEE binary16 -> binary32, exact for every input (normal, subnormal, zero,
@@ -754,7 +762,7 @@ int glacier_cuda_glacier_open(const uint8_t* bytes, uint64_t len, glacier_cuda_f
 int glacier_cuda_glacier_validate_pages(const uint8_t* bytes, uint64_t len) {
   Container c;
   const int rc = admit(bytes, len, &c);
-  return rc ? rc : check_all_pages(bytes, c);
+  return rc ? rc : check_all_pages(bytes, c, false);
 }
 
 int glacier_cuda_glacier_page(const uint8_t* bytes, uint64_t len, uint64_t index, glacier_cuda_page_entry* out) {
@@ -806,7 +814,7 @@ int glacier_cuda_model_load_glacier(glacier_cuda_model* model, const uint8_t* by
   if (c.pages.empty()) return fail(GLACIER_CUDA_FMT_NO_LAYERS, "the container has no pages");
   // Every page is read through readPage in the reference loader, so every
   // payload's CRC (and quantized sub-header) is checked before any upload.
-  if ((rc = check_all_pages(bytes, c))) return rc;
+  if ((rc = check_all_pages(bytes, c, true))) return rc;
 
   glacier_cuda_file_geometry geo;
   geometry(c, &geo);

@@ -70,6 +70,17 @@ SIGNATURES = {
     "glacier_cuda_glacier_page_decode_f32": ([vp, C.c_uint64, C.c_uint64, vp, C.c_uint64], i32),
     "glacier_cuda_glacier_geometry": ([vp, C.c_uint64, vp], i32),
     "glacier_cuda_model_load_glacier": ([vp, vp, C.c_uint64, i32], i32),
+    "glacier_cuda_context_create": ([i32], vp),
+    "glacier_cuda_context_destroy": ([vp], None),
+    "glacier_cuda_context_stream": ([vp], vp),
+    "glacier_cuda_int4_weight_create": ([vp, vp, C.c_uint64, vp, C.c_uint64, u32, u32, u32], vp),
+    "glacier_cuda_int4_weight_destroy": ([vp], None),
+    "glacier_cuda_int4_matvec_dispatch": ([vp, vp, vp, C.c_uint64, vp, C.c_uint64], i32),
+    "glacier_cuda_int4_weight_read_output": ([vp, vp, C.c_uint64], i32),
+    "glacier_cuda_int4_weight_matvec": ([vp, vp, vp, vp, vp], i32),
+    "glacier_cuda_int4_weight_matmul": ([vp, vp, sz, vp, sz, sz, vp, vp], i32),
+    "glacier_cuda_int4_weight_lmhead_argmax": ([vp, vp, sz, vp, sz, vp, vp, vp, vp, vp], i32),
+    "glacier_cuda_all_finite_f32": ([vp, sz, vp, vp], i32),
     "glacier_cuda_glrt_open": ([vp, C.c_uint64, vp, vp], i32),
     "glacier_cuda_glrt_record": ([vp, C.c_uint64, C.c_uint64, vp], i32),
     "glacier_cuda_glrt_model_info": ([vp, C.c_uint64, vp, vp], i32),

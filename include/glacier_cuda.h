@@ -326,6 +326,55 @@ int glacier_cuda_model_profile(glacier_cuda_model *model, int enable);
 int glacier_cuda_model_profile_read(glacier_cuda_model *model, double *ms, uint64_t *regions, size_t kinds);
 
 /* ------------------------------------------------------------------------
+ * Persistent INT4 weight handles: the Metal persistent-weight API
+ * (src/backends/metal/backend.zig:571-595, shim.m:4005-4111, 5502-5624) on
+ * the B200 kernels.  A context binds one device and one stream.
+ * ---------------------------------------------------------------------- */
+
+typedef struct glacier_cuda_context glacier_cuda_context;
+typedef struct glacier_cuda_int4_weight glacier_cuda_int4_weight;
+
+glacier_cuda_context *glacier_cuda_context_create(int device_ordinal); /* NULL on error */
+void glacier_cuda_context_destroy(glacier_cuda_context *ctx);
+void *glacier_cuda_context_stream(glacier_cuda_context *ctx); /* its cudaStream_t */
+
+/* glacier_metal_int4_weight_create: host codes and f32 scales in, device copy
+ * out; NULL for a non-power-of-two group, an empty shape, more than 2^32
+ * elements, or too few packed bytes / scales. */
+glacier_cuda_int4_weight *glacier_cuda_int4_weight_create(glacier_cuda_context *ctx, const uint8_t *packed,
+                                                         uint64_t packed_bytes, const float *scales,
+                                                         uint64_t scale_count, uint32_t group_size,
+                                                         uint32_t in_features, uint32_t out_features);
+void glacier_cuda_int4_weight_destroy(glacier_cuda_int4_weight *weight);
+
+/* glacier_metal_int4_matvec_dispatch: host input, synchronous; the output stays in
+ * the handle until glacier_cuda_int4_weight_read_output copies it
+ * (glacier_metal_int4_weight_read_output).  Counts must cover the matrix. */
+int glacier_cuda_int4_matvec_dispatch(glacier_cuda_context *ctx, glacier_cuda_int4_weight *weight,
+                                      const float *input, uint64_t input_count, float *output,
+                                      uint64_t output_count);
+int glacier_cuda_int4_weight_read_output(glacier_cuda_int4_weight *weight, float *output, uint64_t output_count);
+
+/* Device-pointer forms on a caller stream. */
+int glacier_cuda_int4_weight_matvec(glacier_cuda_int4_weight *weight, const float *x, float *y, const float *bias,
+                                    void *stream);
+int glacier_cuda_int4_weight_matmul(glacier_cuda_int4_weight *weight, const float *x, size_t ldx, float *y,
+                                    size_t ldy, size_t batch, const float *bias, void *stream);
+
+/* LM head + argmaxEligible (sampling.zig:55-107) per row: device x [batch, in],
+ * optional eligibility words [batch][word_count], tokens / status / 24-byte
+ * results per row as glacier_cuda_argmax_eligible_f32 writes them.  status_out,
+ * results_out and logits_out may be NULL. */
+int glacier_cuda_int4_weight_lmhead_argmax(glacier_cuda_int4_weight *weight, const float *x, size_t batch,
+                                           const uint64_t *eligible_words, size_t word_count, int32_t *tokens_out,
+                                           int32_t *status_out, glacier_argmax_result *results_out,
+                                           float *logits_out, void *stream);
+
+/* glacier_all_finite_f32_neon (int4_neon.c:67-80): device *result = 1 when all
+ * `count` device values are finite, else 0. */
+int glacier_cuda_all_finite_f32(const float *values, size_t count, int32_t *result, void *stream);
+
+/* ------------------------------------------------------------------------
  * The portable .glacier container (docs/FORMAT_SPEC.md; src/model/format.zig,
  * src/model/qio.zig) read from a host image of the whole file (a read or an
  * mmap).  Host-only: none of these touches a GPU except

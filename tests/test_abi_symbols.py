@@ -33,3 +33,14 @@ def test_python_binding_covers_header():
 def test_version_callable_without_gpu():
     from glacier_b200 import _lib
     assert _lib.lib().glacier_cuda_version() >= 1
+
+
+def test_context_create_without_gpu_returns_null():
+    """On a host with no usable GPU the context constructor fails cleanly (NULL + message)."""
+    import torch
+    if torch.cuda.is_available():
+        return
+    from glacier_b200 import _lib
+    L = _lib.lib()
+    assert not L.glacier_cuda_context_create(0)
+    assert b"context_create" in L.glacier_cuda_last_error()

@@ -9,6 +9,8 @@ file path.  Images come from tests/glacier_writer.py.
 """
 import copy
 import json
+import struct
+import zlib
 
 import numpy as np
 import pytest
@@ -171,6 +173,14 @@ def test_loader_rejections():
     gf = GlacierFile(bytes(img))
     img[gf.page(gf.num_pages - 1).data_offset] ^= 1
     assert reason_name(load_error(img, cfg)) == "CrcMismatch"
+    # A sub-header that disagrees with its entry under a valid CRC: readPage passes it and the
+    # loader rejects the page (loader.zig:1697-1700).
+    img = gw.model_image(m)
+    last = gf.page(gf.num_pages - 1)
+    struct.pack_into("<I", img, last.data_offset + 8, 16)  # group 16 in the sub-header, 32 in the entry
+    payload = bytes(img[last.data_offset:last.data_offset + last.data_len])
+    struct.pack_into("<I", img, gf.info.page_index_offset + 64 * (gf.num_pages - 1) + 52, zlib.crc32(payload))
+    assert reason_name(load_error(img, cfg)) == "BadPayload"
     # A packed tensor whose non-final page splits a group (concatInt4Pages BadPayload).
     pk, sc = m.layers[0]["wq"]
     bad = gw.int4_pages(0, "attn_q", pk, sc, cfg.group)
