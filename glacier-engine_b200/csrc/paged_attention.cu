@@ -431,17 +431,20 @@ __global__ void __launch_bounds__(1024) attn_combine_kernel(const float* __restr
 }
 
 // fp32 output of one (lane, head) per CTA, for few lanes: warp 0 computes the
-// chunk weights, then the 8 warps take chunks s = warp, warp + 8, ... (each lane
-// 4 consecutive dims) and warp 0 adds the 8 partial sums in warp order.
-__global__ void __launch_bounds__(256) attn_combine_head_kernel(const float* __restrict__ part_o,
-                                                                const float* __restrict__ part_ml, int nsplit,
-                                                                int head_dim, int num_heads, float* __restrict__ out,
-                                                                size_t ldo, const int32_t* __restrict__ ctx_lens,
-                                                                int chunk) {
+// chunk weights, then the W warps take chunks s = warp, warp + W, ... (each lane
+// 4 consecutive dims) and warp 0 adds the W partial sums in warp order.  Many
+// chunks (one lane's context cut into one-page items) take W = 32, so each
+// warp has at most a few dependent partial loads in flight.
+template <int W>
+__global__ void __launch_bounds__(W * 32) attn_combine_head_kernel(const float* __restrict__ part_o,
+                                                                   const float* __restrict__ part_ml, int nsplit,
+                                                                   int head_dim, int num_heads,
+                                                                   float* __restrict__ out, size_t ldo,
+                                                                   const int32_t* __restrict__ ctx_lens, int chunk) {
   griddep_launch();
   griddep_wait();
   extern __shared__ float wts[];  // [nsplit]
-  __shared__ float4 part[8][32];
+  __shared__ float4 part[W][32];
   const int lane_id = blockIdx.x, head = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nsplit_lane = min(nsplit, (ctx_lens[lane_id] + chunk - 1) / chunk);
@@ -466,7 +469,7 @@ __global__ void __launch_bounds__(256) attn_combine_head_kernel(const float* __r
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   if (active) {
     const float* po = part_o + base * head_dim + 4 * lane;
-    for (int s = warp; s < nsplit_lane; s += 8) {
+    for (int s = warp; s < nsplit_lane; s += W) {
       const float4 v = *reinterpret_cast<const float4*>(po + (size_t)s * head_dim);
       const float w = wts[s];
       acc.x = fmaf(v.x, w, acc.x);
@@ -480,7 +483,7 @@ __global__ void __launch_bounds__(256) attn_combine_head_kernel(const float* __r
   if (warp == 0 && active) {
     float4 t = part[0][lane];
 #pragma unroll
-    for (int w = 1; w < 8; ++w) {
+    for (int w = 1; w < W; ++w) {
       const float4 q = part[w][lane];
       t.x += q.x;
       t.y += q.y;
@@ -499,7 +502,7 @@ size_t attention_workspace_floats(size_t lanes, size_t num_heads, size_t head_di
 }
 
 // Positions per work item: 512 (32 pages) unless that leaves fewer than two
-// items per warp of the persistent grid, then halved down to 32 (few lanes:
+// items per warp of the persistent grid, then halved down to 16 (few lanes:
 // short items spread one context over many SMs).  The combine keeps one weight
 // per (head, chunk) in 48 KB of shared memory, which bounds the chunk count.
 int attention_chunk(size_t lanes, size_t num_heads, size_t num_kv_heads, size_t max_ctx) {
@@ -507,7 +510,7 @@ int attention_chunk(size_t lanes, size_t num_heads, size_t num_kv_heads, size_t 
   const size_t max_split = (48 * 1024) / (sizeof(float) * num_heads);
   size_t chunk = 512;
   while (ceil_div(max_ctx, chunk) > max_split) chunk *= 2;
-  while (chunk > 32 && lanes * num_kv_heads * ceil_div(max_ctx, chunk) < 2 * warps &&
+  while (chunk > 16 && lanes * num_kv_heads * ceil_div(max_ctx, chunk) < 2 * warps &&
          ceil_div(max_ctx, chunk / 2) <= max_split)
     chunk /= 2;
   return (int)chunk;
@@ -644,9 +647,14 @@ int paged_attention(const float* q, size_t ldq, const float* pool, size_t page_f
     // lane); fp32 output with few lanes takes a block per (lane, head).
     if (!so.xs && lanes * num_heads < (size_t)sm_count()) {
       GLC_REQUIRE(head_dim <= 128 && head_dim % 4 == 0 && ldo % 4 == 0, "paged_attention: head_dim %zu", head_dim);
-      return launch_pdl(attn_combine_head_kernel, dim3((unsigned)lanes, (unsigned)num_heads), dim3(256),
-                        (size_t)nsplit * sizeof(float), stream, 1, (const float*)prm.part_o,
-                        (const float*)prm.part_ml, nsplit, (int)head_dim, (int)num_heads, out, ldo, ctx_lens, chunk);
+      const dim3 hgrid((unsigned)lanes, (unsigned)num_heads);
+      if (nsplit > 64)
+        return launch_pdl(attn_combine_head_kernel<32>, hgrid, dim3(1024), (size_t)nsplit * sizeof(float), stream, 1,
+                          (const float*)prm.part_o, (const float*)prm.part_ml, nsplit, (int)head_dim,
+                          (int)num_heads, out, ldo, ctx_lens, chunk);
+      return launch_pdl(attn_combine_head_kernel<8>, hgrid, dim3(256), (size_t)nsplit * sizeof(float), stream, 1,
+                        (const float*)prm.part_o, (const float*)prm.part_ml, nsplit, (int)head_dim, (int)num_heads,
+                        out, ldo, ctx_lens, chunk);
     }
     const size_t hpb = num_heads;
     // One warp per head for the weights (up to 32 warps), enough threads for 8 values each.
