@@ -763,3 +763,74 @@ GOR_EXPORT int gor_decode_token(const gor_model *m, float *pool, size_t page_flo
     free(buf);
     return 0;
 }
+
+/* ------------------------------------------------------------------------ */
+/* progressive_int4.zig: the Prism 1 + 1 + 2-bit decomposition (research     */
+/* track in the reference; scalar oracle only)                               */
+/* ------------------------------------------------------------------------ */
+
+/* progressive_int4.zig:1-12, :874-880 decomposeValidNibble: coarse 8*b3 - 4,
+ * middle 4*b2 - 2, fine (u & 3) - 1; their sum is u - 7.  tier 1, 2 or 4. */
+GOR_EXPORT int gor_prism_value(uint8_t nibble, int tier)
+{
+    const int coarse = (nibble & 8) ? 4 : -4;
+    const int middle = (nibble & 4) ? 2 : -2;
+    const int fine = (int)(nibble & 3) - 1;
+    return tier == 1 ? coarse : tier == 2 ? coarse + middle : coarse + middle + fine;
+}
+
+/* PackedPlanes.init (progressive_int4.zig:149-184): bit i % 8 of byte i / 8 in
+ * the coarse and middle planes, two-bit lane i % 4 of byte i / 4 in the fine
+ * plane; padding bits zero.  Planes are sized ceil(n/8), ceil(n/8), ceil(n/4). */
+GOR_EXPORT void gor_prism_split(const uint8_t *packed, size_t n, uint8_t *coarse1, uint8_t *middle1,
+                                uint8_t *fine2)
+{
+    memset(coarse1, 0, ceil_div(n, 8));
+    memset(middle1, 0, ceil_div(n, 8));
+    memset(fine2, 0, ceil_div(n, 4));
+    for (size_t i = 0; i < n; ++i) {
+        const uint8_t u = (packed[i / 2] >> ((i & 1) * 4)) & 15;
+        coarse1[i / 8] |= (uint8_t)(((u >> 3) & 1) << (i & 7));
+        middle1[i / 8] |= (uint8_t)(((u >> 2) & 1) << (i & 7));
+        fine2[i / 4] |= (uint8_t)((u & 3) << ((i & 3) * 2));
+    }
+}
+
+/* dotAll (progressive_int4.zig:730-755): one sequential pass, per element
+ * result += x * (tier_value * scale), multiply and add rounded separately. */
+GOR_EXPORT void gor_prism_dot_all(const float *x, const uint8_t *packed, const float *scales, size_t n,
+                                  size_t group, float out[3])
+{
+    float r1 = 0.f, r2 = 0.f, r4 = 0.f;
+    for (size_t i = 0; i < n; ++i) {
+        const uint8_t u = (packed[i / 2] >> ((i & 1) * 4)) & 15;
+        const float s = scales[i / group];
+        r1 += x[i] * ((float)gor_prism_value(u, 1) * s);
+        r2 += x[i] * ((float)gor_prism_value(u, 2) * s);
+        r4 += x[i] * ((float)gor_prism_value(u, 4) * s);
+    }
+    out[0] = r1;
+    out[1] = r2;
+    out[2] = r4;
+}
+
+/* dotP1/P2/P4PlanesUnchecked (progressive_int4.zig:1000-1041): the same
+ * order over the split planes; a tier reads only the planes it needs
+ * (middle1 may be NULL for tier 1, fine2 NULL below tier 4). */
+GOR_EXPORT float gor_prism_dot_planes(const float *x, int tier, const uint8_t *coarse1, const uint8_t *middle1,
+                                      const uint8_t *fine2, const float *scales, size_t n, size_t group)
+{
+    float r = 0.f;
+    for (size_t i = 0; i < n; ++i) {
+        const int c = (coarse1[i / 8] >> (i & 7)) & 1 ? 4 : -4;
+        int v = c;
+        if (tier >= 2) v += (middle1[i / 8] >> (i & 7)) & 1 ? 2 : -2;
+        if (tier == 4) {
+            const uint8_t u = (uint8_t)((((coarse1[i / 8] >> (i & 7)) & 1) << 3) |
+                                        (((middle1[i / 8] >> (i & 7)) & 1) << 2) | ((fine2[i / 4] >> ((i & 3) * 2)) & 3));
+            v = (int)u - 7; /* the integer is rebuilt before scaling (:1032-1035) */
+        }
+        r += x[i] * ((float)v * scales[i / group]);
+    }
+    return r;
+}

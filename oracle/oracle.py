@@ -69,6 +69,13 @@ def lib():
         L.gor_half_to_float.argtypes = [C.c_uint16]
         L.gor_half_to_float.restype = C.c_float
         L.gor_decode_token.argtypes = [vp, vp, sz, vp, sz, C.c_uint32, vp, vp]
+        L.gor_prism_value.argtypes = [C.c_uint8, C.c_int]
+        L.gor_prism_split.argtypes = [vp, sz, vp, vp, vp]
+        L.gor_prism_split.restype = None
+        L.gor_prism_dot_all.argtypes = [vp, vp, vp, sz, sz, vp]
+        L.gor_prism_dot_all.restype = None
+        L.gor_prism_dot_planes.argtypes = [vp, C.c_int, vp, vp, vp, vp, sz, sz]
+        L.gor_prism_dot_planes.restype = C.c_float
         _lib = L
     return _lib
 
@@ -356,3 +363,39 @@ class OracleModel:
         if rc:
             raise ValueError(f"decode_token failed: {rc}")
         return logits, hidden
+
+
+# --- Prism progressive INT4 (progressive_int4.zig; research track) -------------------
+
+def prism_value(nibble: int, tier: int) -> int:
+    """decomposeValidNibble(...).value(tier): tier 1 coarse, 2 coarse+middle, 4 exact u - 7."""
+    return int(lib().gor_prism_value(nibble, tier))
+
+
+def prism_split(packed, n: int):
+    """PackedPlanes.init: (coarse1, middle1, fine2) little-lane bit planes of n codes."""
+    pk = np.ascontiguousarray(packed, np.uint8)
+    c = np.zeros(-(-n // 8), np.uint8)
+    m = np.zeros(-(-n // 8), np.uint8)
+    f = np.zeros(-(-n // 4), np.uint8)
+    lib().gor_prism_split(_p(pk), n, _p(c) if c.size else None, _p(m) if m.size else None,
+                          _p(f) if f.size else None)
+    return c, m, f
+
+
+def prism_dot_all(x, packed, scales, group: int):
+    """dotAll: (p1, p2, p4) dot products in one sequential pass."""
+    xv = _f32(x)
+    out = np.zeros(3, np.float32)
+    lib().gor_prism_dot_all(_p(xv), _p(np.ascontiguousarray(packed, np.uint8)), _p(_f32(scales)), xv.size, group,
+                            _p(out))
+    return out
+
+
+def prism_dot_planes(x, tier: int, coarse1, middle1, fine2, scales, group: int) -> float:
+    """dotPlanesTier on the split planes (a tier reads only its planes)."""
+    xv = _f32(x)
+    arr = [None if a is None else np.ascontiguousarray(a, np.uint8) for a in (coarse1, middle1, fine2)]
+    ptr = [None if a is None or a.size == 0 else _p(a) for a in arr]
+    return float(lib().gor_prism_dot_planes(_p(xv), tier, ptr[0], ptr[1], ptr[2], _p(_f32(scales)), xv.size,
+                                            group))
