@@ -143,6 +143,44 @@ int reduce_splits(const float* part, size_t split_stride, int nsplit, float* y, 
 
 using namespace glacier;
 
+namespace glacier {
+
+// Workspace of the batched matmul: the split activations (padded to 16 rows)
+// and, when K is split, the per-split partial outputs.
+size_t matmul_workspace_bytes(size_t batch, size_t in_features, size_t out_features) {
+  const size_t np = ceil_div(batch < 16 ? 16 : batch, 16) * 16;
+  const int ns = gemm_splits(out_features, in_features);
+  const size_t part = ns > 1 ? (size_t)ns * batch * out_features * sizeof(float) : 0;
+  return ceil_div(gemm_split_bytes(np, in_features), 256) * 256 + part;
+}
+
+// y[batch, M] = x[batch, K] * dequant(W)^T + bias: the tcgen05 GEMM for up to
+// 128 rows when the weight qualifies, else the GEMV kernels.
+int int4_matmul(const Int4Weight& w, const float* x, size_t batch, const float* bias, float* y, void* workspace,
+                size_t workspace_bytes, cudaStream_t st) {
+  const size_t in_features = w.K, out_features = w.M;
+  if (!gemm_tc_supported(w) || batch > 128) return int4_linear(w, x, in_features, batch, bias, y, out_features, st);
+  const size_t np = ceil_div(batch < 16 ? 16 : batch, 16) * 16;
+  const size_t need = matmul_workspace_bytes(batch, in_features, out_features);
+  GLC_REQUIRE(workspace && workspace_bytes >= need, "int4_matmul: workspace of %zu bytes needed", need);
+  __half* xs = static_cast<__half*>(workspace);
+  float* xscale = reinterpret_cast<float*>(xs + 2 * np * in_features);
+  GLC_CHECK_CUDA(cudaMemsetAsync(xs, 0, 2 * np * in_features * sizeof(__half), st));
+  int rc = split_activation(x, in_features, batch, in_features, np, xs, xscale, st);
+  if (rc) return rc;
+  CUtensorMap map;
+  if ((rc = encode_split_map(&map, xs, np, in_features))) return rc;
+  const int ns = gemm_splits(out_features, in_features);
+  if (ns == 1) return gemm_int4_tc(w, map, xscale, batch, np, y, out_features, 1, 0, bias, st);
+  float* part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) +
+                                         ceil_div(gemm_split_bytes(np, in_features), 256) * 256);
+  const size_t stride = batch * out_features;
+  if ((rc = gemm_int4_tc(w, map, xscale, batch, np, part, out_features, ns, stride, bias, st))) return rc;
+  return reduce_splits(part, stride, ns, y, stride, st);
+}
+
+}  // namespace glacier
+
 extern "C" {
 
 const char* glacier_cuda_last_error(void) { return g_last_error; }
@@ -202,15 +240,8 @@ int glacier_cuda_int4_linear_q8(const float* x, size_t batch, const uint8_t* pac
   return int4_linear_q8(w, x, in_features, batch, bias, y, out_features, (cudaStream_t)stream);
 }
 
-static size_t matmul_ws_bytes(size_t batch, size_t in_features, size_t out_features) {
-  const size_t np = ceil_div(batch < 16 ? 16 : batch, 16) * 16;
-  const int ns = gemm_splits(out_features, in_features);
-  const size_t part = ns > 1 ? (size_t)ns * batch * out_features * sizeof(float) : 0;
-  return ceil_div(gemm_split_bytes(np, in_features), 256) * 256 + part;
-}
-
 size_t glacier_cuda_int4_matmul_workspace(size_t batch, size_t in_features, size_t out_features) {
-  return matmul_ws_bytes(batch, in_features, out_features);
+  return matmul_workspace_bytes(batch, in_features, out_features);
 }
 
 int glacier_cuda_int4_matmul_f16scale(const float* x, size_t batch, const uint8_t* packed, const uint16_t* scales,
@@ -224,27 +255,9 @@ int glacier_cuda_int4_matmul_f16scale(const float* x, size_t batch, const uint8_
   w.M = out_features;
   w.K = in_features;
   w.group = group_size;
-  int rc = int4_weight_prepare(w);
+  const int rc = int4_weight_prepare(w);
   if (rc) return rc;
-  cudaStream_t st = (cudaStream_t)stream;
-  if (!gemm_tc_supported(w) || batch > 128)
-    return int4_linear(w, x, in_features, batch, bias, y, out_features, st);
-  const size_t np = ceil_div(batch < 16 ? 16 : batch, 16) * 16;
-  const size_t need = matmul_ws_bytes(batch, in_features, out_features);
-  GLC_REQUIRE(workspace && workspace_bytes >= need, "int4_matmul: workspace of %zu bytes needed", need);
-  __half* xs = static_cast<__half*>(workspace);
-  float* xscale = reinterpret_cast<float*>(xs + 2 * np * in_features);
-  GLC_CHECK_CUDA(cudaMemsetAsync(xs, 0, 2 * np * in_features * sizeof(__half), st));
-  if ((rc = split_activation(x, in_features, batch, in_features, np, xs, xscale, st))) return rc;
-  CUtensorMap map;
-  if ((rc = encode_split_map(&map, xs, np, in_features))) return rc;
-  const int ns = gemm_splits(out_features, in_features);
-  if (ns == 1) return gemm_int4_tc(w, map, xscale, batch, np, y, out_features, 1, 0, bias, st);
-  float* part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) +
-                                         ceil_div(gemm_split_bytes(np, in_features), 256) * 256);
-  const size_t stride = batch * out_features;
-  if ((rc = gemm_int4_tc(w, map, xscale, batch, np, part, out_features, ns, stride, bias, st))) return rc;
-  return reduce_splits(part, stride, ns, y, stride, st);
+  return int4_matmul(w, x, batch, bias, y, workspace, workspace_bytes, (cudaStream_t)stream);
 }
 
 int glacier_cuda_rmsnorm_f32(const float* x, const float* weight, float eps, float* out, size_t batch, size_t dim,

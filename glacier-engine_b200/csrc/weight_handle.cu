@@ -18,6 +18,9 @@
 namespace glacier {
 
 size_t argmax_workspace_bytes(size_t batch, size_t n);
+size_t matmul_workspace_bytes(size_t batch, size_t in_features, size_t out_features);
+int int4_matmul(const Int4Weight& w, const float* x, size_t batch, const float* bias, float* y, void* workspace,
+                size_t workspace_bytes, cudaStream_t st);
 int argmax_rows(const float* logits, size_t ld, size_t batch, size_t n, const uint64_t* words, size_t word_count,
                 glacier_argmax_result* out, int32_t* tokens, int32_t* status, void* workspace, size_t ws_bytes,
                 cudaStream_t stream);
@@ -66,7 +69,7 @@ struct glacier_cuda_context {
 struct glacier_cuda_int4_weight {
   int device = 0;
   uint32_t in_f = 0, out_f = 0, group = 0;
-  DeviceBuffer packed, scales, input, output, logits, argmax_ws, argmax_out;
+  DeviceBuffer packed, scales, input, output, logits, argmax_ws, argmax_out, matmul_ws;
   Int4Weight w;
 };
 
@@ -113,14 +116,19 @@ void* glacier_cuda_context_stream(glacier_cuda_context* ctx) { return ctx ? (voi
 
 // glacier_metal_int4_weight_create_admitted (shim.m:4005-4061): the same
 // admission (power-of-two group, non-empty shape, at most 2^32 elements, enough
-// packed bytes and scales) and NULL on any failure.
-glacier_cuda_int4_weight* glacier_cuda_int4_weight_create(glacier_cuda_context* ctx, const uint8_t* packed,
-                                                         uint64_t packed_bytes, const float* scales,
-                                                         uint64_t scale_count, uint32_t group_size,
-                                                         uint32_t in_features, uint32_t out_features) {
+// packed bytes and scales) and NULL on any failure.  scale_dtype 0 keeps f32
+// scales (the portable numerics); 1 takes IEEE fp16 bit patterns, the
+// reference's fp16 scale cache (int4_weights.zig:348-358), which also lets
+// batches of 5 to 128 rows run on the tcgen05 GEMM.
+glacier_cuda_int4_weight* glacier_cuda_int4_weight_create_ex(glacier_cuda_context* ctx, const uint8_t* packed,
+                                                            uint64_t packed_bytes, const void* scales,
+                                                            uint64_t scale_count, uint32_t scale_dtype,
+                                                            uint32_t group_size, uint32_t in_features,
+                                                            uint32_t out_features) {
   if (!ctx || !packed || !scales || group_size == 0 || (group_size & (group_size - 1)) || !in_features ||
-      !out_features) {
-    set_error(GLACIER_CUDA_EINVAL, "int4_weight_create: null argument, empty shape or non-power-of-two group");
+      !out_features || scale_dtype > 1) {
+    set_error(GLACIER_CUDA_EINVAL,
+              "int4_weight_create: null argument, empty shape, non-power-of-two group or unknown scale type");
     return nullptr;
   }
   const uint64_t elements = (uint64_t)in_features * out_features;
@@ -138,7 +146,8 @@ glacier_cuda_int4_weight* glacier_cuda_int4_weight_create(glacier_cuda_context* 
   h->out_f = out_features;
   h->group = group_size;
   Int4Weight& w = h->w;
-  w.f16 = false;
+  const size_t esz = scale_dtype ? 2 : 4;
+  w.f16 = scale_dtype == 1;
   w.M = out_features;
   w.K = in_features;
   w.group = group_size;
@@ -146,15 +155,17 @@ glacier_cuda_int4_weight* glacier_cuda_int4_weight_create(glacier_cuda_context* 
   // row; otherwise groups straddle rows and the scales stay one flat array.
   const bool rows = in_features % group_size == 0;
   const size_t per_row = in_features / group_size;
-  const size_t stride = rows ? ceil_div(per_row * 4, (size_t)16) * 16 / 4 : 0;
-  const size_t scale_bytes = rows ? (size_t)out_features * stride * 4 : need_scales * 4;
+  const size_t stride = rows ? ceil_div(per_row * esz, (size_t)16) * 16 / esz : 0;
+  const size_t scale_bytes = rows ? (size_t)out_features * stride * esz : need_scales * esz;
   bool ok = !h->packed.ensure(need_packed) && !h->scales.ensure(scale_bytes) &&
             !h->input.ensure((size_t)in_features * 4) && !h->output.ensure((size_t)out_features * 4);
   if (ok) {
     ok = cudaMemcpy(h->packed.p, packed, need_packed, cudaMemcpyHostToDevice) == cudaSuccess;
     if (ok && rows) {
-      std::vector<float> staged((size_t)out_features * stride, 0.f);
-      for (size_t r = 0; r < out_features; ++r) memcpy(&staged[r * stride], scales + r * per_row, per_row * 4);
+      std::vector<uint8_t> staged((size_t)out_features * stride * esz, 0);
+      const uint8_t* src = static_cast<const uint8_t*>(scales);
+      for (size_t r = 0; r < out_features; ++r)
+        memcpy(&staged[r * stride * esz], src + r * per_row * esz, per_row * esz);
       ok = cudaMemcpy(h->scales.p, staged.data(), scale_bytes, cudaMemcpyHostToDevice) == cudaSuccess;
     } else if (ok) {
       ok = cudaMemcpy(h->scales.p, scales, scale_bytes, cudaMemcpyHostToDevice) == cudaSuccess;
@@ -175,6 +186,14 @@ glacier_cuda_int4_weight* glacier_cuda_int4_weight_create(glacier_cuda_context* 
     return nullptr;
   }
   return h;
+}
+
+glacier_cuda_int4_weight* glacier_cuda_int4_weight_create(glacier_cuda_context* ctx, const uint8_t* packed,
+                                                         uint64_t packed_bytes, const float* scales,
+                                                         uint64_t scale_count, uint32_t group_size,
+                                                         uint32_t in_features, uint32_t out_features) {
+  return glacier_cuda_int4_weight_create_ex(ctx, packed, packed_bytes, scales, scale_count, 0, group_size,
+                                            in_features, out_features);
 }
 
 void glacier_cuda_int4_weight_destroy(glacier_cuda_int4_weight* weight) {
@@ -227,7 +246,17 @@ int glacier_cuda_int4_weight_matvec(glacier_cuda_int4_weight* weight, const floa
 int glacier_cuda_int4_weight_matmul(glacier_cuda_int4_weight* weight, const float* x, size_t ldx, float* y,
                                     size_t ldy, size_t batch, const float* bias, void* stream) {
   GLC_REQUIRE(weight && ldx >= weight->in_f && ldy >= weight->out_f, "int4_weight_matmul: bad strides");
-  return int4_linear(weight->w, x, ldx, batch, bias, y, ldy, (cudaStream_t)stream);
+  const cudaStream_t s = (cudaStream_t)stream;
+  // Dense rows of more than four activations go to the tcgen05 GEMM when the
+  // weight qualifies (fp16 scales, groups 8/16/32); its workspace is the handle's.
+  if (batch > 4 && batch <= 128 && ldx == weight->in_f && ldy == weight->out_f && weight->w.tcg && weight->w.f16) {
+    int rc = bind(weight->device);
+    if (rc) return rc;
+    const size_t ws = matmul_workspace_bytes(batch, weight->in_f, weight->out_f);
+    if ((rc = weight->matmul_ws.ensure(ws))) return rc;
+    return int4_matmul(weight->w, x, batch, bias, y, weight->matmul_ws.p, ws, s);
+  }
+  return int4_linear(weight->w, x, ldx, batch, bias, y, ldy, s);
 }
 
 // The LM head and its greedy selection in one call: logits = x * W^T for each

@@ -74,6 +74,7 @@ SIGNATURES = {
     "glacier_cuda_context_destroy": ([vp], None),
     "glacier_cuda_context_stream": ([vp], vp),
     "glacier_cuda_int4_weight_create": ([vp, vp, C.c_uint64, vp, C.c_uint64, u32, u32, u32], vp),
+    "glacier_cuda_int4_weight_create_ex": ([vp, vp, C.c_uint64, vp, C.c_uint64, u32, u32, u32, u32], vp),
     "glacier_cuda_int4_weight_destroy": ([vp], None),
     "glacier_cuda_int4_matvec_dispatch": ([vp, vp, vp, C.c_uint64, vp, C.c_uint64], i32),
     "glacier_cuda_int4_weight_read_output": ([vp, vp, C.c_uint64], i32),

@@ -345,6 +345,14 @@ glacier_cuda_int4_weight *glacier_cuda_int4_weight_create(glacier_cuda_context *
                                                          uint64_t packed_bytes, const float *scales,
                                                          uint64_t scale_count, uint32_t group_size,
                                                          uint32_t in_features, uint32_t out_features);
+/* Same with a scale type: 0 f32 scales (as above), 1 IEEE fp16 bit patterns (the
+ * fp16 scale cache of int4_weights.zig:348-358); fp16 weights of groups 8/16/32
+ * run batches of 5..128 rows on the tcgen05 GEMM. */
+glacier_cuda_int4_weight *glacier_cuda_int4_weight_create_ex(glacier_cuda_context *ctx, const uint8_t *packed,
+                                                            uint64_t packed_bytes, const void *scales,
+                                                            uint64_t scale_count, uint32_t scale_dtype,
+                                                            uint32_t group_size, uint32_t in_features,
+                                                            uint32_t out_features);
 void glacier_cuda_int4_weight_destroy(glacier_cuda_int4_weight *weight);
 
 /* glacier_metal_int4_matvec_dispatch: host input, synchronous; the output stays in

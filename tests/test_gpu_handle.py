@@ -138,3 +138,31 @@ def test_all_finite(bad):
     assert r.item() == (1 if bad is None else 0)
     L.call("glacier_cuda_all_finite_f32", vd.data_ptr(), 0, r.data_ptr(), None)
     assert r.item() == 1
+
+
+@pytest.mark.parametrize("group", [8, 16, 32])
+def test_fp16_scale_handle_gemm_batches(ctx, group):
+    """scale_dtype 1: the fp16 scale cache; batches above four rows run the tcgen05 GEMM."""
+    L = lib()
+    rng = np.random.default_rng(group)
+    out_f, in_f = 2048, 1024
+    packed, scales = make(rng, out_f, in_f, group)
+    s16 = scales.astype(np.float16)
+    w = L.handle(L.lib().glacier_cuda_int4_weight_create_ex(ctx, p(packed), packed.size, p(s16.view(np.uint16)),
+                                                            s16.size, 1, group, in_f, out_f))
+    try:
+        ref_scales = s16.astype(np.float32)
+        for batch in (1, 3, 16, 64):
+            x = rng.standard_normal((batch, in_f)).astype(np.float32)
+            xd = torch.from_numpy(x).cuda()
+            yd = torch.zeros((batch, out_f), device="cuda")
+            L.call("glacier_cuda_int4_weight_matmul", w, xd.data_ptr(), in_f, yd.data_ptr(), out_f, batch, None,
+                   None)
+            torch.cuda.synchronize()
+            ref = oracle.linear_int4(x, packed, ref_scales, out_f, in_f, group)
+            assert max_rel_err(yd.cpu().numpy(), ref) <= REL_TOL, batch
+    finally:
+        L.lib().glacier_cuda_int4_weight_destroy(w)
+    # An unknown scale type is refused.
+    assert not L.lib().glacier_cuda_int4_weight_create_ex(ctx, p(packed), packed.size, p(scales), scales.size, 2,
+                                                          group, in_f, out_f)
