@@ -38,6 +38,14 @@ TENSOR_KINDS = {0: "embedding", 1: "attn_q", 2: "attn_k", 3: "attn_v", 4: "attn_
 PRECISIONS = {0: "fp16", 1: "bf16", 2: "int8", 3: "int4", 4: "int2", 5: "tri1p58", 6: "fp32"}
 
 
+def _map_file(path: str) -> np.ndarray:
+    """The file as a read-only byte array: a memory mapping (pages load on first
+    touch, nothing is copied), or an empty array for an empty file."""
+    if os.path.getsize(path) == 0:
+        return np.zeros(0, np.uint8)
+    return np.memmap(path, dtype=np.uint8, mode="r")
+
+
 def reason_name(err: _lib.GlacierCudaError) -> str:
     """The reference error name behind a GLACIER_CUDA_EFORMAT failure."""
     return REASONS[err.reason] if 0 <= err.reason < len(REASONS) else f"reason {err.reason}"
@@ -54,7 +62,7 @@ class GlacierFile:
     def __init__(self, source):
         if isinstance(source, (str, os.PathLike)):
             self.path = os.fspath(source)
-            self._buf = np.fromfile(self.path, dtype=np.uint8)
+            self._buf = _map_file(self.path)
         else:
             self.path = None
             self._buf = np.frombuffer(memoryview(source), np.uint8)

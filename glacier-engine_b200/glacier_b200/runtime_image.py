@@ -15,6 +15,7 @@ import os
 import numpy as np
 
 from . import _lib
+from .glacier_file import _map_file
 
 ENCODINGS = {0: "raw_f32", 1: "int4", 2: "pair_nibble"}
 PACKED_LAYOUTS = {0: "row_major", 1: "rows4_k16", 0xFFFF: "none"}
@@ -29,7 +30,7 @@ class RuntimeImage:
     def __init__(self, source, verify_crc: bool = True, verify_digest: bool = True, allow_v1: bool = True,
                  abi_policy: str | None = None, expected_source_fingerprint: bytes | None = None):
         if isinstance(source, (str, os.PathLike)):
-            self._buf = np.fromfile(os.fspath(source), dtype=np.uint8)
+            self._buf = _map_file(os.fspath(source))
         else:
             self._buf = np.frombuffer(memoryview(source), np.uint8)
         self._fp = None

@@ -276,3 +276,16 @@ def test_empty_container_has_no_layers():
     with pytest.raises(_lib.GlacierCudaError) as e:
         f.geometry()
     assert reason_name(e.value) == "NoLayers"
+
+
+def test_open_from_path_is_a_read_only_mapping(tmp_path):
+    """A path opens as a memory mapping of the file (nothing copied), like the reference's mmap reader."""
+    path = tmp_path / "m.glacier"
+    path.write_bytes(bytes(portable_container()))
+    f = GlacierFile(str(path))
+    assert isinstance(f._buf, np.memmap) and f.num_pages == 2
+    f.validate_pages()
+    (tmp_path / "empty.glacier").write_bytes(b"")
+    with pytest.raises(_lib.GlacierCudaError) as e:
+        GlacierFile(str(tmp_path / "empty.glacier"))
+    assert reason_name(e.value) == "TruncatedHeader"

@@ -282,3 +282,10 @@ def test_large_image_parallel_verification():
     with pytest.raises(_lib.GlacierCudaError) as e:
         RuntimeImage(bytes(bad), verify_crc=False)
     assert reason_name(e.value) == "DigestMismatch" and "record 7:" in str(e.value)
+
+
+def test_open_from_path(tmp_path):
+    path = tmp_path / "m.glrt"
+    path.write_bytes(bytes(image()))
+    r = RuntimeImage(str(path))
+    assert r.num_records == 15 and r.model_info().group_size == 16
