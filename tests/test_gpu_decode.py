@@ -75,6 +75,15 @@ def test_decode_7b_head_geometry():
     assert run_parity(cfg, lanes=2, prompt_len=18, new_tokens=4) >= 6
 
 
+@pytest.mark.parametrize("lanes", [1, 2])
+def test_decode_7b_layer_shapes_gemv_mode(lanes):
+    """One layer at the full 7B shapes in GEMV mode (cluster K-split GEMVs, the SwiGLU folded
+    into the 3584 x 18944 down projection)."""
+    from glacier_b200.model import ModelConfig
+    cfg = ModelConfig(num_layers=1, dim=3584, hidden=18944, num_heads=28, num_kv_heads=4, head_dim=128, vocab=2048)
+    assert run_parity(cfg, lanes=lanes, prompt_len=3, new_tokens=3) >= 3 * lanes
+
+
 def test_decode_05b_head_geometry_batch5():
     from glacier_b200.model import ModelConfig
     # five lanes: the tensor-core GEMV runs as a 4-row launch plus a 1-row launch
