@@ -765,6 +765,17 @@ int glacier_cuda_glacier_validate_pages(const uint8_t* bytes, uint64_t len) {
   return rc ? rc : check_all_pages(bytes, c, false);
 }
 
+int glacier_cuda_glacier_pages(const uint8_t* bytes, uint64_t len, glacier_cuda_page_entry* out, uint64_t capacity,
+                               uint64_t* count) {
+  GLC_REQUIRE(count && (out || capacity == 0), "glacier_pages: null output");
+  Container c;
+  const int rc = admit(bytes, len, &c);
+  if (rc) return rc;
+  *count = c.pages.size();
+  std::copy(c.pages.begin(), c.pages.begin() + std::min<uint64_t>(capacity, c.pages.size()), out);
+  return GLACIER_CUDA_OK;
+}
+
 int glacier_cuda_glacier_page(const uint8_t* bytes, uint64_t len, uint64_t index, glacier_cuda_page_entry* out) {
   GLC_REQUIRE(out, "glacier_page: null output");
   Container c;

@@ -728,31 +728,48 @@ int glacier_cuda_glrt_open(const uint8_t* bytes, uint64_t len, const glacier_cud
   return rc;
 }
 
-int glacier_cuda_glrt_record(const uint8_t* bytes, uint64_t len, uint64_t index, glacier_cuda_glrt_entry* out) {
-  GLC_REQUIRE(out, "glrt_record: null output");
+int glacier_cuda_glrt_records(const uint8_t* bytes, uint64_t len, glacier_cuda_glrt_entry* out, uint64_t capacity,
+                              uint64_t* count) {
+  GLC_REQUIRE(count && (out || capacity == 0), "glrt_records: null output");
   glacier_cuda_glrt_options o = {};
   o.skip_payload_crc = o.skip_payload_digest = 1;
   Image im;
   const int rc = admit(bytes, len, &o, &im);
   if (rc) return rc;
-  GLC_REQUIRE(index < im.recs.size(), "glrt_record: record %llu of %zu", (unsigned long long)index, im.recs.size());
-  const Rec& x = im.recs[index];
-  out->layer_idx = x.layer;
-  out->tensor_kind = x.kind;
-  out->encoding = x.encoding;
-  out->packed_layout = x.layout;
-  out->role = x.role;
-  out->pair_nibble_layout = x.pair_layout;
-  out->group_size = x.group;
-  out->out_f = x.out_f;
-  out->in_f = x.in_f;
-  out->payload_crc32 = x.crc;
-  out->num_elements = x.n;
-  for (int s = 0; s < kStreams; ++s) {
-    out->stream_offset[s] = x.s[s].off;
-    out->stream_len[s] = x.s[s].len;
+  *count = im.recs.size();
+  for (uint64_t i = 0; i < std::min<uint64_t>(capacity, im.recs.size()); ++i) {
+    const Rec& x = im.recs[i];
+    glacier_cuda_glrt_entry& e = out[i];
+    e.layer_idx = x.layer;
+    e.tensor_kind = x.kind;
+    e.encoding = x.encoding;
+    e.packed_layout = x.layout;
+    e.role = x.role;
+    e.pair_nibble_layout = x.pair_layout;
+    e.group_size = x.group;
+    e.out_f = x.out_f;
+    e.in_f = x.in_f;
+    e.payload_crc32 = x.crc;
+    e.num_elements = x.n;
+    for (int s = 0; s < kStreams; ++s) {
+      e.stream_offset[s] = x.s[s].off;
+      e.stream_len[s] = x.s[s].len;
+    }
+    memcpy(e.payload_digest, x.digest, 32);
   }
-  memcpy(out->payload_digest, x.digest, 32);
+  return GLACIER_CUDA_OK;
+}
+
+int glacier_cuda_glrt_record(const uint8_t* bytes, uint64_t len, uint64_t index, glacier_cuda_glrt_entry* out) {
+  GLC_REQUIRE(out, "glrt_record: null output");
+  std::vector<glacier_cuda_glrt_entry> all;
+  uint64_t n = 0;
+  int rc = glacier_cuda_glrt_records(bytes, len, nullptr, 0, &n);
+  if (rc) return rc;
+  GLC_REQUIRE(index < n, "glrt_record: record %llu of %llu", (unsigned long long)index, (unsigned long long)n);
+  all.resize(n);
+  if ((rc = glacier_cuda_glrt_records(bytes, len, all.data(), n, &n))) return rc;
+  *out = all[index];
   return GLACIER_CUDA_OK;
 }
 

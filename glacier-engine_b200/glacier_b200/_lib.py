@@ -67,6 +67,7 @@ SIGNATURES = {
     "glacier_cuda_glacier_open": ([vp, C.c_uint64, vp], i32),
     "glacier_cuda_glacier_validate_pages": ([vp, C.c_uint64], i32),
     "glacier_cuda_glacier_page": ([vp, C.c_uint64, C.c_uint64, vp], i32),
+    "glacier_cuda_glacier_pages": ([vp, C.c_uint64, vp, C.c_uint64, vp], i32),
     "glacier_cuda_glacier_page_decode_f32": ([vp, C.c_uint64, C.c_uint64, vp, C.c_uint64], i32),
     "glacier_cuda_glacier_geometry": ([vp, C.c_uint64, vp], i32),
     "glacier_cuda_model_load_glacier": ([vp, vp, C.c_uint64, i32], i32),
@@ -84,6 +85,7 @@ SIGNATURES = {
     "glacier_cuda_all_finite_f32": ([vp, sz, vp, vp], i32),
     "glacier_cuda_glrt_open": ([vp, C.c_uint64, vp, vp], i32),
     "glacier_cuda_glrt_record": ([vp, C.c_uint64, C.c_uint64, vp], i32),
+    "glacier_cuda_glrt_records": ([vp, C.c_uint64, vp, C.c_uint64, vp], i32),
     "glacier_cuda_glrt_model_info": ([vp, C.c_uint64, vp, vp], i32),
     "glacier_cuda_model_load_glrt": ([vp, vp, C.c_uint64, vp], i32),
     "glacier_cuda_rows4_k16_to_row_major": ([vp, vp, sz, sz], i32),

@@ -91,7 +91,12 @@ class GlacierFile:
         return e
 
     def pages(self) -> list[_lib.PageEntry]:
-        return [self.page(i) for i in range(self.num_pages)]
+        """Every page entry, from one admission of the image."""
+        n = self.num_pages
+        arr = (_lib.PageEntry * max(n, 1))()
+        count = C.c_uint64()
+        _lib.call("glacier_cuda_glacier_pages", self._ptr, self.size, arr, n, C.byref(count))
+        return list(arr[:count.value])
 
     def validate_pages(self) -> None:
         """Every quantized sub-header and CRC-32 (FileReader.validateAllPageCrcs)."""

@@ -62,7 +62,12 @@ class RuntimeImage:
         return e
 
     def records(self) -> list[_lib.GlrtEntry]:
-        return [self.record(i) for i in range(self.num_records)]
+        """Every record, from one structural admission of the image."""
+        n = self.num_records
+        arr = (_lib.GlrtEntry * max(n, 1))()
+        count = C.c_uint64()
+        _lib.call("glacier_cuda_glrt_records", self._ptr, self.size, arr, n, C.byref(count))
+        return list(arr[:count.value])
 
     def stream(self, rec: _lib.GlrtEntry, name: str) -> np.ndarray:
         """The bytes of one stream of a record (a view into the image)."""

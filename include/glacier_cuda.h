@@ -492,6 +492,11 @@ int glacier_cuda_glacier_validate_pages(const uint8_t *bytes, uint64_t len);
 
 int glacier_cuda_glacier_page(const uint8_t *bytes, uint64_t len, uint64_t index, glacier_cuda_page_entry *out);
 
+/* Every page entry in one admission: writes min(capacity, pages) entries and
+ * sets *count to the page count (capacity 0 queries the count). */
+int glacier_cuda_glacier_pages(const uint8_t *bytes, uint64_t len, glacier_cuda_page_entry *out, uint64_t capacity,
+                               uint64_t *count);
+
 /* One page's elements as f32 (FileReader.readPageDequant(f32), format.zig:638-662):
  * CRC first, then the quantized sub-header, then the decode.  count must equal
  * the page's element count. */
@@ -560,6 +565,11 @@ int glacier_cuda_glrt_open(const uint8_t *bytes, uint64_t len, const glacier_cud
 
 /* One record of a structurally admitted image (payload content not re-verified). */
 int glacier_cuda_glrt_record(const uint8_t *bytes, uint64_t len, uint64_t index, glacier_cuda_glrt_entry *out);
+
+/* Every record in one structural admission: writes min(capacity, records)
+ * entries and sets *count to the record count (capacity 0 queries the count). */
+int glacier_cuda_glrt_records(const uint8_t *bytes, uint64_t len, glacier_cuda_glrt_entry *out, uint64_t capacity,
+                              uint64_t *count);
 
 /* Admission plus the prepared-model schema (loader.zig validatePreparedConfig
  * :618-652, validatePreparedRecordSet :656-714): the config to create the model

@@ -6,6 +6,7 @@ error it must raise, the page-geometry and quant-sub-header rejections, the
 raw-page decode known answers, and the CRC check.  Images come from
 tests/glacier_writer.py (struct + zlib), a second implementation of the format.
 """
+import ctypes
 import json
 import struct
 import zlib
@@ -289,3 +290,13 @@ def test_open_from_path_is_a_read_only_mapping(tmp_path):
     with pytest.raises(_lib.GlacierCudaError) as e:
         GlacierFile(str(tmp_path / "empty.glacier"))
     assert reason_name(e.value) == "TruncatedHeader"
+
+
+def test_bulk_page_query_matches_single_queries():
+    f = GlacierFile(bytes(portable_container()))
+    bulk = f.pages()
+    assert [(e.page_id, e.data_offset, e.crc32) for e in bulk] == \
+        [(f.page(i).page_id, f.page(i).data_offset, f.page(i).crc32) for i in range(f.num_pages)]
+    count = ctypes.c_uint64()
+    _lib.call("glacier_cuda_glacier_pages", f._ptr, f.size, None, 0, ctypes.byref(count))
+    assert count.value == 2

@@ -289,3 +289,13 @@ def test_open_from_path(tmp_path):
     path.write_bytes(bytes(image()))
     r = RuntimeImage(str(path))
     assert r.num_records == 15 and r.model_info().group_size == 16
+
+
+def test_bulk_record_query_matches_single_queries():
+    r = RuntimeImage(bytes(image(mlp="pair")))
+    bulk = r.records()
+    assert len(bulk) == r.num_records
+    for i, e in enumerate(bulk):
+        one = r.record(i)
+        assert (e.layer_idx, e.tensor_kind, e.role, bytes(e.payload_digest)) == \
+            (one.layer_idx, one.tensor_kind, one.role, bytes(one.payload_digest))
