@@ -188,3 +188,81 @@ def load_model(source, max_positions: int, overrides: dict | None = None, scales
     ov.update(overrides or {})
     cfg = resolve_config(gf.geometry(), ov)
     return DeviceModel.from_glacier(gf, cfg, max_positions, scales_f16)
+
+
+class HostModel:
+    """A `.glacier` model's tensors as host arrays, in the layout glacier_b200.model
+    uses (layers of (packed, scales) INT4 pairs and f32 vectors), so that
+    TensorParallelShard can cut a real file into per-GPU shards the same way it
+    cuts a synthetic model.  Tensors are assembled as the library's loader does
+    (loader.zig:1214-1540): INT4 pages concatenated in page order with their
+    per-page scales, raw pages decoded to f32; an fp16 embedding stays fp16 and
+    any other embedding becomes f32 rows (INT4 rows as dequantizeRow forms
+    them); a tied head reuses the INT4 embedding."""
+
+    KINDS = {1: "wq", 2: "wk", 3: "wv", 4: "wo", 5: "wu", 6: "wd", 7: "wg", 8: "input_norm", 11: "post_attn_norm",
+             12: "bq", 13: "bk", 14: "bv"}
+
+    def __init__(self, gf: GlacierFile, cfg: dict):
+        from .model import ModelConfig
+        self.cfg = {k: cfg[k] for k in ("num_layers", "dim", "hidden", "num_heads", "num_kv_heads", "head_dim",
+                                        "vocab", "group", "eps", "theta")}
+        self.config = ModelConfig(**self.cfg)
+        gf.validate_pages()
+        groups: dict = {}
+        for e in gf.pages():
+            groups.setdefault((e.layer_idx, e.tensor_kind), []).append(e)
+        buf = gf._buf
+
+        def int4(pages):
+            g = pages[0].quant_group
+            packed, scales = [], []
+            for k, e in enumerate(pages):
+                n = e.row_end - e.row_start
+                if e.precision != 3 or e.quant_group != g or (k + 1 < len(pages) and (n % g or n % 2)):
+                    raise ValueError(f"page {e.page_id}: not an INT4 page of whole groups")
+                ng = -(-n // g)
+                base = e.data_offset + 16
+                scales.append(np.frombuffer(buf[base:base + 4 * ng].tobytes(), np.float32))
+                packed.append(np.asarray(buf[base + 4 * ng:base + 4 * ng + -(-n // 2)]))
+            return np.concatenate(packed).astype(np.uint8), np.concatenate(scales)
+
+        def raw(pages):
+            return np.concatenate([gf.decode_page(int(e.page_id)) for e in pages])
+
+        self.layers = [dict() for _ in range(self.cfg["num_layers"])]
+        for (layer, kind), pages in groups.items():
+            name = self.KINDS.get(kind)
+            if name is None or layer >= len(self.layers):
+                continue
+            self.layers[layer][name] = int4(pages) if name.startswith("w") else raw(pages)
+        for i, L in enumerate(self.layers):
+            for name in ("wq", "wk", "wv", "wo", "wg", "wu", "wd", "input_norm", "post_attn_norm"):
+                if name not in L:
+                    raise ValueError(f"layer {i} has no {name}")
+            for name in ("bq", "bk", "bv"):
+                L.setdefault(name, None)
+        self.final_norm = raw(groups[(0, 10)])
+        emb = groups[(0, 0)]
+        if all(e.precision == 0 for e in emb):  # fp16 pages: the file's bits
+            self.embedding = np.concatenate(
+                [np.frombuffer(buf[e.data_offset:e.data_offset + e.data_len].tobytes(), np.float16) for e in emb])
+        else:
+            self.embedding = raw(emb)
+        self.embedding = self.embedding.reshape(self.cfg["vocab"], self.cfg["dim"])
+        if cfg.get("tie_word_embeddings"):
+            self.lm_head = int4(emb)
+        else:
+            self.lm_head = int4(groups[(0, 9)])
+
+
+def host_model(source, overrides: dict | None = None) -> HostModel:
+    """The tensors of a `.glacier` model on the host (see HostModel), with the
+    same configuration resolution as load_model."""
+    gf = source if isinstance(source, GlacierFile) else GlacierFile(source)
+    ov = {}
+    if gf.path and os.path.exists(gf.path + ".json"):
+        with open(gf.path + ".json", "rb") as f:
+            ov.update(parse_sidecar(f.read()))
+    ov.update(overrides or {})
+    return HostModel(gf, resolve_config(gf.geometry(), ov))

@@ -197,8 +197,13 @@ class DeviceModel:
             self._int4(-1, _lib.W_LM_HEAD, *m.lm_head)
             fn = np.ascontiguousarray(m.final_norm, np.float32)
             _lib.call("glacier_cuda_model_load_f32", self.h, -1, _lib.N_FINAL, _p(fn), fn.size)
-            emb = np.ascontiguousarray(m.embedding, np.float16).view(np.uint16)
-            _lib.call("glacier_cuda_model_load_embedding_f16", self.h, _p(emb), emb.size)
+            if np.asarray(m.embedding).dtype == np.float32:
+                # f32 rows (a model file's INT4, bf16 or fp32 embedding): kept as they are.
+                emb32 = np.ascontiguousarray(m.embedding, np.float32)
+                _lib.call("glacier_cuda_model_load_embedding_f32", self.h, _p(emb32), emb32.size)
+            else:
+                emb = np.ascontiguousarray(m.embedding, np.float16).view(np.uint16)
+                _lib.call("glacier_cuda_model_load_embedding_f16", self.h, _p(emb), emb.size)
             _lib.call("glacier_cuda_model_finalize", self.h)
         except Exception:
             self.close()

@@ -300,3 +300,49 @@ def test_bulk_page_query_matches_single_queries():
     count = ctypes.c_uint64()
     _lib.call("glacier_cuda_glacier_pages", f._ptr, f.size, None, 0, ctypes.byref(count))
     assert count.value == 2
+
+
+@pytest.mark.parametrize("page_elems", [65536, 4096])
+def test_host_model_reassembles_the_written_model(page_elems):
+    """The host view of a file holds exactly the tensors it was written from, so tensor-parallel
+    shards cut from the file equal the shards cut from the model."""
+    from glacier_b200.glacier_file import host_model
+    from glacier_b200.model import ModelConfig, SyntheticModel, TensorParallelShard
+    cfg = ModelConfig(num_layers=2, dim=256, hidden=512, num_heads=8, num_kv_heads=2, head_dim=64, vocab=1000)
+    m = SyntheticModel(cfg, seed=9)
+    ov = dict(num_heads=8, num_kv_heads=2, head_dim=64, eps=cfg.eps, theta=cfg.theta)
+    hm = host_model(GlacierFile(bytes(gw.model_image(m, page_elems=page_elems))), ov)
+    assert hm.cfg == m.cfg
+    assert hm.embedding.dtype == np.float16 and np.array_equal(hm.embedding, m.embedding)
+    assert np.array_equal(hm.final_norm, m.final_norm)
+    for a, b in zip(hm.lm_head, m.lm_head):
+        assert np.array_equal(a, b)
+    for La, Lb in zip(hm.layers, m.layers):
+        for k, v in Lb.items():
+            if isinstance(v, tuple):
+                assert all(np.array_equal(x, y) for x, y in zip(La[k], v)), k
+            else:
+                assert np.array_equal(La[k], v), k
+    sa, sb = TensorParallelShard(hm, 1, 2), TensorParallelShard(m, 1, 2)
+    assert sa.cfg == sb.cfg
+    for La, Lb in zip(sa.layers, sb.layers):
+        for k, v in Lb.items():
+            if isinstance(v, tuple):
+                assert all(np.array_equal(x, y) for x, y in zip(La[k], v)), k
+
+
+def test_host_model_tied_int4_embedding():
+    from glacier_b200.glacier_file import host_model
+    from glacier_b200.model import ModelConfig, SyntheticModel
+    cfg = ModelConfig(num_layers=1, dim=64, hidden=128, num_heads=4, num_kv_heads=2, head_dim=16, vocab=32)
+    m = SyntheticModel(cfg, seed=2)
+    rng = np.random.default_rng(3)
+    packed = rng.integers(0, 256, 32 * 64 // 2, dtype=np.uint8)
+    scales = rng.random(32 * 64 // 32, dtype=np.float32)
+    img = gw.model_image(m, embedding=("int4", packed, scales), tie=True)
+    hm = host_model(GlacierFile(bytes(img)), dict(num_heads=4, num_kv_heads=2, head_dim=16,
+                                                   tie_word_embeddings=True))
+    q = np.stack([packed & 15, packed >> 4], -1).reshape(-1).astype(np.float32) - 7
+    assert hm.embedding.dtype == np.float32
+    assert np.array_equal(hm.embedding.ravel(), q * np.repeat(scales, 32))
+    assert np.array_equal(hm.lm_head[0], packed) and np.array_equal(hm.lm_head[1], scales)

@@ -201,3 +201,24 @@ def test_group_16_image():
     finally:
         fm.close()
         dm.close()
+
+
+def test_host_model_upload_matches_file_load():
+    """A model uploaded tensor by tensor from the host view of a file (the path tensor-parallel
+    shards take) decodes exactly like the library's own file loader, f32 embedding rows included."""
+    from glacier_b200.glacier_file import host_model
+    from glacier_b200.model import DeviceModel, SyntheticModel
+    cfg = small_cfg()
+    m = SyntheticModel(cfg, seed=27)
+    rng = np.random.default_rng(5)
+    packed = rng.integers(0, 256, cfg.vocab * cfg.dim // 2, dtype=np.uint8)
+    scales = (np.abs(rng.standard_normal(cfg.vocab * cfg.dim // cfg.group)) * 0.05).astype(np.float32)
+    gf = GlacierFile(bytes(gw.model_image(m, embedding=("int4", packed, scales), tie=True)))
+    ov = overrides(cfg, tie=True)
+    fm = load_model(gf, MAX_PAGES * 16, ov)
+    hm = DeviceModel(host_model(gf, ov), MAX_PAGES * 16)
+    try:
+        assert same_bits(decode_logits(fm), decode_logits(hm))
+    finally:
+        fm.close()
+        hm.close()
