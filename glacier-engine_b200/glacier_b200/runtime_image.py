@@ -114,3 +114,76 @@ def pair_nibble_split(pairs: np.ndarray, pair_scales_f16: np.ndarray, out_f: int
     _lib.call("glacier_cuda_pair_nibble_split", p.ctypes.data, s.ctypes.data, out_f, in_f, group, gate.ctypes.data,
               up.ctypes.data, gs.ctypes.data, us.ctypes.data)
     return gate, up, gs, us
+
+
+class HostModel:
+    """A prepared image's tensors as host arrays in glacier_b200.model's layout
+    (INT4 as row-major (packed, f32 scales), norms and biases as f32), put back
+    from rows4_k16 / rows4-grid / PairNibble form by the library's layout
+    transforms exactly as its loader does, so TensorParallelShard can cut a
+    prepared image into per-GPU shards.  The embedding becomes f32 rows
+    (dequantizeRow: code offset times the f32 group scale)."""
+
+    KINDS = {1: "wq", 2: "wk", 3: "wv", 4: "wo", 5: "wu", 6: "wd", 7: "wg", 8: "input_norm", 11: "post_attn_norm",
+             12: "bq", 13: "bk", 14: "bv"}
+
+    def __init__(self, img: RuntimeImage):
+        from .model import ModelConfig
+        i = img.model_info()
+        if i.group_size == 0:
+            raise ValueError("the image holds no INT4 records")
+        self.cfg = dict(num_layers=i.num_layers, dim=i.dim, hidden=i.hidden, num_heads=i.num_heads,
+                        num_kv_heads=i.num_kv_heads, head_dim=i.head_dim, vocab=i.vocab, group=i.group_size,
+                        eps=i.rms_eps, theta=i.rope_theta)
+        self.config = ModelConfig(**self.cfg)
+        recs = img.records()
+
+        def int4(r):
+            n = r.out_f * r.in_f
+            pk = img.stream(r, "packed_weights")
+            packed = np.array(pk) if r.packed_layout == 0 else rows4_k16_to_row_major(pk, r.out_f, r.in_f)
+            if img.stream(r, "scales_f32").size:
+                scales = np.frombuffer(img.stream(r, "scales_f32").tobytes(), np.float32).copy()
+            elif img.stream(r, "scales_f16").size:
+                scales = np.frombuffer(img.stream(r, "scales_f16").tobytes(), np.float16).astype(np.float32)
+            else:
+                grid = np.frombuffer(img.stream(r, "scales_f16_rows4").tobytes(), np.float16)
+                scales = rows4_scales_to_row_major(grid, r.out_f, r.in_f // r.group_size)
+            assert packed.size == -(-n // 2)
+            return packed, scales
+
+        def raw(r):
+            return np.frombuffer(img.stream(r, "raw").tobytes(), np.float32).copy()
+
+        self.layers = [dict(bq=None, bk=None, bv=None) for _ in range(i.num_layers)]
+        self.lm_head = None
+        emb = None
+        for r in recs:
+            if r.role == 1:  # PairNibble gate/up
+                grid = np.frombuffer(img.stream(r, "scales_f16_rows4").tobytes(), np.float16)
+                g, u, gs, us = pair_nibble_split(img.stream(r, "packed_weights"), grid, r.out_f, r.in_f,
+                                                 r.group_size)
+                self.layers[r.layer_idx]["wg"], self.layers[r.layer_idx]["wu"] = (g, gs), (u, us)
+            elif r.layer_idx == GLOBAL_LAYER:
+                if r.tensor_kind == 10:
+                    self.final_norm = raw(r)
+                elif r.tensor_kind == 0:
+                    emb = int4(r)
+                elif r.tensor_kind == 9:
+                    self.lm_head = int4(r)
+            else:
+                name = self.KINDS.get(r.tensor_kind)
+                if name is None:
+                    raise ValueError(f"record kind {r.tensor_kind} is not part of this decode path")
+                self.layers[r.layer_idx][name] = int4(r) if name.startswith("w") else raw(r)
+        packed, scales = emb
+        q = np.stack([packed & 15, packed >> 4], -1).reshape(-1)[: i.vocab * i.dim].astype(np.float32) - 7
+        self.embedding = (q * np.repeat(scales, i.group_size)[: q.size]).reshape(i.vocab, i.dim)
+        if i.tie_embeddings:
+            self.lm_head = emb
+
+
+def host_model(source, **open_options) -> HostModel:
+    """The tensors of a `.glrt` image on the host (see HostModel)."""
+    img = source if isinstance(source, RuntimeImage) else RuntimeImage(source, **open_options)
+    return HostModel(img)

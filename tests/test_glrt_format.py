@@ -299,3 +299,34 @@ def test_bulk_record_query_matches_single_queries():
         one = r.record(i)
         assert (e.layer_idx, e.tensor_kind, e.role, bytes(e.payload_digest)) == \
             (one.layer_idx, one.tensor_kind, one.role, bytes(one.payload_digest))
+
+
+@pytest.mark.parametrize("kw", [dict(), dict(layout="rows4_k16", scale_streams=("rows4",)), dict(mlp="pair"),
+                                dict(scale_streams=("f16",), tie=True)])
+def test_host_model_reassembles_the_prepared_model(kw):
+    """Every prepared layout comes back as the row-major tensors it was prepared from, so
+    tensor-parallel shards cut from the image equal the shards cut from the model."""
+    from glacier_b200.model import TensorParallelShard
+    from glacier_b200.runtime_image import host_model
+    kw = dict(kw)
+    tie = kw.pop("tie", False)
+    m, emb = small_model()
+    hm = host_model(bytes(gr.build(gr.model_records(m, emb, tie=tie, **kw), gr.model_cfg(m, tie=tie))))
+    assert {k: hm.cfg[k] for k in ("num_layers", "dim", "hidden", "num_heads", "num_kv_heads", "head_dim", "vocab",
+                                   "group")} == {k: m.cfg[k] for k in ("num_layers", "dim", "hidden", "num_heads",
+                                                                       "num_kv_heads", "head_dim", "vocab", "group")}
+    for La, Lb in zip(hm.layers, m.layers):
+        for k, v in Lb.items():
+            if isinstance(v, tuple):
+                assert all(np.array_equal(x, y) for x, y in zip(La[k], v)), k
+            else:
+                assert np.array_equal(La[k], v), k
+    q = np.stack([emb[0] & 15, emb[0] >> 4], -1).reshape(-1).astype(np.float32) - 7
+    assert np.array_equal(hm.embedding.ravel(), q * np.repeat(emb[1], 16))
+    head = emb if tie else m.lm_head
+    assert np.array_equal(hm.lm_head[0], head[0]) and np.array_equal(hm.lm_head[1], head[1])
+    sa, sb = TensorParallelShard(hm, 0, 2), TensorParallelShard(m, 0, 2)
+    for La, Lb in zip(sa.layers, sb.layers):
+        for k, v in Lb.items():
+            if isinstance(v, tuple):
+                assert all(np.array_equal(x, y) for x, y in zip(La[k], v)), k

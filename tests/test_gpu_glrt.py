@@ -101,3 +101,21 @@ def test_load_rejections():
     with pytest.raises(_lib.GlacierCudaError) as e:
         load_model(bytes(img), MAX_PAGES * 16)
     assert reason_name(e.value) == "CrcMismatch"
+
+
+def test_host_model_upload_matches_image_load():
+    """Uploading the host view of a prepared image (the tensor-parallel path) decodes exactly like
+    the library's own image loader, for a rows4_k16 PairNibble image with a tied head."""
+    from glacier_b200.model import DeviceModel
+    from glacier_b200.runtime_image import host_model
+    m, emb = model()
+    img = bytes(gr.build(gr.model_records(m, emb, tie=True, layout="rows4_k16", scale_streams=("rows4",),
+                                          mlp="pair"), gr.model_cfg(m, tie=True)))
+    fm = load_model(img, MAX_PAGES * 16)
+    hm = DeviceModel(host_model(img), MAX_PAGES * 16)
+    try:
+        a, b = decode_logits(fm), decode_logits(hm)
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    finally:
+        fm.close()
+        hm.close()
