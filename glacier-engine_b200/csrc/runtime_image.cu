@@ -269,9 +269,9 @@ int decode_record(const uint8_t* r, uint16_t version, uint64_t index, Rec* x) {
   x->layout = rd<uint16_t>(r + 10);
   if (x->layout > LAY_ROWS4 && x->layout != LAY_NONE)
     return fail(GLACIER_CUDA_FMT_BAD_PACKED_LAYOUT, "record %llu: packed layout %u", ix, x->layout);
-  x->role = version == 1 ? ROLE_TENSOR : rd<uint16_t>(r + 120);
+  x->role = version == 1 ? (uint16_t)ROLE_TENSOR : rd<uint16_t>(r + 120);
   if (x->role > ROLE_PAIR) return fail(GLACIER_CUDA_FMT_BAD_ROLE, "record %llu: role %u", ix, x->role);
-  x->pair_layout = version == 1 ? PAIR_NONE : rd<uint16_t>(r + 122);
+  x->pair_layout = version == 1 ? (uint16_t)PAIR_NONE : rd<uint16_t>(r + 122);
   if (x->pair_layout != PAIR_ROWS4 && x->pair_layout != PAIR_NONE)
     return fail(GLACIER_CUDA_FMT_BAD_PAIR_NIBBLE_LAYOUT, "record %llu: pair layout %u", ix, x->pair_layout);
   x->group = rd<uint32_t>(r + 12);
