@@ -45,6 +45,8 @@ def parse():
     ap.add_argument("--impl", choices=["glacier", "reference"], default="glacier")
     ap.add_argument("--lanes", type=int, default=64)
     ap.add_argument("--model", default="qwen2.5-7b")
+    ap.add_argument("--model-file", default=None,
+                    help="run on the tensors of a .glacier file or .glrt image instead of the preset's synthetic model")
     ap.add_argument("--ctx-min", type=int, default=256)
     ap.add_argument("--ctx-max", type=int, default=4096)
     ap.add_argument("--seed", type=int, default=2024)
@@ -205,13 +207,31 @@ def dist_setup():
 # reference arm
 # ---------------------------------------------------------------------------
 
+def bench_model(args):
+    """(ModelConfig, host model) the bench runs: the preset's synthetic model with
+    random weights, or the tensors of --model-file (a .glacier file or a .glrt
+    image, read through the library's own readers)."""
+    from glacier_b200.model import PRESETS, SyntheticModel
+    if getattr(args, "model_file", None):
+        if args.model_file.endswith(".glrt"):
+            from glacier_b200.runtime_image import host_model
+        else:
+            from glacier_b200.glacier_file import host_model
+        m = host_model(args.model_file)
+        return m.config, m
+    cfg = PRESETS[args.model]
+    return cfg, SyntheticModel(cfg, seed=args.seed, layers=args.layers)
+
+
+def data_label(args) -> str:
+    return f"model file {os.path.basename(args.model_file)}" if getattr(args, "model_file", None) else "synthetic"
+
+
 def run_reference(args):
     ws, rank, _ = dist_setup()
     if rank != 0:
         return
-    from glacier_b200.model import PRESETS, SyntheticModel
-    cfg = PRESETS[args.model]
-    model = SyntheticModel(cfg, seed=args.seed, layers=args.layers)
+    cfg, model = bench_model(args)
     ctxs = lane_contexts(args, args.lanes, 0)
     # warmup steps (untimed), then K timed steps; a step is one lane-token.
     time_cpu_oracle(model, ctxs, args, 0, max_tokens=max(1, args.warmup))
@@ -219,7 +239,7 @@ def run_reference(args):
     line = {
         "impl": "reference", "metric": METRIC, "value": r["value"], "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 / r["value"], "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": data_label(args),
         "config": {"workload": "7B decode, 64 lanes, ctx U[256,4096], greedy (config 5); reference step = "
                                "one lane-token on the host cores", "model": args.model, "lanes": args.lanes},
         "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
@@ -235,8 +255,7 @@ def run_reference(args):
 def run_glacier(args):
     import torch
     from glacier_b200 import _lib
-    from glacier_b200.model import (PRESETS, DecodeSession, DeviceModel, SyntheticModel, TensorParallelShard,
-                                    tp_unique_id)
+    from glacier_b200.model import DecodeSession, DeviceModel, TensorParallelShard, tp_unique_id
 
     ws, rank, local = dist_setup()
     torch.cuda.set_device(local)
@@ -247,7 +266,6 @@ def run_glacier(args):
     tp = args.tp
     if tp > 1 and tp != ws:
         raise SystemExit(f"--tp {tp} needs {tp} ranks (got {ws})")
-    cfg = PRESETS[args.model]
     lanes = args.lanes
     # Tensor parallel: every rank serves the same lanes; lane partition: each rank its own.
     ctxs = lane_contexts(args, lanes, 0 if tp > 1 else rank)
@@ -255,7 +273,7 @@ def run_glacier(args):
     max_pages = -(-(int(ctxs.max()) + total_steps + 1) // 16)
 
     t0 = time.time()
-    model = SyntheticModel(cfg, seed=args.seed, layers=args.layers)
+    cfg, model = bench_model(args)
     if tp > 1:
         dm = DeviceModel(TensorParallelShard(model, rank, tp), max_positions=max_pages * 16)
         uid = [tp_unique_id() if rank == 0 else None]
@@ -360,7 +378,7 @@ def run_glacier(args):
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": dev_ms / args.steps, "higher_is_better": True,
             "scaling": "strong" if tp > 1 else "weak", "vs_baseline": None,
-            "dtype": "f32 activations / int4 g32 weights (fp16 scales) / f32 KV", "data": "synthetic",
+            "dtype": "f32 activations / int4 g32 weights (fp16 scales) / f32 KV", "data": data_label(args),
             "config": {"workload": (f"7B decode, {lanes} lanes over {tp} tensor-parallel GPUs" if tp > 1 else
                                     "7B decode, 64 lanes per GPU") + ", ctx U[256,4096], greedy (BASELINE config 5)",
                        "model": args.model, "lanes_per_gpu": lanes if tp == 1 else lanes / tp,
@@ -580,13 +598,12 @@ def run_prefill(args):
     dense bf16 peak (useful FLOPs: 2 x 6.525e9 linear params x T + 200,704 x T^2 causal attention)."""
     import torch
     from glacier_b200 import _lib
-    from glacier_b200.model import PRESETS, DecodeSession, DeviceModel, SyntheticModel
+    from glacier_b200.model import DecodeSession, DeviceModel
     ws, rank, local = dist_setup()
     torch.cuda.set_device(local)
-    cfg = PRESETS[args.model]
     T = args.tokens
     max_pages = -(-(T + 1) // 16)
-    model = SyntheticModel(cfg, seed=args.seed, layers=args.layers)
+    cfg, model = bench_model(args)
     dm = DeviceModel(model, max_positions=max_pages * 16)
     sess = DecodeSession(dm, 1, max_pages, reserve_lanes=128)
     rng = np.random.default_rng(args.seed + rank)
@@ -630,7 +647,7 @@ def run_prefill(args):
         "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f32 activations / int4 g32 weights (fp16 scales) / f32 KV; fp16 hi/lo tensor-core operands",
-        "data": "synthetic", "config": {"workload": f"7B prefill, T={T} (BASELINE config 4)", "model": args.model,
+        "data": data_label(args), "config": {"workload": f"7B prefill, T={T} (BASELINE config 4)", "model": args.model,
                                         "tokens": T, "layers": nl, "chunk_rows": 128},
         "roofline": {"bound": "tensor", "achieved": flops / (ms / 1e3) / 1e12, "peak": peak / 1e12,
                      "unit": "TFLOP/s", "frac": flops / (ms / 1e3) / peak, "traffic": None,
