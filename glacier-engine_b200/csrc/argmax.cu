@@ -188,7 +188,11 @@ int argmax_rows(const float* logits, size_t ld, size_t batch, size_t n, const ui
 //    the first pass writes every partial slot that the second pass reads;
 //  * the first call on each device looks up the array's device address
 //    (cudaGetSymbolAddress) with that device current and caches it. Make that
-//    first call before any stream capture begins on the device.
+//    first call before any stream capture begins on the device. The cached
+//    address is valid while the CUDA context that first loaded the library on
+//    the device lives: after cudaDeviceReset the module is reloaded elsewhere,
+//    so a process that resets a device must not call this entry point on it
+//    again.
 // ---------------------------------------------------------------------------
 
 static_assert(GLACIER_CUDA_ARGMAX_NOALLOC_SCRATCH_BYTES % 256 == 0, "scratch size must keep 256-byte alignment");

@@ -90,8 +90,30 @@ void* device_symbol_address_raw(const void* symbol) {
   return cudaGetSymbolAddress(&p, symbol) == cudaSuccess ? p : nullptr;
 }
 
+// The attribute belongs to the kernel on one device, so the largest size set so
+// far is remembered per (kernel, current device) under a mutex: a process that
+// drives several GPUs sets it once on each, and concurrent host threads neither
+// race on the record nor skip the call.
 int allow_dynamic_smem(const void* kernel, int bytes) {
+  struct Entry {
+    const void* kernel;
+    int device;
+    int bytes;
+  };
+  static std::mutex mu;
+  static std::vector<Entry> done;
+  int dev = 0;
+  GLC_CHECK_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(mu);
+  Entry* e = nullptr;
+  for (auto& d : done)
+    if (d.kernel == kernel && d.device == dev) e = &d;
+  if (e && e->bytes >= bytes) return GLACIER_CUDA_OK;
   GLC_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  if (e)
+    e->bytes = bytes;
+  else
+    done.push_back({kernel, dev, bytes});
   return GLACIER_CUDA_OK;
 }
 

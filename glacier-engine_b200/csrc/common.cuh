@@ -61,14 +61,17 @@ int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base
 
 // Device address of a library __device__ variable on the current device, looked
 // up once per (variable, device) (host code cannot use the variable's name as
-// an address).  Returns nullptr on failure.
+// an address).  Returns nullptr on failure.  The cached address is valid while
+// the CUDA context that first loaded the library on that device lives (a
+// cudaDeviceReset reloads the module, and the library is not used after one).
 void* device_symbol_address_raw(const void* symbol);
 template <typename T>
 inline T* device_symbol_address(const T& symbol) {
   return static_cast<T*>(device_symbol_address_raw(static_cast<const void*>(&symbol)));
 }
 
-// Allows `bytes` of dynamic shared memory for `kernel` (once per kernel).
+// Allows `bytes` of dynamic shared memory for `kernel` on the current device
+// (the attribute is set once per kernel, device and larger size).
 int allow_dynamic_smem(const void* kernel, int bytes);
 
 // Launch with programmatic dependent launch allowed (and an optional cluster

@@ -544,11 +544,9 @@ int add_rmsnorm(const float* a, size_t lda, const float* b, size_t ldb, size_t b
   const size_t slice = ((ceil_div(dim, (size_t)cl)) + 7) & ~(size_t)7;
   const size_t smem = slice * sizeof(float);
   GLC_REQUIRE(smem <= 160 * 1024, "rmsnorm: dim %zu too large", dim);
-  static size_t attr = 0;
-  if (smem > 48 * 1024 && attr < smem) {
+  if (smem > 48 * 1024) {
     const int rc = allow_dynamic_smem((const void*)add_rmsnorm_kernel, (int)smem);
     if (rc) return rc;
-    attr = smem;
   }
   int d = (int)dim;
   void* args[] = {(void*)&a, &lda, (void*)&b, &ldb, &b_split_stride, &nb, &residual, &ldr, (void*)&w, &eps, &out,
@@ -576,11 +574,9 @@ int silu_mul(const float* gate, const float* up, size_t ld_in, float* out, size_
   const size_t slice = ((ceil_div(n, (size_t)cl)) + 7) & ~(size_t)7;
   const size_t smem = slice * sizeof(float);
   GLC_REQUIRE(smem <= 160 * 1024, "silu_mul: row %zu too long", n);
-  static size_t attr = 0;
-  if (smem > 48 * 1024 && attr < smem) {
+  if (smem > 48 * 1024) {
     const int rc = allow_dynamic_smem((const void*)silu_mul_split_kernel, (int)smem);
     if (rc) return rc;
-    attr = smem;
   }
   int nn = (int)n;
   void* args[] = {(void*)&gate, (void*)&up, &ld_in, &out, &ld_out, &so, &nn};

@@ -627,12 +627,9 @@ int gemm_int4_tc(const Int4Weight& w, const CUtensorMap& xmap, const float* xsca
   GLC_REQUIRE(smem <= 227 * 1024, "int4 gemm: %zu bytes of shared memory", smem);
   const void* kern = per32 == 1 ? (const void*)gemm_tc_kernel<1>
                      : per32 == 2 ? (const void*)gemm_tc_kernel<2> : (const void*)gemm_tc_kernel<4>;
-  static size_t attr[3] = {0, 0, 0};
-  size_t& done = attr[per32 == 1 ? 0 : per32 == 2 ? 1 : 2];
-  if (done < smem) {
+  {
     const int rc = allow_dynamic_smem(kern, (int)smem);
     if (rc) return rc;
-    done = smem;
   }
   int* err = device_symbol_address(g_gemm_error);
   GLC_REQUIRE(err != nullptr, "int4 gemm: device status word unavailable");

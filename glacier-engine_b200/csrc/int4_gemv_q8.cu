@@ -333,11 +333,7 @@ int launch_q8(const uint8_t* packed, const ScaleT* scales, const float* x, size_
                       2 * kQ8Stages * sizeof(uint64_t);
   GLC_REQUIRE(smem <= 227 * 1024, "int4 q8 gemv: %zu bytes of shared memory", smem);
   auto kern = gemv_q8_kernel<ScaleT, T, KP>;
-  static size_t done = 0;
-  if (done < smem) {
-    if ((rc = allow_dynamic_smem((const void*)kern, (int)smem))) return rc;
-    done = smem;
-  }
+  if ((rc = allow_dynamic_smem((const void*)kern, (int)smem))) return rc;
   int* err = device_symbol_address(g_gemv_q8_error);
   GLC_REQUIRE(err != nullptr, "int4 q8 gemv: device status word unavailable");
   Q8Params prm{x, ldx, bias, y, ldy, (int)M, (int)K, (int)batch, (int)ceil_div(K, 256), err};

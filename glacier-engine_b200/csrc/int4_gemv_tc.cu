@@ -318,13 +318,8 @@ int launch_gemv_tc(const Int4Weight& w, const float* x, const float* xu, size_t 
                       4 * kRows * sizeof(float) + 2 * kStages * sizeof(uint64_t);
   GLC_REQUIRE(smem <= 200 * 1024, "int4 gemv: K slice too long for shared memory (K=%zu)", K);
   auto kern = gemv_tc_kernel<ScaleT>;
-  static size_t attr_bytes[2] = {0, 0};
-  size_t& done = attr_bytes[sizeof(ScaleT) == 2 ? 0 : 1];
-  if (done < smem) {
-    rc = allow_dynamic_smem((const void*)kern, (int)smem);
-    if (rc) return rc;
-    done = smem;
-  }
+  rc = allow_dynamic_smem((const void*)kern, (int)smem);
+  if (rc) return rc;
   int* err = nullptr;
   GLC_CHECK_CUDA(cudaGetSymbolAddress((void**)&err, g_gemv_error));
   GemvParams prm{x, ldx, bias, y, ldy, (int)M, (int)K, (int)batch, stages, spc, err, xu};

@@ -611,20 +611,7 @@ int paged_attention(const float* q, size_t ldq, const float* pool, size_t page_f
   GLC_ATTN_CASE(64, 5) GLC_ATTN_CASE(64, 6) GLC_ATTN_CASE(64, 7) GLC_ATTN_CASE(64, 8)
 #undef GLC_ATTN_CASE
   GLC_REQUIRE(kern != nullptr, "paged_attention: no kernel for head_dim %zu / group %zu", head_dim, group);
-  {
-    // The shared-memory attribute is per kernel instance; set it once per instance.
-    static const void* ready[16] = {};
-    bool seen = false;
-    for (const void* r : ready) seen |= r == (const void*)kern;
-    if (!seen) {
-      if ((rc = allow_dynamic_smem((const void*)kern, (int)smem))) return rc;
-      for (auto& r : ready)
-        if (!r) {
-          r = (const void*)kern;
-          break;
-        }
-    }
-  }
+  if ((rc = allow_dynamic_smem((const void*)kern, (int)smem))) return rc;
   int* err = device_symbol_address(g_attn_error);
   GLC_REQUIRE(err != nullptr, "paged_attention: device status word unavailable");
   const size_t items = lanes * num_kv_heads * (size_t)nsplit;

@@ -242,6 +242,11 @@ class HostModel:
                     raise ValueError(f"layer {i} has no {name}")
             for name in ("bq", "bk", "bv"):
                 L.setdefault(name, None)
+        for key, what in (((0, 10), "final norm"), ((0, 0), "embedding")):
+            if key not in groups:
+                raise ValueError(f"the model has no {what} tensor")
+        if not cfg.get("tie_word_embeddings") and (0, 9) not in groups:
+            raise ValueError("the model has no LM head tensor and does not tie it to the embedding")
         self.final_norm = raw(groups[(0, 10)])
         emb = groups[(0, 0)]
         if all(e.precision == 0 for e in emb):  # fp16 pages: the file's bits

@@ -157,8 +157,11 @@ class HostModel:
 
         self.layers = [dict(bq=None, bk=None, bv=None) for _ in range(i.num_layers)]
         self.lm_head = None
+        self.final_norm = None
         emb = None
         for r in recs:
+            if r.layer_idx != GLOBAL_LAYER and not 0 <= r.layer_idx < i.num_layers:
+                raise ValueError(f"record of layer {r.layer_idx} in an image of {i.num_layers} layers")
             if r.role == 1:  # PairNibble gate/up
                 grid = np.frombuffer(img.stream(r, "scales_f16_rows4").tobytes(), np.float16)
                 g, u, gs, us = pair_nibble_split(img.stream(r, "packed_weights"), grid, r.out_f, r.in_f,
@@ -176,6 +179,16 @@ class HostModel:
                 if name is None:
                     raise ValueError(f"record kind {r.tensor_kind} is not part of this decode path")
                 self.layers[r.layer_idx][name] = int4(r) if name.startswith("w") else raw(r)
+        for n, L in enumerate(self.layers):
+            for name in ("wq", "wk", "wv", "wo", "wg", "wu", "wd", "input_norm", "post_attn_norm"):
+                if name not in L:
+                    raise ValueError(f"layer {n} has no {name}")
+        if emb is None:
+            raise ValueError("the image has no embedding record")
+        if getattr(self, "final_norm", None) is None:
+            raise ValueError("the image has no final norm record")
+        if self.lm_head is None and not i.tie_embeddings:
+            raise ValueError("the image has no LM head record and does not tie it to the embedding")
         packed, scales = emb
         q = np.stack([packed & 15, packed >> 4], -1).reshape(-1)[: i.vocab * i.dim].astype(np.float32) - 7
         self.embedding = (q * np.repeat(scales, i.group_size)[: q.size]).reshape(i.vocab, i.dim)

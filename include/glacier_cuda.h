@@ -194,7 +194,9 @@ int glacier_cuda_argmax_eligible_f32(const float *logits, size_t batch, size_t n
  * larger calls return GLACIER_CUDA_EINVAL before any launch.  All calls on a device share the
  * array: calls that overlap on the GPU race and must be ordered by the caller.  The first call on
  * a device looks up the array's address with that device current; make it before any stream
- * capture starts. */
+ * capture starts.  That address is kept for the rest of the process: it stays valid while the
+ * CUDA context that first loaded the library on the device lives, so a process that resets the
+ * device (cudaDeviceReset) must not call this entry point on it again. */
 #define GLACIER_CUDA_ARGMAX_NOALLOC_SCRATCH_BYTES 65536
 int glacier_cuda_argmax_eligible_f32_noalloc(const float *logits, size_t batch, size_t n,
                                              const uint64_t *words, size_t word_count, int32_t *tokens,

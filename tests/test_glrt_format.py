@@ -330,3 +330,19 @@ def test_host_model_reassembles_the_prepared_model(kw):
         for k, v in Lb.items():
             if isinstance(v, tuple):
                 assert all(np.array_equal(x, y) for x, y in zip(La[k], v)), k
+
+
+@pytest.mark.parametrize("drop", [("layer", "mlp_down"), ("global", "final_norm"), ("global", "embedding"),
+                                  ("global", "lm_head")])
+def test_host_model_rejects_an_incomplete_image(drop):
+    """An image missing a tensor the decode path needs ends in a ValueError naming the gap
+    (from the reader's schema check or from HostModel), never in a later TypeError or KeyError."""
+    from glacier_b200.runtime_image import host_model
+    m, emb = small_model()
+    recs = gr.model_records(m, emb)
+    want = gr.gw.KIND[drop[1]]
+    keep = [r for r in recs if not (r.kind == want and ((r.layer == gr.GLOBAL) == (drop[0] == "global"))
+                                    and (drop[0] == "global" or r.layer == 0))]
+    assert len(keep) == len(recs) - 1
+    with pytest.raises(ValueError):
+        host_model(bytes(gr.build(keep, gr.model_cfg(m))))
