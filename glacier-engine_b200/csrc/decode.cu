@@ -645,6 +645,7 @@ static int step_impl(glacier_cuda_model* m, glacier_cuda_kv* kv, size_t lanes, c
   const int so_ = m->tp_comm ? 1 : so_gemm, sd = m->tp_comm ? 1 : sd_gemm;
   auto tp_reduce = [&](float* buf, int nsplit) -> int {
     int r;
+    mark(GLACIER_CUDA_STEP_ALL_REDUCE);
     if (nsplit > 1 && (r = reduce_splits(buf, B * D, nsplit, buf, B * D, st))) return r;
     return tp_all_reduce(m->tp_comm, buf, B * D, st);
   };

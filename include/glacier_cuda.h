@@ -322,6 +322,7 @@ enum glacier_cuda_step_kind {
   GLACIER_CUDA_STEP_PROJ_DOWN,
   GLACIER_CUDA_STEP_LM_HEAD,
   GLACIER_CUDA_STEP_ARGMAX,
+  GLACIER_CUDA_STEP_ALL_REDUCE,    /* tensor parallel: split-K sum + NCCL all-reduce of o / down */
   GLACIER_CUDA_STEP_KINDS
 };
 int glacier_cuda_model_profile(glacier_cuda_model *model, int enable);

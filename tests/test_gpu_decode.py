@@ -227,3 +227,79 @@ def test_prefill_chunks_on_gemv_path():
     # 4 reserved lanes: GEMV projections; 19 prompt tokens = chunks of 4 (x4) and 3
     cfg = ModelConfig(num_layers=2, dim=256, hidden=512, num_heads=8, num_kv_heads=2, head_dim=64, vocab=1000)
     assert _prefill_parity(cfg, reserve_lanes=4, prompt_len=19, new_tokens=3) >= 2
+
+
+def test_model_load_qio_equals_direct_upload():
+    """glacier_cuda_model_load_qio takes the reference's qio page payload (qio.zig:73 encodePage:
+    16-byte sub-header, f32 scales, packed nibbles) as the oracle's gor_qio_encode writes it.  A
+    model loaded from payloads decodes bit-identically to the same model loaded from the
+    quantizer's (packed, scales), both match the oracle, and malformed payloads are rejected
+    before any write."""
+    import ctypes as C
+    from glacier_b200 import _lib
+    from glacier_b200.model import DecodeSession, DeviceModel, ModelConfig, SyntheticModel
+    cfg = ModelConfig(num_layers=2, dim=256, hidden=512, num_heads=8, num_kv_heads=2, head_dim=64, vocab=1000)
+    m = SyntheticModel(cfg, seed=17)
+    rng = np.random.default_rng(17)
+    payloads = {}
+    shapes = {"wq": (cfg.q_dim, cfg.dim), "wk": (cfg.kv_dim, cfg.dim), "wv": (cfg.kv_dim, cfg.dim),
+              "wo": (cfg.dim, cfg.q_dim), "wg": (cfg.hidden, cfg.dim), "wu": (cfg.hidden, cfg.dim),
+              "wd": (cfg.dim, cfg.hidden)}
+    kinds = {"wq": _lib.W_Q, "wk": _lib.W_K, "wv": _lib.W_V, "wo": _lib.W_O, "wg": _lib.W_GATE, "wu": _lib.W_UP,
+             "wd": _lib.W_DOWN}
+    for i, L in enumerate(m.layers):
+        for key, (o, k) in shapes.items():
+            w = rng.standard_normal(o * k, dtype=np.float32) * np.float32(0.05)
+            L[key] = oracle.quantize(w, 32)
+            payloads[(i, kinds[key])] = oracle.qio_encode(w, 32)
+    w = rng.standard_normal(cfg.vocab * cfg.dim, dtype=np.float32) * np.float32(0.05)
+    m.lm_head = oracle.quantize(w, 32)
+    payloads[(-1, _lib.W_LM_HEAD)] = oracle.qio_encode(w, 32)
+    # The payload is header + the quantizer's scales + its packed codes, byte for byte.
+    for (i, kind), pl in payloads.items():
+        packed, scales = m.lm_head if i < 0 else m.layers[i][[k for k, v in kinds.items() if v == kind][0]]
+        assert pl[16:16 + 4 * scales.size] == scales.tobytes() and pl[16 + 4 * scales.size:] == packed.tobytes()
+
+    class QioDeviceModel(DeviceModel):
+        def _int4(self, layer, kind, packed, scales):
+            pl = np.frombuffer(payloads[(layer, kind)], np.uint8)
+            _lib.call("glacier_cuda_model_load_qio", self.h, layer, kind, pl.ctypes.data, pl.size)
+
+    # The quantizer's scales are arbitrary f32 values: both models keep them in f32 (no fp16
+    # mirror), as the oracle computes.
+    da, db = DeviceModel(m, 64, scales_f16=False), QioDeviceModel(m, 64, scales_f16=False)
+    sa, sb = DecodeSession(da, 2, 4), DecodeSession(db, 2, 4)
+    om = oracle.OracleModel(m, rope_positions=64, threads=4)
+    pools = [np.zeros(4 * om.page_floats(), np.float32) for _ in range(2)]
+    bt = np.arange(4, dtype=np.int32)
+    la = torch.empty((2, cfg.vocab), dtype=torch.float32, device="cuda")
+    lb = torch.empty_like(la)
+    cur = np.array([3, 900], np.int32)
+    for pos in range(5):
+        ta = sa.step(tokens=cur, positions=[pos] * 2, logits=la).cpu().numpy()
+        tb = sb.step(tokens=cur, positions=[pos] * 2, logits=lb).cpu().numpy()
+        assert la.cpu().numpy().tobytes() == lb.cpu().numpy().tobytes()
+        assert ta.tolist() == tb.tolist()
+        for b in range(2):
+            ol, _ = om.decode_token(pools[b], bt, pos, int(cur[b]))
+            assert max_err_vs_row_max(la.cpu().numpy()[b], ol) <= DECODE_LOGIT_TOL
+        cur = ta.astype(np.int32)
+    # Malformed payloads: bad magic, wrong group, truncated, wrong element count, not INT4.
+    good = bytearray(payloads[(0, _lib.W_O)])
+    bad_magic = bytearray(good); bad_magic[0] ^= 1
+    bad_group = bytearray(good); bad_group[8:12] = (16).to_bytes(4, "little")
+    bad_prec = bytearray(good); bad_prec[12] = 2
+    truncated = good[:-1]
+    wrong_n = bytes(oracle.qio_encode(np.zeros(cfg.dim * cfg.dim // 2, np.float32), 32))
+    h = _lib.handle(_lib.lib().glacier_cuda_model_create(C.byref(_lib.ModelConfigC(
+        2, 256, 512, 8, 2, 64, 1000, 32, 1e-6, 1e6, 64, 1))))
+    try:
+        for pl in (bad_magic, bad_group, bad_prec, truncated, wrong_n):
+            buf = np.frombuffer(bytes(pl), np.uint8)
+            assert _lib.lib().glacier_cuda_model_load_qio(h, 0, _lib.W_O, buf.ctypes.data, buf.size) == _lib.EINVAL
+    finally:
+        _lib.lib().glacier_cuda_model_destroy(h)
+    for s in (sa, sb):
+        s.close()
+    da.close()
+    db.close()

@@ -20,6 +20,8 @@ def dev(a):
     (4608, 3584, 64),    # 7B fused QKV at 64 lanes
     (3584, 18944, 64),   # 7B down projection
     (256, 512, 128),     # widest batch tile
+    (37888, 3584, 64),   # 7B fused gate/up at 64 lanes (the longest unit list of the persistent grid)
+    (152064, 3584, 64),  # 7B LM head at 64 lanes
 ])
 def test_gemm_matches_oracle(out_f, in_f, batch):
     from glacier_b200 import _lib, ops
@@ -32,10 +34,13 @@ def test_gemm_matches_oracle(out_f, in_f, batch):
     y = ops.linear_int4_tensor_core(dev(x), dev(packed), dev(s16.view(np.int16)), out_f, in_f, 32, bias=dev(bias))
     torch.cuda.synchronize()
     assert _lib.lib().glacier_cuda_device_status(1) == 0
-    ref = oracle.linear_int4(x, packed, s32, out_f, in_f, 32, bias=bias, threads=8)
+    # The oracle follows every row of the batch up to 16 and a spread of rows beyond (the
+    # per-row activation scales of rows 1 and 2 among them) on the largest matrices.
+    rows = np.arange(batch) if out_f * in_f * batch <= 2**33 else np.unique(np.r_[0:16, 31, 47, 63] % batch)
+    ref = oracle.linear_int4(x[rows], packed, s32, out_f, in_f, 32, bias=bias, threads=16)
     y = y.cpu().numpy()
-    for b in range(batch):
-        assert max_rel_err(y[b], ref[b]) <= REL_TOL, b
+    for i, b in enumerate(rows):
+        assert max_rel_err(y[b], ref[i]) <= REL_TOL, b
 
 
 

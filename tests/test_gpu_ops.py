@@ -144,3 +144,29 @@ def test_argmax_plain_large_vocab_first_max():
     toks, st = ops.argmax_eligible(dev(lg))
     assert host(toks).tolist() == [oracle.argmax(lg[i]) for i in range(3)]
     assert host(st).tolist() == [0, 0, 0]
+
+
+def test_paged_attention_64_lanes_past_the_reference_cap():
+    """Config 5's attention launch: 64 lanes of the 7B geometry with lanes at contexts 4096, 4097
+    and 4352 (the reference caps attention at 4096, forward.zig:386; the oracle lifts the cap)
+    beside lanes drawn from [256, 4096].  Lanes share physical pages through their block tables
+    (the kernel only reads them), so the pool stays small while every lane reads its own
+    sequence of pages."""
+    from glacier_b200 import ops
+    heads, kv_heads, hd = 28, 4, 128
+    rng = np.random.default_rng(4352)
+    L, layer = 2, 1
+    kvd = kv_heads * hd
+    pf = oracle.page_floats(L, kvd)
+    ctxs = rng.integers(256, 4097, size=64).astype(np.int32)
+    ctxs[:3] = [4096, 4097, 4352]
+    max_pages = 4352 // 16
+    phys = 400
+    bt = rng.integers(0, phys, size=(64, max_pages)).astype(np.int32)
+    pool = rng.standard_normal(phys * pf, dtype=np.float32)
+    q = rng.standard_normal((64, heads * hd), dtype=np.float32)
+    out = host(ops.paged_attention_f32(dev(q), dev(pool), pf, dev(bt), dev(ctxs), max_pages * 16, layer, heads,
+                                       kv_heads, hd))
+    for b in range(64):
+        ref = oracle.paged_attention(q[b], pool, pf, bt[b], int(ctxs[b]), layer, heads, kv_heads, hd)
+        assert max_rel_err(out[b], ref) <= REL_TOL, (b, int(ctxs[b]))
