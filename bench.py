@@ -15,6 +15,14 @@ needed between steps.
 Multi-GPU: one process per GPU (torchrun); lanes are partitioned by GPU with a
 full weight replica each and no collective on the data path (weak scaling).
 Rank 0 prints one JSON line.
+
+Beside the headline, the same line carries the other BASELINE configurations,
+each with its own roofline and CPU baseline: on one GPU `gemv_config1` (the
+4864 x 896 GEMV), `config2` (0.5B, batch 1, 128 tokens after a 512-token
+prefill), `config3` (1.5B, 8 lanes, 256 tokens each), `prefill` (7B prompts of
+128 / 512 / 2048 tokens) and `batch1` (7B, one lane); under torchrun
+`strong_scaling` (64 lanes in total split over the N GPUs) and `tp` (one
+64-lane job over N tensor-parallel GPUs, where the 7B heads divide by N).
 """
 from __future__ import annotations
 
@@ -62,7 +70,12 @@ def parse():
     ap.add_argument("--tokens", type=int, default=2048, help="prompt length for --workload prefill")
     ap.add_argument("--profile-steps", type=int, default=10,
                     help="decode steps of the per-kernel-class event pass that follows the timed region")
-    return ap.parse_args()
+    ap.add_argument("--no-extras", action="store_true",
+                    help="headline only: skip the other configurations' keys (small cases for profiling)")
+    a = ap.parse_args()
+    if a.model_file and a.layers is not None:
+        ap.error("--layers cuts the synthetic preset; it does not apply to --model-file")
+    return a
 
 
 # ---------------------------------------------------------------------------
@@ -227,6 +240,16 @@ def data_label(args) -> str:
     return f"model file {os.path.basename(args.model_file)}" if getattr(args, "model_file", None) else "synthetic"
 
 
+def model_label(args, cfg, layers: int | None = None) -> str:
+    """The model a line measures: the preset's name, or the model file's name with the
+    geometry read from it."""
+    nl = layers if layers is not None else cfg.num_layers
+    if getattr(args, "model_file", None):
+        return (f"{os.path.basename(args.model_file)} ({nl} layers, dim {cfg.dim}, ffn {cfg.hidden}, "
+                f"{cfg.num_heads}/{cfg.num_kv_heads} heads of {cfg.head_dim}, vocab {cfg.vocab}, g{cfg.group})")
+    return args.model if nl == cfg.num_layers else f"{args.model} ({nl} of {cfg.num_layers} layers)"
+
+
 def run_reference(args):
     ws, rank, _ = dist_setup()
     if rank != 0:
@@ -240,8 +263,9 @@ def run_reference(args):
         "impl": "reference", "metric": METRIC, "value": r["value"], "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 / r["value"], "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": data_label(args),
-        "config": {"workload": "7B decode, 64 lanes, ctx U[256,4096], greedy (config 5); reference step = "
-                               "one lane-token on the host cores", "model": args.model, "lanes": args.lanes},
+        "config": {"workload": f"decode, {args.lanes} lanes, ctx U[{args.ctx_min},{args.ctx_max}], greedy "
+                               "(config 5); reference step = one lane-token on the host cores",
+                   "model": model_label(args, cfg, model.cfg["num_layers"]), "lanes": args.lanes},
         "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": r["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -354,12 +378,24 @@ def run_glacier(args):
     # Per-kernel-class pass: the library records CUDA events on the step's stream
     # between its kernel classes for a few more steps of the same decode.
     dom = step_kernel_timing(torch, dm, sess, cfg, lanes, stream, args.profile_steps, device_step)
-    # The batch-1 half of the metric is a single-GPU measurement: rank 0 takes it,
-    # with no collective in it, while the other ranks go on to the final max-over-ranks.
-    b1 = None
-    if rank == 0:
-        b1 = batch1_decode(torch, model, cfg, args, rank, stream)
-        b1["gemv_activation_modes"] = gemv_modes_timing(torch, cfg)
+    sess.close()
+    extras = {}
+    # Multi-GPU extras (every rank takes the same collective steps in the same order):
+    # the lane partition with a fixed 64-lane job, and tensor parallelism over the N ranks.
+    if ws > 1 and tp == 1 and not args.no_extras:
+        extras["strong_scaling"] = strong_scaling(torch, dm, cfg, args, ws, rank)
+        extras["tp"] = tp_pass(torch, model, cfg, args, ws, rank)
+    # Single-GPU extras (the line at N = 1): batch 1 and prefill on this upload, then the
+    # other BASELINE configurations on their own synthetic models.
+    if ws == 1 and not args.no_extras:
+        extras["batch1"] = batch1_decode(torch, model, cfg, args, rank, stream, dm)
+        extras["batch1"]["gemv_activation_modes"] = gemv_modes_timing(torch, cfg)
+        extras["prefill"] = prefill_sweep(torch, dm, model, cfg, args)
+    dm.close()
+    if ws == 1 and not args.no_extras and not args.model_file:
+        extras["gemv_config1"] = gemv_config1(torch, args)
+        extras["config2"] = config2_decode(torch, args)
+        extras["config3"] = config3_decode(torch, args)
 
     dev_ms, e2e_ms = max_over_ranks([dev_ms, e2e_s * 1e3], ws, dev)
     tokens_total = lanes * args.steps * (1 if tp > 1 else ws)
@@ -379,9 +415,11 @@ def run_glacier(args):
             "ms_per_step": dev_ms / args.steps, "higher_is_better": True,
             "scaling": "strong" if tp > 1 else "weak", "vs_baseline": None,
             "dtype": "f32 activations / int4 g32 weights (fp16 scales) / f32 KV", "data": data_label(args),
-            "config": {"workload": (f"7B decode, {lanes} lanes over {tp} tensor-parallel GPUs" if tp > 1 else
-                                    "7B decode, 64 lanes per GPU") + ", ctx U[256,4096], greedy (BASELINE config 5)",
-                       "model": args.model, "lanes_per_gpu": lanes if tp == 1 else lanes / tp,
+            "config": {"workload": (f"decode, {lanes} lanes over {tp} tensor-parallel GPUs" if tp > 1 else
+                                    f"decode, {lanes} lanes per GPU") +
+                                   f", ctx U[{args.ctx_min},{args.ctx_max}], greedy (BASELINE config 5)",
+                       "model": model_label(args, cfg, dm.cfg["num_layers"]),
+                       "lanes_per_gpu": lanes if tp == 1 else lanes / tp,
                        "mean_ctx": float(np.mean(ctxs)),
                        "parallelism": (f"tensor parallel x{tp} (Megatron split, NCCL all-reduce of o and down)"
                                        if tp > 1 else f"lane partition x{ws} (weights replicated, no collective)"),
@@ -390,7 +428,7 @@ def run_glacier(args):
             "achieved_step_gbs": step_bytes / (dev_ms / args.steps / 1e3) / 1e9,
             "roofline": dom["roofline"],
             "kernels": dom["kernels"],
-            "batch1": b1,
+            **extras,
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 2 * lanes * 4,
                     "d2h_bytes_per_step": lanes * 4},
@@ -399,8 +437,6 @@ def run_glacier(args):
             "peaks_source": peaks.get("_source"),
         }
         print(json.dumps(line), flush=True)
-    sess.close()
-    dm.close()
     if ws > 1:
         torch.distributed.destroy_process_group()
 
@@ -418,9 +454,9 @@ def load_peaks() -> dict:
 # DRAM bytes (dram__bytes_read + write) per algorithmic byte, from one ncu capture of a smaller
 # case of the same kernel (profiles/); traffic scales with the K/V rows a launch reads.
 DRAM_TRAFFIC_RATIO = {
-    "attention": (271.8e6 / 265.1e6, "ncu: 265.7 MB read + 6.1 MB written for 265.1 MB algorithmic (1 layer, 32 "
-                                     "lanes, mean ctx 2015), scaled to this launch's K/V bytes; "
-                                     "profiles/attn_tma_128x7_32lanes.md"),
+    "attention": (271.8e6 / 265.1e6, "ncu dram__bytes_read.sum + dram__bytes_write.sum: 265.7 MB read + 6.1 MB "
+                                     "written for 265.1 MB algorithmic (1 layer, 32 lanes, mean ctx 2015), scaled "
+                                     "to this launch's K/V bytes"),
 }
 
 STEP_KINDS = ("embed", "norm", "proj_qkv", "rope_append", "attention", "attn_combine", "proj_o", "proj_gate_up",
@@ -490,7 +526,7 @@ def step_kernel_timing(torch, dm, sess, cfg, lanes, stream, steps, device_step) 
     return {"kernels": kernels, "roofline": roof}
 
 
-def batch1_decode(torch, model, cfg, args, rank, stream) -> dict:
+def batch1_decode(torch, model, cfg, args, rank, stream, dm=None) -> dict:
     """Batch-1 half of the metric: one lane of the same 7B model decoding alone, on a DeviceModel
     reserved for one lane (GEMV path: 4 lanes or fewer never take the batched GEMM).  Context
     drawn like config 5's lanes; KV rows random.  Timed on the device with CUDA events over
@@ -501,8 +537,10 @@ def batch1_decode(torch, model, cfg, args, rank, stream) -> dict:
     ctx = int(lane_contexts(args, 1, rank)[0])
     steps, warm = 20, 3
     max_pages = -(-(ctx + steps + 2 * warm + args.profile_steps + 4) // 16)
-    dm = DeviceModel(model, max_positions=max_pages * 16)
-    sess = DecodeSession(dm, 1, max_pages)
+    own = dm is None or dm.max_positions < max_pages * 16
+    if own:
+        dm = DeviceModel(model, max_positions=max_pages * 16)
+    sess = DecodeSession(dm, 1, max_pages)  # one reserved lane: the GEMV path
     g = torch.Generator(device="cuda")
     g.manual_seed(args.seed + 1000 + rank)
     pages = sess.pages()
@@ -539,9 +577,14 @@ def batch1_decode(torch, model, cfg, args, rank, stream) -> dict:
     hbm = float(load_peaks()["hbm_gbs"])
     prof = step_kernel_timing(torch, dm, sess, cfg, 1, stream, args.profile_steps, step)
     sess.close()
-    dm.close()
+    if own:
+        dm.close()
+    cpu = time_cpu_oracle(model, np.array([ctx], np.int32), args, min(args.cpu_seconds, 4.0))
     return {"tok_s": 1e3 / ms, "ms_per_token": ms, "ctx": ctx, "algorithmic_bytes_per_token": int(byt),
             "achieved_gbs": byt / (ms * 1e-3) / 1e9, "frac_of_hbm_peak": byt / (ms * 1e-3) / 1e9 / hbm,
+            "roofline": {"bound": "hbm", "achieved": byt / (ms * 1e-3) / 1e9, "peak": hbm, "unit": "GB/s",
+                         "frac": byt / (ms * 1e-3) / 1e9 / hbm, "algorithmic_bytes": int(byt)},
+            "cpu_baseline": {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "timing": f"CUDA events over {steps} CUDA-graph replays of the greedy step after {warm} warm-up steps",
             "kernels": prof["kernels"]}
 
@@ -590,6 +633,351 @@ def gemv_modes_timing(torch, cfg) -> dict:
             del g
         out[f"{name}_{M}x{K}"] = e
     return out
+
+
+def _graph_time_us(torch, stream, call, n: int) -> float:
+    """Mean device time of `call(i)` over one replay of a CUDA graph of n back-to-back calls
+    (after a warm replay), CUDA events on the capture stream."""
+    with torch.cuda.stream(stream):
+        for i in range(3):
+            call(i)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(n):
+                call(i)
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        g.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    del g
+    return e0.elapsed_time(e1) / n * 1e3
+
+
+def gemv_config1(torch, args) -> dict:
+    """Config 1, the reference's kernel microbench shape (bench/int4_kernel.zig:18-30): one
+    4864 x 896 INT4 g32 GEMV, y = x * dequant(W)^T, x ~ N(0, 1) fp32, uniform codes, fp16 scales
+    of |N(0, 0.02)|.  The matrix is 2.47 MB, inside the 126 MB L2, so the timed loop walks
+    rotating copies uploaded once through the persistent weight handle (fp16 scale rows padded
+    for TMA), more than 4x L2 in total, as one CUDA graph of 600 calls.  Algorithmic bytes per
+    call: codes + fp16 scales + x + y = 2,474,496.  CPU baseline: the oracle's
+    linearInt4OnTheFly on 1 thread and with the reference's row split over all host threads."""
+    import ctypes as C
+    import oracle
+    from glacier_b200 import _lib
+    from glacier_b200.model import random_int4
+    L = _lib.lib()
+    M, K, G = 4864, 896, 32
+    rng = np.random.default_rng(args.seed + 11)
+    packed, s32 = random_int4(rng, M, K, G)
+    s16 = s32.astype(np.float16).view(np.uint16)
+    x = rng.standard_normal(K, dtype=np.float32)
+    wbytes = M * K // 2 + M * K // G * 2
+    byt = wbytes + 4 * K + 4 * M
+    l2 = torch.cuda.get_device_properties(torch.cuda.current_device()).L2_cache_size
+    copies = int(4 * l2 // wbytes) + 1
+    ctx = _lib.handle(L.glacier_cuda_context_create(torch.cuda.current_device()))
+    hs = []
+    try:
+        for _ in range(copies):
+            hs.append(_lib.handle(L.glacier_cuda_int4_weight_create_ex(
+                ctx, packed.ctypes.data, packed.size, s16.ctypes.data, s16.size, 1, G, K, M)))
+        xd = torch.from_numpy(x).cuda()
+        yd = torch.empty(M, dtype=torch.float32, device="cuda")
+        st = torch.cuda.Stream()
+
+        def call(i):
+            assert L.glacier_cuda_int4_weight_matvec(hs[i % copies], xd.data_ptr(), yd.data_ptr(), None,
+                                                     C.c_void_p(st.cuda_stream)) == 0
+
+        us = _graph_time_us(torch, st, call, 600)
+        y = yd.cpu().numpy()
+    finally:
+        for h in hs:
+            L.glacier_cuda_int4_weight_destroy(h)
+        L.glacier_cuda_context_destroy(ctx)
+    ref = oracle.linear_int4(x, packed, s32, M, K, G)[0]
+    err = float(np.abs(y - ref).max() / max(np.abs(ref).max(), 1e-30))
+    hbm = float(load_peaks()["hbm_gbs"])
+    cpu = {}
+    for th in (1, cpu_threads()):
+        reps, t = 0, 0.0
+        while t < 1.0:
+            t0 = time.perf_counter()
+            oracle.linear_int4(x, packed, s32, M, K, G, threads=th)
+            t += time.perf_counter() - t0
+            reps += 1
+        cpu[th] = t / reps * 1e6
+    return {
+        "us": us, "gbs": byt / (us * 1e-6) / 1e9,
+        "config": f"4864x896 INT4 g32, fp16 scales, batch 1; {copies} rotating copies "
+                  f"({copies * wbytes / 1e6:.0f} MB > 4x L2), CUDA graph of 600 calls",
+        "max_err_vs_row_max": err,
+        "roofline": {"bound": "hbm", "achieved": byt / (us * 1e-6) / 1e9, "peak": hbm, "unit": "GB/s",
+                     "frac": byt / (us * 1e-6) / 1e9 / hbm, "algorithmic_bytes": byt},
+        "cpu_baseline": {"value": cpu[1], "unit": "us per GEMV", "cores": 1, "kind": "port",
+                         "all_cores_us": cpu[cpu_threads()], "all_cores": cpu_threads(),
+                         "sample": "the oracle's linearInt4OnTheFly on the same matrix and input, repeated for "
+                                   "about 1 s per thread count (row split over all host threads for all_cores)"},
+    }
+
+
+def _random_pages(torch, sess, seed):
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    pages = sess.pages()
+    for i in range(0, pages.shape[0], 256):
+        pages[i:i + 256].normal_(generator=g)
+
+
+def _graph_decode(torch, sess, warm: int, steps: int) -> float:
+    """ms per greedy step: `warm` stream steps, then a CUDA graph of one greedy step replayed
+    `warm` times untimed and `steps` times timed (CUDA events on the side stream)."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(warm):
+            out = sess.step(stream=side)
+            sess.tokens.copy_(out)
+            sess.positions.add_(1)
+        sess.capture_greedy_step(stream=side)
+        for _ in range(warm):
+            sess.replay_greedy_step()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(side)
+        for _ in range(steps):
+            sess.replay_greedy_step()
+        e1.record(side)
+    torch.cuda.synchronize()
+    assert (sess.status.cpu().numpy() == 0).all()
+    return e0.elapsed_time(e1) / steps
+
+
+def config2_decode(torch, args) -> dict:
+    """Config 2: the 0.5B model (24 layers, D 896, FFN 4864, 14/2 heads of 64, vocab 151936),
+    batch 1: a 512-token prompt of uniform ids through glacier_cuda_prefill, then 128 greedy
+    tokens (CUDA-graph replays of the greedy step after 3 warm-up tokens).  Algorithmic bytes
+    per token: every INT4 code and fp16 scale (LM head included) + the lane's K/V rows."""
+    from glacier_b200.model import PRESETS, DecodeSession, DeviceModel, SyntheticModel
+    cfg = PRESETS["qwen2.5-0.5b"]
+    m = SyntheticModel(cfg, seed=args.seed + 2)
+    prompt_len, new, warm = 512, 128, 3
+    max_pages = -(-(prompt_len + new + 2 * warm + 2) // 16)
+    dm = DeviceModel(m, max_positions=max_pages * 16)
+    sess = DecodeSession(dm, 1, max_pages)
+    rng = np.random.default_rng(args.seed + 3)
+    prompt = rng.integers(0, cfg.vocab, size=prompt_len).astype(np.int32)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    tok = sess.prefill(prompt)
+    e1.record()
+    torch.cuda.synchronize()
+    prefill_ms = e0.elapsed_time(e1)
+    assert int(sess.last_status.cpu()[0]) == 0
+    sess.tokens.copy_(tok)
+    sess.positions.fill_(prompt_len)
+    ms = _graph_decode(torch, sess, warm, new)
+    mean_ctx = prompt_len + 2 * warm + new / 2
+    byt = cfg.int4_bytes_per_token() + int(mean_ctx) * cfg.num_layers * 2 * cfg.kv_dim * 4
+    hbm = float(load_peaks()["hbm_gbs"])
+    sess.close()
+    dm.close()
+    cpu = time_cpu_oracle(m, np.array([prompt_len + new // 2], np.int32), args, min(args.cpu_seconds, 4.0))
+    return {
+        "tok_s": 1e3 / ms, "ms_per_token": ms, "prefill_512_ms": prefill_ms,
+        "config": "0.5B shape, batch 1, 512-token uniform prompt (chunked prefill on the one-lane GEMV "
+                  "path), then 128 greedy tokens; CUDA-graph replays of the greedy step",
+        "algorithmic_bytes_per_token": int(byt),
+        "roofline": {"bound": "hbm", "achieved": byt / (ms * 1e-3) / 1e9, "peak": hbm, "unit": "GB/s",
+                     "frac": byt / (ms * 1e-3) / 1e9 / hbm},
+        "cpu_baseline": {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
+    }
+
+
+def config3_decode(torch, args) -> dict:
+    """Config 3: the 1.5B model (28 layers, D 1536, FFN 8960, 12/2 heads of 128, vocab 151936),
+    8 lanes with contexts U[128, 2048] (random FP32 K/V rows up to each lane's context), greedy,
+    256 tokens per lane (CUDA-graph replays of the greedy step after 3 warm-up steps).
+    Algorithmic bytes per step: the weights once + every lane's K/V rows."""
+    from glacier_b200.model import PRESETS, DecodeSession, DeviceModel, SyntheticModel
+    cfg = PRESETS["qwen2.5-1.5b"]
+    m = SyntheticModel(cfg, seed=args.seed + 4)
+    lanes, steps, warm = 8, 256, 3
+    rng = np.random.default_rng(args.seed + 5)
+    ctxs = rng.integers(128, 2049, size=lanes).astype(np.int32)
+    max_pages = -(-(int(ctxs.max()) + steps + 2 * warm + 2) // 16)
+    dm = DeviceModel(m, max_positions=max_pages * 16)
+    sess = DecodeSession(dm, lanes, max_pages)
+    _random_pages(torch, sess, args.seed + 6)
+    sess.tokens.copy_(torch.from_numpy(rng.integers(0, cfg.vocab, size=lanes).astype(np.int32)))
+    sess.positions.copy_(torch.from_numpy(ctxs))
+    ms = _graph_decode(torch, sess, warm, steps)
+    kv = int(np.sum(ctxs + 2 * warm + steps // 2)) * cfg.num_layers * 2 * cfg.kv_dim * 4
+    byt = cfg.int4_bytes_per_token() + kv
+    hbm = float(load_peaks()["hbm_gbs"])
+    sess.close()
+    dm.close()
+    cpu = time_cpu_oracle(m, ctxs, args, min(args.cpu_seconds, 4.0))
+    return {
+        "tok_s": lanes * 1e3 / ms, "ms_per_step": ms, "lanes": lanes, "mean_ctx": float(np.mean(ctxs)),
+        "config": "1.5B shape, 8 lanes, ctx U[128,2048], greedy 256 tokens per lane (tcgen05 GEMM path); "
+                  "CUDA-graph replays of the greedy step",
+        "algorithmic_bytes_per_step": int(byt),
+        "roofline": {"bound": "hbm", "achieved": byt / (ms * 1e-3) / 1e9, "peak": hbm, "unit": "GB/s",
+                     "frac": byt / (ms * 1e-3) / 1e9 / hbm},
+        "cpu_baseline": {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
+    }
+
+
+def prefill_flops(cfg, nl: int, T: int) -> float:
+    """Useful FLOPs of a T-token prompt: 2 x linear params x T + causal attention (QK and PV)."""
+    lin = nl * ((cfg.q_dim + 2 * cfg.kv_dim) * cfg.dim + cfg.dim * cfg.q_dim + 3 * cfg.hidden * cfg.dim)
+    return 2.0 * lin * T + nl * 4.0 * cfg.head_dim * cfg.num_heads * T * (T + 1) / 2
+
+
+def prefill_sweep(torch, dm, model, cfg, args) -> dict:
+    """Config 4 on the bench's own 7B upload: one prompt of T = 128, 512 and 2048 uniform ids,
+    chunks of 128 rows on the tcgen05 GEMM, timed on the device (1 warm-up, 3 timed prompts).
+    MFU against the measured dense bf16 peak.  CPU baseline: the reference feeds g32 prompts one
+    token at a time (generate.zig:2377), so its prompt rate is its per-token rate, timed on the
+    oracle at a context of 256."""
+    from glacier_b200.model import DecodeSession
+    peaks = load_peaks()
+    peak = float(peaks.get("bf16_tflops", 1590.0)) * 1e12
+    nl = dm.cfg["num_layers"]
+    out = {}
+    for T in (128, 512, 2048):
+        sess = DecodeSession(dm, 1, -(-(T + 1) // 16), reserve_lanes=128)
+        prompt = torch.from_numpy(np.random.default_rng(args.seed + T).integers(0, cfg.vocab, size=T)
+                                  .astype(np.int32)).cuda()
+        sess.prefill(prompt)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(3):
+            sess.prefill(prompt)
+        e1.record()
+        torch.cuda.synchronize()
+        assert int(sess.last_status.cpu()[0]) == 0
+        ms = e0.elapsed_time(e1) / 3
+        fl = prefill_flops(cfg, nl, T)
+        out[f"T{T}"] = {"tok_s": T / (ms / 1e3), "ms": ms,
+                        "roofline": {"bound": "tensor", "achieved": fl / (ms / 1e3) / 1e12, "peak": peak / 1e12,
+                                     "unit": "TFLOP/s", "frac": fl / (ms / 1e3) / peak}}
+        sess.close()
+    cpu = time_cpu_oracle(model, np.array([256], np.int32), args, min(args.cpu_seconds, 4.0))
+    out["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind")}
+    out["cpu_baseline"]["sample"] = ("prompt tokens fed one at a time (the reference's g32 prompt path) at context "
+                                     "256: " + cpu["sample"])
+    out["note"] = ("useful FLOPs (MFU); the exact fp16 hi/lo operand split runs 3x the MMA work; "
+                   "peak " + str(peaks.get("_source")))
+    return out
+
+
+def strong_scaling(torch, dm, cfg, args, ws, rank, lanes_total: int = 64) -> dict:
+    """Lane partition with a fixed job: `lanes_total` lanes (contexts drawn like the headline's)
+    split over the N ranks, each rank decoding its share on its full weight replica; whole-job
+    tok/s from the max over ranks of the device time of `args.steps` steps."""
+    from glacier_b200.model import DecodeSession
+    per = -(-lanes_total // ws)
+    lanes = max(0, min(per, lanes_total - rank * per))
+    all_ctx = lane_contexts(args, lanes_total, 0)
+    ctxs = all_ctx[rank * per:rank * per + lanes]
+    ms = 0.0
+    sess = None
+    if lanes:
+        max_pages = -(-(int(ctxs.max()) + args.warmup + args.steps + 2) // 16)
+        sess = DecodeSession(dm, lanes, max_pages)
+        _random_pages(torch, sess, args.seed + 77 + rank)
+        sess.tokens.fill_(1)
+        sess.positions.copy_(torch.from_numpy(ctxs))
+        for _ in range(args.warmup):
+            out = sess.step()
+            sess.tokens.copy_(out)
+            sess.positions.add_(1)
+    torch.cuda.synchronize()
+    torch.distributed.barrier()
+    torch.cuda.synchronize()
+    if sess is not None:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            out = sess.step()
+            sess.tokens.copy_(out)
+            sess.positions.add_(1)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        assert (sess.status.cpu().numpy() == 0).all()
+        sess.close()
+    (ms,) = max_over_ranks([ms], ws, torch.device("cuda", torch.cuda.current_device()))
+    return {"lanes_total": lanes_total, "lanes_per_gpu": per, "tok_s": lanes_total * args.steps / (ms / 1e3),
+            "ms_per_step": ms / args.steps, "scaling": "strong",
+            "timing": "device time of the timed steps, CUDA events, max over ranks"}
+
+
+def tp_pass(torch, model, cfg, args, ws, rank) -> dict:
+    """Tensor parallelism over the N ranks (Megatron split: each rank holds H/N q heads, Hkv/N kv
+    heads, F/N FFN rows and the matching o / down columns; an NCCL all-reduce after o and after
+    down): one 64-lane job with the headline's contexts.  Reports whole-job tok/s (max over
+    ranks of the device time) and the all-reduce share of the profiled step."""
+    import ctypes as C
+    from glacier_b200 import _lib
+    from glacier_b200.model import DecodeSession, DeviceModel, TensorParallelShard, tp_unique_id
+    c = model.cfg
+    if c["num_heads"] % ws or c["num_kv_heads"] % ws or c["hidden"] % (ws * c["group"]):
+        return {"unavailable": f"{c['num_heads']} q / {c['num_kv_heads']} kv heads do not split over {ws} GPUs "
+                               "(the Megatron split needs whole kv heads per GPU)"}
+    lanes = 64
+    ctxs = lane_contexts(args, lanes, 0)
+    max_pages = -(-(int(ctxs.max()) + args.warmup + args.steps + args.profile_steps + 2) // 16)
+    dm = DeviceModel(TensorParallelShard(model, rank, ws), max_positions=max_pages * 16)
+    uid = [tp_unique_id() if rank == 0 else None]
+    torch.distributed.broadcast_object_list(uid, src=0)
+    dm.enable_tensor_parallel(rank, ws, uid[0])
+    sess = DecodeSession(dm, lanes, max_pages)
+    _random_pages(torch, sess, args.seed + 99 + rank)
+    sess.tokens.fill_(1)
+    sess.positions.copy_(torch.from_numpy(ctxs))
+
+    def step():
+        out = sess.step()
+        sess.tokens.copy_(out)
+        sess.positions.add_(1)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    torch.distributed.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    # Per-class device time of a few more steps: the all-reduce share.
+    n = len(STEP_KINDS) + 1
+    _lib.call("glacier_cuda_model_profile", dm.h, 1)
+    for _ in range(args.profile_steps):
+        step()
+    _lib.call("glacier_cuda_model_profile", dm.h, 0)
+    cms = (C.c_double * n)()
+    regions = (C.c_uint64 * n)()
+    _lib.call("glacier_cuda_model_profile_read", dm.h, cms, regions, n)
+    share = cms[n - 1] / max(sum(cms), 1e-30)
+    assert (sess.status.cpu().numpy() == 0).all()
+    sess.close()
+    dm.close()
+    ms, share = max_over_ranks([ms, share], ws, torch.device("cuda", torch.cuda.current_device()))
+    return {"lanes": lanes, "tp": ws, "tok_s": lanes * args.steps / (ms / 1e3), "ms_per_step": ms / args.steps,
+            "all_reduce_share": share, "scaling": "strong",
+            "parallelism": f"tensor parallel x{ws} (Megatron split, NCCL all-reduce of o and down, 2 per layer)"}
 
 
 def run_prefill(args):
