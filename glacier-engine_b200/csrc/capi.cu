@@ -138,7 +138,7 @@ int qkv_rope_append(const float* qkv, size_t ld, size_t split_stride, int nsplit
                     size_t page_floats, const int32_t* block_tables, size_t max_pages, size_t layer,
                     cudaStream_t stream);
 size_t attention_workspace_floats(size_t lanes, size_t num_heads, size_t head_dim, size_t nsplit);
-int attention_chunk(size_t lanes, size_t num_heads, size_t num_kv_heads, size_t max_ctx);
+int attention_segments(size_t lanes, size_t num_heads, size_t head_dim, size_t max_ctx);
 int paged_attention(const float* q, size_t ldq, const float* pool, size_t page_floats, const int32_t* block_tables,
                     size_t max_pages, const int32_t* ctx_lens, size_t max_ctx, size_t lanes, size_t layer,
                     size_t num_heads, size_t num_kv_heads, size_t head_dim, float* out, size_t ldo, float* workspace,
@@ -158,6 +158,7 @@ int gemm_int4_tc(const Int4Weight& w, const CUtensorMap& xmap, const float* xsca
                  size_t ldy, int nsplit, size_t split_stride, const float* bias, cudaStream_t stream);
 int gemm_device_error(int clear);
 int attn_device_error(int clear);
+int persist_device_error(int clear);
 int gemm_splits(size_t M, size_t K);
 int reduce_splits(const float* part, size_t split_stride, int nsplit, float* y, size_t n, cudaStream_t stream);
 
@@ -214,9 +215,10 @@ unsigned long long glacier_cuda_launch_count(void) { return g_launches.load(std:
 int glacier_cuda_device_status(int clear) {
   GLC_CHECK_CUDA(cudaDeviceSynchronize());
   const int v = gemv_device_error(clear), w = ops_device_error(clear), g = gemm_device_error(clear),
-            a = attn_device_error(clear), q = q8_device_error(clear);
-  if (v < 0 || w < 0 || g < 0 || a < 0 || q < 0) return set_error(GLACIER_CUDA_ECUDA, "device status read failed");
-  return (v || g || a || q) ? 1 : (w ? 2 : 0);
+            a = attn_device_error(clear), q = q8_device_error(clear), p = persist_device_error(clear);
+  if (v < 0 || w < 0 || g < 0 || a < 0 || q < 0 || p < 0)
+    return set_error(GLACIER_CUDA_ECUDA, "device status read failed");
+  return (v || g || a || q || p == 1) ? 1 : ((w || p) ? 2 : 0);
 }
 
 int glacier_cuda_int4_matvec_f32(const float* x, const uint8_t* packed, const float* scales,
@@ -318,8 +320,8 @@ int glacier_cuda_qkv_rope_append_f32(const float* qkv, size_t ld, const float* b
 size_t glacier_cuda_paged_attention_workspace(size_t lanes, size_t num_heads, size_t num_kv_heads, size_t head_dim,
                                               size_t max_ctx) {
   if (!lanes || !num_kv_heads || !max_ctx) return 0;
-  const int chunk = attention_chunk(lanes, num_heads, num_kv_heads, max_ctx);
-  return attention_workspace_floats(lanes, num_heads, head_dim, ceil_div(max_ctx, (size_t)chunk));
+  return attention_workspace_floats(lanes, num_heads, head_dim,
+                                    attention_segments(lanes, num_heads, head_dim, max_ctx));
 }
 
 int glacier_cuda_paged_attention_f32(const float* q, const float* kv_pages, size_t page_floats,
@@ -328,13 +330,11 @@ int glacier_cuda_paged_attention_f32(const float* q, const float* kv_pages, size
                                      size_t head_dim, float* out, float* workspace, size_t workspace_floats,
                                      void* stream) {
   GLC_REQUIRE(lanes > 0 && num_kv_heads > 0, "paged_attention: empty batch");
-  // The kernel's two work counters sit at the start of the workspace and must start at zero.
   const size_t need = glacier_cuda_paged_attention_workspace(lanes, num_heads, num_kv_heads, head_dim, max_ctx);
   GLC_REQUIRE(workspace && workspace_floats >= need, "paged_attention: workspace of %zu floats needed", need);
-  GLC_CHECK_CUDA(cudaMemsetAsync(workspace, 0, 4 * sizeof(float), (cudaStream_t)stream));
   return paged_attention(q, num_heads * head_dim, kv_pages, page_floats, block_tables, max_pages, ctx_lens, max_ctx,
                          lanes, layer, num_heads, num_kv_heads, head_dim, out, num_heads * head_dim, workspace,
-                         workspace_floats, attention_chunk(lanes, num_heads, num_kv_heads, max_ctx), (cudaStream_t)stream);
+                         workspace_floats, attention_segments(lanes, num_heads, head_dim, max_ctx), (cudaStream_t)stream);
 }
 
 size_t glacier_cuda_argmax_workspace(size_t batch, size_t n) { return argmax_workspace_bytes(batch, n); }

@@ -396,6 +396,17 @@ __device__ __forceinline__ void store_split8(const SplitOut& so, int r, size_t K
   *reinterpret_cast<uint4*>(so.xs + ((size_t)so.np + r) * K + base) = *reinterpret_cast<uint4*>(l);
 }
 
+// fp16 bits (low 16 bits of h) to the equal fp32 value without the conversion
+// unit: the magnitude bits shifted into an fp32 field give the value times
+// 2^-112 for normal and subnormal inputs alike (the fp32 result of a subnormal
+// input is itself subnormal), and the power-of-two product is exact.  Finite
+// inputs only (scales are).  In hot loops this keeps the fp16 -> fp32 scale
+// conversions off the narrow special-function pipe.
+__device__ __forceinline__ float half_to_float_bits(uint32_t h) {
+  const uint32_t b = ((h & 0x8000u) << 16) | ((h & 0x7FFFu) << 13);
+  return __uint_as_float(b) * 0x1p112f;
+}
+
 // Scale loads: the library keeps fp16 scale mirrors (as the reference's
 // int4_weights.withF16Scales does) but also accepts fp32 scales.
 __device__ __forceinline__ float load_scale(const __half* s, size_t i) { return __half2float(s[i]); }

@@ -26,7 +26,7 @@
 #include <memory>
 #include <vector>
 
-#include "common.cuh"
+#include "persistent.cuh"
 
 namespace glacier {
 
@@ -45,7 +45,7 @@ int qkv_rope_append(const float* qkv, size_t ld, size_t split_stride, int nsplit
                     size_t page_floats, const int32_t* block_tables, size_t max_pages, size_t layer,
                     cudaStream_t stream);
 size_t attention_workspace_floats(size_t lanes, size_t num_heads, size_t head_dim, size_t nsplit);
-int attention_chunk(size_t lanes, size_t num_heads, size_t num_kv_heads, size_t max_ctx);
+int attention_segments(size_t lanes, size_t num_heads, size_t head_dim, size_t max_ctx);
 int paged_attention(const float* q, size_t ldq, const float* pool, size_t page_floats, const int32_t* block_tables,
                     size_t max_pages, const int32_t* ctx_lens, size_t max_ctx, size_t lanes, size_t layer,
                     size_t num_heads, size_t num_kv_heads, size_t head_dim, float* out, size_t ldo, float* workspace,
@@ -254,7 +254,7 @@ struct glacier_cuda_model {
   size_t max_lanes = 0, max_pages = 0;
   DevBuf x, hn, qkv, q, attn, proj, gu, act, down, logits, ctx, att_ws, arg_ws, status;
   size_t att_floats = 0, arg_bytes = 0;
-  int att_chunk = 0;
+  int att_segs = 0;
   // Tensor-core GEMM mode (more than 4 lanes): activations in split fp16 form.
   bool gemm = false;
   size_t np = 0;
@@ -265,7 +265,14 @@ struct glacier_cuda_model {
   // Tensor parallelism: this rank's NCCL communicator (nullptr: one GPU).
   void* tp_comm = nullptr;
   int tp_rank = 0, tp_world = 1;
-  ~glacier_cuda_model() { tp_comm_destroy(tp_comm); }
+  // One-lane reservations: the whole decode step as one persistent kernel
+  // (decode_persistent.cu) when switched on (glacier_cuda_model_persistent).
+  PersistState* ps = nullptr;
+  bool persistent = false;
+  ~glacier_cuda_model() {
+    tp_comm_destroy(tp_comm);
+    persist_destroy(ps);
+  }
   StepProfiler prof;  // optional per-kernel-class timing of decode steps
 };
 
@@ -525,8 +532,8 @@ int glacier_cuda_model_reserve(glacier_cuda_model* m, size_t max_lanes, size_t m
   if (rc) return rc;
   const auto& c = m->cfg;
   const size_t L = max_lanes;
-  m->att_chunk = attention_chunk(L, c.num_heads, c.num_kv_heads, max_pages * 16);
-  const size_t nsplit = ceil_div(max_pages * 16, (size_t)m->att_chunk);
+  m->att_segs = attention_segments(L, c.num_heads, c.head_dim, max_pages * 16);
+  const size_t nsplit = (size_t)m->att_segs;
   m->att_floats = attention_workspace_floats(L, c.num_heads, c.head_dim, nsplit);
   m->arg_bytes = argmax_workspace_bytes(L, c.vocab);
   if ((rc = m->x.alloc(L * c.dim * 4)) || (rc = m->hn.alloc(L * c.dim * 4)) ||
@@ -538,11 +545,36 @@ int glacier_cuda_model_reserve(glacier_cuda_model* m, size_t max_lanes, size_t m
       (rc = m->arg_ws.alloc(m->arg_bytes)) || (rc = m->status.alloc(L * 4)) || (rc = m->pf_pos.alloc(L * 4)) ||
       (rc = m->pf_bt.alloc(L * max_pages * 4)))
     return rc;
-  // The attention kernel's work counters (start of its workspace) begin at zero
-  // and every launch leaves them at zero.
-  GLC_CHECK_CUDA(cudaMemset(m->att_ws.p, 0, 4 * sizeof(float)));
   m->max_lanes = max_lanes;
   m->max_pages = max_pages;
+  persist_destroy(m->ps);
+  m->ps = nullptr;
+  if (max_lanes == 1) {
+    PersistModel pm;
+    pm.L = (int)c.num_layers;
+    pm.D = (int)c.dim;
+    pm.F = (int)c.hidden;
+    pm.H = (int)c.num_heads;
+    pm.Hkv = (int)c.num_kv_heads;
+    pm.hd = (int)c.head_dim;
+    pm.V = (int)c.vocab;
+    pm.positions = (int)c.max_positions;
+    pm.emb_f32 = m->emb_f32 ? 1 : 0;
+    pm.eps = c.rms_eps;
+    for (auto& Lp : m->layers) {
+      for (FusedWeight* fw : {&Lp->qkv, &Lp->o, &Lp->gu, &Lp->d}) pm.w.push_back(&fw->w);
+      pm.bqkv.push_back(Lp->bqkv.as<float>());
+      pm.in_norm.push_back(Lp->in_norm.as<float>());
+      pm.post_norm.push_back(Lp->post_norm.as<float>());
+    }
+    pm.w.push_back(&m->lm.w);
+    pm.final_norm = m->final_norm.as<float>();
+    pm.embedding = m->embedding.p;
+    pm.rope_cos = m->rope_cos.as<float>();
+    pm.rope_sin = m->rope_sin.as<float>();
+    rc = persist_create(pm, max_lanes, max_pages, &m->ps);
+    if (rc && rc != GLACIER_CUDA_EUNSUPPORTED) return rc;
+  }
   m->gemm = max_lanes > 4 && gemm_tc_supported(m->layers[0]->qkv.w) && gemm_tc_supported(m->layers[0]->o.w) &&
             gemm_tc_supported(m->layers[0]->d.w) && gemm_tc_supported(m->lm.w);
   if (m->gemm) {
@@ -608,6 +640,11 @@ static int step_impl(glacier_cuda_model* m, glacier_cuda_kv* kv, size_t lanes, c
   const size_t D = c.dim, F = c.hidden, B = lanes;
   const size_t max_ctx = max_pages * 16;
   int rc;
+  // One lane, greedy step, one GPU: the persistent kernel runs the whole step.
+  if (m->ps && m->persistent && head == kHeadAllRows && lanes == 1 && !m->tp_comm)
+    return persist_step(m->ps, lanes, tokens, positions, block_tables, max_pages, kv->pool.as<float>(),
+                        kv->page_floats, m->prof.on, eligible, eligible_words, tokens_out,
+                        status_out ? status_out : m->status.as<int32_t>(), logits_out, st);
   float* x = m->x.as<float>();
   float* hn = m->hn.as<float>();
   StepProfiler* prof = m->prof.on ? &m->prof : nullptr;
@@ -668,7 +705,7 @@ static int step_impl(glacier_cuda_model* m, glacier_cuda_kv* kv, size_t lanes, c
     if ((rc = paged_attention(m->q.as<float>(), m->q_dim, kv->pool.as<float>(), kv->page_floats, block_tables,
                               max_pages, m->ctx.as<int32_t>(), max_ctx, B, l, c.num_heads, c.num_kv_heads, c.head_dim,
                               m->gemm ? nullptr : m->attn.as<float>(), m->q_dim, m->att_ws.as<float>(), m->att_floats,
-                              m->att_chunk, st, so_q, prof, GLACIER_CUDA_STEP_ATTN_COMBINE)))
+                              m->att_segs, st, so_q, prof, GLACIER_CUDA_STEP_ATTN_COMBINE)))
       return rc;
     mark(GLACIER_CUDA_STEP_PROJ_O);
     if ((rc = project(L.o.w, m->attn.as<float>(), m->q_dim, so_q, m->map_q, m->proj.as<float>(), D, so_gemm)))
@@ -807,9 +844,30 @@ int glacier_cuda_model_profile(glacier_cuda_model* m, int enable) {
 
 int glacier_cuda_model_profile_read(glacier_cuda_model* m, double* ms, uint64_t* regions, size_t kinds) {
   GLC_REQUIRE(m && ms && regions && kinds > 0, "model_profile_read: null argument");
-  const int rc = bind_device(m);
+  int rc = bind_device(m);
   if (rc) return rc;
-  return m->prof.read(ms, regions, kinds);
+  if ((rc = m->prof.read(ms, regions, kinds))) return rc;
+  if (m->ps) {
+    // Phases of the persistent step, filed under the kernel classes they replace.
+    unsigned long long ns[8], n[8];
+    if ((rc = persist_read_stats(m->ps, ns, n))) return rc;
+    const int kind_of[7] = {GLACIER_CUDA_STEP_PROJ_QKV, GLACIER_CUDA_STEP_ATTENTION,  GLACIER_CUDA_STEP_PROJ_O,
+                            GLACIER_CUDA_STEP_PROJ_GATE_UP, GLACIER_CUDA_STEP_PROJ_DOWN, GLACIER_CUDA_STEP_LM_HEAD,
+                            GLACIER_CUDA_STEP_ARGMAX};
+    for (int i = 0; i < 7; ++i) {
+      const size_t k = (size_t)kind_of[i];
+      if (k >= kinds || n[i] == 0) continue;
+      ms[k] += (double)ns[i] * 1e-6;
+      regions[k] += n[i];
+    }
+  }
+  return GLACIER_CUDA_OK;
+}
+
+int glacier_cuda_model_persistent(glacier_cuda_model* m, int enable) {
+  GLC_REQUIRE(m, "model_persistent: null model");
+  m->persistent = enable != 0;
+  return m->ps ? 1 : 0;
 }
 
 }  // extern "C"

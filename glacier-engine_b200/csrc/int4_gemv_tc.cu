@@ -112,7 +112,7 @@ struct RowScales<__half> {
   __device__ void load(const uint8_t* p) { v = *reinterpret_cast<const uint4*>(p); }
   __device__ float get(int g) const {
     const uint32_t w = g < 2 ? v.x : g < 4 ? v.y : g < 6 ? v.z : v.w;
-    return __half2float(__ushort_as_half((unsigned short)((g & 1) ? (w >> 16) : (w & 0xFFFFu))));
+    return half_to_float_bits((g & 1) ? (w >> 16) : (w & 0xFFFFu));
   }
 };
 template <>

@@ -7,12 +7,14 @@
 // (src/paged_kv_cache.zig:1421-1442); block_tables[lane][logical page] gives
 // the physical page.
 //
-// B200 design (flash-decoding over TMA-fed warps): the context of each
-// (lane, kv head) is cut into chunks; warps claim chunks dynamically and serve
-// all G = H/Hkv query heads of the GQA group from a single read of each K and V
+// B200 design (flash-decoding over TMA-fed warps): the K/V stages of every
+// (lane, kv head) pair are split evenly over all warps of the grid (static
+// stream-K: each warp streams the same number of bytes); a warp serves all
+// G = H/Hkv query heads of the GQA group from a single read of each K and V
 // row (the reference's shared-KV tile, forward.zig:544-620).  A combine kernel
-// merges a lane's chunks with the usual max/sum rescaling, in chunk order
+// merges a pair's segments with the usual max/sum rescaling, in segment order
 // (deterministic).
+#include <algorithm>
 #include <type_traits>
 
 #include "common.cuh"
@@ -34,18 +36,72 @@ struct AttnParams {
   int max_pages;
   const int32_t* ctx_lens;      // [lanes]
   int layer, num_heads, num_kv_heads, head_dim, group;
-  int chunk;                    // positions per split (multiple of 16)
-  int nsplit;                   // splits per (lane, kv head)
+  int warps;                    // warps of the attention grid (W)
+  int nsplit;                   // segment slots per (lane, kv head)
   float scale;
   float* part_o;                // [lanes, H, nsplit, hd]
   float* part_ml;               // [lanes, H, nsplit, 2]  (max, sum)
 };
 
+constexpr int kStagePositions = 8;  // positions per pipeline stage
+constexpr int kMaxPlanLanes = 128;  // lanes one stage plan covers (4 per thread of a warp)
+
+// Static work split shared by the attention and combine kernels (stream-K):
+// the stages (8 positions of one kv head) of every (lane, kv head) pair are
+// laid end to end, lane-major, and warp w of the grid takes stages
+// [w * Q, (w + 1) * Q).  A pair cut by warp boundaries leaves one partial per
+// warp (segment), numbered from the pair's first warp.  Q is the even share,
+// raised when needed so no pair has more than seg_cap segments.  Run by one
+// warp; C[l] = first stage of lane l (C[lanes] = total); plan = {total, Q}.
+__device__ __forceinline__ void attn_stage_plan(const int32_t* __restrict__ ctx_lens, int lanes, int hkv, int warps,
+                                                int seg_cap, int* C, int* plan) {
+  const int lane = threadIdx.x & 31;
+  int v[4], sum = 0, mx = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int idx = 4 * lane + i;
+    const int ns = idx < lanes ? (max(ctx_lens[idx], 0) + kStagePositions - 1) / kStagePositions : 0;
+    v[i] = hkv * ns;
+    sum += v[i];
+    mx = max(mx, ns);
+  }
+  int incl = sum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  int excl = incl - sum;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int idx = 4 * lane + i;
+    if (idx <= lanes) C[idx] = excl;
+    excl += v[i];
+  }
+  const int total = __shfl_sync(0xffffffffu, incl, 31);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  const int q = max(1, max((total + warps - 1) / warps, (mx + seg_cap - 2) / max(1, seg_cap - 1)));
+  if (lane == 0) {
+    plan[0] = total;
+    plan[1] = q;
+  }
+}
+
+// Segments of pair (lane l, kv head h): its stages [P, P + ns) over warps of Q stages.
+__device__ __forceinline__ int attn_pair_segments(const int* C, const int32_t* ctx_lens, int l, int h, int q) {
+  const int ns = (max(ctx_lens[l], 0) + kStagePositions - 1) / kStagePositions;
+  if (ns == 0) return 0;
+  const int P = C[l] + h * ns;
+  return (P + ns - 1) / q - P / q + 1;
+}
+
 // ---------------------------------------------------------------------------
-// TMA-fed persistent form.  Work item = (lane, kv head, chunk of positions);
-// every warp owns a private ring of half-page stages (8 positions of K and V
-// of one kv head) and walks its own list of items (gw, gw + total warps, ...),
-// so no warp ever waits for another:
+// TMA-fed persistent form.  Each warp takes its contiguous share of the stage
+// sequence (attn_stage_plan), i.e. one segment of one or more consecutive
+// (lane, kv head) pairs; it owns a private ring of half-page stages (8
+// positions of K and V of one kv head), so no warp ever waits for another and
+// every warp streams the same number of K/V bytes:
 //   * lane 0 streams each stage's K and V tiles (8 rows x HD floats, two 2D TMA
 //     boxes over the pool viewed as [rows, kv_dim]) into the next free slot,
 //     running kAttnStages stages ahead across item boundaries;
@@ -55,10 +111,10 @@ struct AttnParams {
 //     lanes (16p + 2h, 16p + 2h + 1) with the score of position p, head h;
 //   * online softmax per stage (running max and sum per head, acc rescaled);
 //   * P.V: lanes over head dims, V rows and probabilities from shared memory.
-// Each item writes one (max, sum, unnormalised o) partial for the combine.
+// Each segment writes one (max, sum, unnormalised o) partial for the combine.
 constexpr int kAttnWarps = 8;   // warps per CTA (one CTA per SM)
 constexpr int kAttnStages = 3;  // half-page stages per warp
-constexpr int kStageRows = 8;   // positions per stage
+constexpr int kStageRows = kStagePositions;
 
 __device__ __forceinline__ void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
@@ -74,7 +130,7 @@ __device__ __forceinline__ float ex2_approx(float x) {
 template <int HD, int NG>
 __global__ void __launch_bounds__(kAttnWarps * 32, 1)
     attn_tma_kernel(const __grid_constant__ CUtensorMap kvmap, const AttnParams p, int lanes, int rows_per_page,
-                    int* work_counter, int* err) {
+                    int* err) {
   constexpr int TILE = kStageRows * HD;  // floats per K (or V) stage tile of one kv head
   constexpr int DL = HD / 16;            // score phase: dims per lane (16 lanes per position)
   constexpr int DL4 = DL / 4;
@@ -84,10 +140,12 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
   __shared__ uint64_t bars[kAttnWarps][kAttnStages];
   __shared__ __align__(16) float scr_all[kAttnWarps][kStageRows * kMaxGroup];
   __shared__ __align__(16) float2 prb_all[kAttnWarps][kStageRows * kMaxGroup];  // {p, p} per (position, head)
-  __shared__ int queue[kAttnWarps][8];  // items claimed by lane 0, in issue order (-1 ends the list)
+  __shared__ int queue[kAttnWarps][8];  // pairs queued by lane 0, in issue order (-1 ends the list)
+  __shared__ int Cs[kMaxPlanLanes + 1];
+  __shared__ int plan[2];
 
   griddep_launch();
-  griddep_wait();  // q, the KV pages and the work counter come from earlier kernels
+  griddep_wait();  // q, the KV pages and the context lengths come from earlier kernels
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int l16 = lane & 15, ph = lane >> 4;
   float* ring = sm + (size_t)warp * kAttnStages * 2 * TILE;
@@ -95,45 +153,54 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
   float2* prb = prb_all[warp];
   constexpr int G = NG;
   const int Hkv = p.num_kv_heads;
-  const int total = lanes * Hkv * p.nsplit;
+  if (warp == 0) attn_stage_plan(p.ctx_lens, lanes, Hkv, p.warps, p.nsplit, Cs, plan);
   if (lane == 0) {
     for (int i = 0; i < kAttnStages; ++i) mbar_init(&bars[warp][i], 1);
     fence_mbar_init();
   }
-  __syncwarp();
-
-  // Items are numbered split-major (all lanes' first chunks, then the second
-  // ones, ...) and claimed dynamically, so long contexts do not pile up on
-  // some warps.  Stages of item `it` (0 when the chunk lies past the context).
-  auto item_stages = [&](int it, int& lid, int& kvh, int& split, int& n) {
-    split = it / (lanes * Hkv);
-    const int r = it - split * lanes * Hkv;
-    lid = r / Hkv;
-    kvh = r - lid * Hkv;
-    const int ctx = p.ctx_lens[lid];
-    const int j0 = split * p.chunk;
-    n = max(0, min(ctx, j0 + p.chunk) - j0);
-    return (n + kStageRows - 1) / kStageRows;
+  __syncthreads();
+  const int total = plan[0], Q = plan[1];
+  const int gw = blockIdx.x * kAttnWarps + warp;
+  const int g0 = min(total, gw * Q), g1 = min(total, g0 + Q);  // this warp's stages
+  // Pair geometry: stages ns of lane l, first stage P of (l, h), this warp's part [sb, se).
+  auto pair_span = [&](int pair, int& lid, int& kvh, int& P, int& sb, int& se) {
+    lid = pair / Hkv;
+    kvh = pair - lid * Hkv;
+    const int ns = (max(p.ctx_lens[lid], 0) + kStageRows - 1) / kStageRows;
+    P = Cs[lid] + kvh * ns;
+    sb = max(0, g0 - P);
+    se = min(ns, g1 - P);
   };
+  // First pair of the warp: the lane whose stages hold g0 (largest l with C[l] <= g0).
+  int first_pair = lanes * Hkv;
+  if (g0 < g1) {
+    int lo = 0, hi = lanes - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (Cs[mid] <= g0) lo = mid; else hi = mid - 1;
+    }
+    const int ns = (max(p.ctx_lens[lo], 0) + kStageRows - 1) / kStageRows;
+    first_pair = lo * Hkv + min(Hkv - 1, (g0 - Cs[lo]) / max(ns, 1));
+  }
 
   // ---- issue cursor (lane 0): the next stage of this warp's sequence ----
-  int c_item = 0, c_st = 0, c_ns = 0, c_lid = 0, c_kvh = 0, c_split = 0, c_n = 0;
+  int c_pair = first_pair - 1, c_st = 0, c_se = 0, c_lid = 0, c_kvh = 0;
   uint32_t claimed = 0;
-  bool drained = false;  // no work left to claim (the -1 marker is queued)
-  auto claim = [&]() {  // lane 0: next non-empty item into the queue, or the end marker
+  bool drained = false;  // no pair left (the -1 marker is queued)
+  auto claim = [&]() {  // lane 0: next pair with stages in [g0, g1) into the queue, or the end marker
     while (true) {
-      const int it = atomicAdd(work_counter, 1);
-      if (it >= total) {
+      ++c_pair;
+      int P, sb, se;
+      if (c_pair < lanes * Hkv) pair_span(c_pair, c_lid, c_kvh, P, sb, se);
+      if (c_pair >= lanes * Hkv || P >= g1) {
         queue[warp][claimed++ & 7] = -1;
         drained = true;
         return;
       }
-      const int ns = item_stages(it, c_lid, c_kvh, c_split, c_n);
-      if (ns > 0) {
-        c_item = it;
-        c_ns = ns;
-        c_st = 0;
-        queue[warp][claimed++ & 7] = it;
+      if (sb < se) {
+        c_st = sb;
+        c_se = se;
+        queue[warp][claimed++ & 7] = c_pair;
         return;
       }
     }
@@ -147,12 +214,12 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
   uint32_t issued = 0;
   auto issue_next = [&]() {  // lane 0 only
     if (drained) return;
-    if (c_st >= c_ns) {
+    if (c_st >= c_se) {
       claim();
       if (drained) return;
     }
     const int s = issued % kAttnStages;
-    const int j = c_split * p.chunk + c_st * kStageRows;  // first position of the stage
+    const int j = c_st * kStageRows;  // first position of the stage
     const int phys = p.block_tables[(size_t)c_lid * p.max_pages + (j >> 4)];
     const int yk = phys * rows_per_page + p.layer * 32 + (j & 15);
     float* dst = ring + (size_t)s * 2 * TILE;
@@ -171,9 +238,10 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
     __syncwarp();
     const int item = queue[warp][taken++ & 7];
     if (item < 0) break;
-    int lid, kvh, split, n;
-    const int nst = item_stages(item, lid, kvh, split, n);
-    const size_t part_base = ((size_t)lid * p.num_heads + (size_t)kvh * G) * p.nsplit + split;
+    int lid, kvh, P, sb, se;
+    pair_span(item, lid, kvh, P, sb, se);
+    const int nst = se - sb, ctx = p.ctx_lens[lid];
+    const size_t part_base = ((size_t)lid * p.num_heads + (size_t)kvh * G) * p.nsplit + (gw - P / Q);
     // q of the G heads, scaled by 1/sqrt(hd) * log2(e) (softmax in base 2), this
     // lane's dims 4*l16 + 64*i + c.
     const float qs = p.scale * kLog2e;
@@ -205,7 +273,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
       }
       const float* Kt = ring + (size_t)s * 2 * TILE;
       const float* Vt = Kt + TILE;
-      const int nvalid = min(kStageRows, n - kStageRows * st);
+      const int nvalid = min(kStageRows, ctx - kStageRows * (sb + st));
       // -- scores (base-2 logits) for 8 positions, 2 per step --
 #pragma unroll
       for (int step = 0; step < kStageRows / 2; ++step) {
@@ -338,21 +406,13 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
     }
   }
   // Leave no copy in flight (a wait that gave up leaves some outstanding).
-  if (lane == 0) {
+  if (lane == 0)
     for (uint32_t i = consumed; i < issued; ++i) mbar_wait(&bars[warp][i % kAttnStages], (i / kAttnStages) & 1, err);
-    // The last warp to finish zeroes the work counters for the next launch.
-    __threadfence();
-    if (atomicAdd(work_counter + 1, 1) == (int)(gridDim.x * kAttnWarps) - 1) {
-      work_counter[0] = 0;
-      work_counter[1] = 0;
-      __threadfence();
-    }
-  }
   __syncwarp();
 }
 
-// out[lane, h, :] = sum_s o_s * e^(m_s - M) / sum_s l_s * e^(m_s - M), in chunk
-// order.  One CTA per (lane, block of heads): a warp per head computes the chunk
+// out[lane, h, :] = sum_s o_s * e^(m_s - M) / sum_s l_s * e^(m_s - M), in segment
+// order.  One CTA per (lane, block of heads): a warp per head computes the segment
 // weights once, then each thread combines 8 consecutive values of one head from
 // registers and writes them as fp32 or, for the o-projection GEMM, in split form
 // with the lane's row max from one block reduction (one block of all heads).
@@ -360,20 +420,27 @@ __global__ void __launch_bounds__(1024) attn_combine_kernel(const float* __restr
                                                             const float* __restrict__ part_ml, int nsplit,
                                                             int head_dim, int num_heads, float* __restrict__ out,
                                                             size_t ldo, SplitOut so,
-                                                            const int32_t* __restrict__ ctx_lens, int chunk,
-                                                            int heads_per_block) {
+                                                            const int32_t* __restrict__ ctx_lens, int lanes,
+                                                            int num_kv_heads, int warps_total, int heads_per_block) {
   griddep_launch();
   griddep_wait();
-  extern __shared__ float wts[];  // [num_heads][nsplit] chunk weights
+  extern __shared__ float wts[];  // [num_heads][nsplit] segment weights
   __shared__ float2 sh[32];
   __shared__ __align__(8) float2 xch;
+  __shared__ int Cs[kMaxPlanLanes + 1], plan[2], segs[kMaxPlanLanes];
   const int lane_id = blockIdx.x;
   const int head0 = blockIdx.y * heads_per_block;
   const int nh = min(heads_per_block, num_heads - head0);
-  // Only the chunks that hold part of this lane's context have partials.
-  const int nsplit_lane = min(nsplit, (ctx_lens[lane_id] + chunk - 1) / chunk);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  // The segments each head of this lane was cut into (the attention kernel's plan).
+  if (warp == 0) attn_stage_plan(ctx_lens, lanes, num_kv_heads, warps_total, nsplit, Cs, plan);
+  __syncthreads();
+  const int group = num_heads / num_kv_heads;
+  for (int t = threadIdx.x; t < nh; t += blockDim.x)
+    segs[t] = attn_pair_segments(Cs, ctx_lens, lane_id, (head0 + t) / group, plan[1]);
+  __syncthreads();
   for (int t = warp; t < nh; t += nwarps) {
+    const int nsplit_lane = segs[t];
     const size_t base = ((size_t)lane_id * num_heads + head0 + t) * nsplit;
     if (nsplit_lane <= 32) {  // one chunk per lane of the warp: one load of (max, sum)
       const float2 ml = lane < nsplit_lane ? *reinterpret_cast<const float2*>(part_ml + (base + lane) * 2)
@@ -407,6 +474,7 @@ __global__ void __launch_bounds__(1024) attn_combine_kernel(const float* __restr
     const int t = e0 / head_dim, d = e0 - t * head_dim;
     const float* po = part_o + ((size_t)lane_id * num_heads + head0 + t) * nsplit * head_dim + d;
     const float* wt = wts + t * nsplit;
+    const int nsplit_lane = segs[t];
 #pragma unroll 4
     for (int s = 0; s < nsplit_lane; ++s) {
       float v[8];
@@ -440,14 +508,18 @@ __global__ void __launch_bounds__(W * 32) attn_combine_head_kernel(const float* 
                                                                    const float* __restrict__ part_ml, int nsplit,
                                                                    int head_dim, int num_heads,
                                                                    float* __restrict__ out, size_t ldo,
-                                                                   const int32_t* __restrict__ ctx_lens, int chunk) {
+                                                                   const int32_t* __restrict__ ctx_lens, int lanes,
+                                                                   int num_kv_heads, int warps_total) {
   griddep_launch();
   griddep_wait();
   extern __shared__ float wts[];  // [nsplit]
   __shared__ float4 part[W][32];
+  __shared__ int Cs[kMaxPlanLanes + 1], plan[2];
   const int lane_id = blockIdx.x, head = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nsplit_lane = min(nsplit, (ctx_lens[lane_id] + chunk - 1) / chunk);
+  if (warp == 0) attn_stage_plan(ctx_lens, lanes, num_kv_heads, warps_total, nsplit, Cs, plan);
+  __syncthreads();
+  const int nsplit_lane = attn_pair_segments(Cs, ctx_lens, lane_id, head / (num_heads / num_kv_heads), plan[1]);
   const size_t base = ((size_t)lane_id * num_heads + head) * nsplit;
   if (warp == 0) {
     float M = -INFINITY;
@@ -498,22 +570,19 @@ __global__ void __launch_bounds__(W * 32) attn_combine_head_kernel(const float* 
 
 // Workspace floats needed by paged_attention for the given split count.
 size_t attention_workspace_floats(size_t lanes, size_t num_heads, size_t head_dim, size_t nsplit) {
-  return 4 + lanes * num_heads * nsplit * (head_dim + 2);  // work counters + chunk partials
+  return 4 + lanes * num_heads * nsplit * (head_dim + 2);  // 4 reserved + segment partials
 }
 
-// Positions per work item: 512 (32 pages) unless that leaves fewer than two
-// items per warp of the persistent grid, then halved down to 16 (few lanes:
-// short items spread one context over many SMs).  The combine keeps one weight
-// per (head, chunk) in 48 KB of shared memory, which bounds the chunk count.
-int attention_chunk(size_t lanes, size_t num_heads, size_t num_kv_heads, size_t max_ctx) {
-  const size_t warps = (size_t)sm_count() * kAttnWarps;
-  const size_t max_split = (48 * 1024) / (sizeof(float) * num_heads);
-  size_t chunk = 512;
-  while (ceil_div(max_ctx, chunk) > max_split) chunk *= 2;
-  while (chunk > 16 && lanes * num_kv_heads * ceil_div(max_ctx, chunk) < 2 * warps &&
-         ceil_div(max_ctx, chunk / 2) <= max_split)
-    chunk /= 2;
-  return (int)chunk;
+// Segment slots per (lane, kv head): as many as the combine's weight table (one
+// float per head and segment in 48 KB of shared memory) and a 64 MiB partial
+// buffer allow, and no more than a context of max_ctx can use.  Few lanes get
+// many slots (one context spread over every warp); 64 lanes get ~70, while the
+// even share of such a batch cuts a pair into about a dozen segments.
+int attention_segments(size_t lanes, size_t num_heads, size_t head_dim, size_t max_ctx) {
+  const size_t by_smem = (48 * 1024) / (sizeof(float) * num_heads);
+  const size_t by_mem = ((size_t)64 << 20) / (lanes * num_heads * (head_dim + 2) * sizeof(float));
+  const size_t by_ctx = ceil_div(max_ctx, (size_t)kStagePositions) + 1;
+  return (int)std::max<size_t>(2, std::min({by_smem, std::max<size_t>(16, by_mem), by_ctx}));
 }
 
 int attn_device_error(int clear) {
@@ -560,7 +629,7 @@ static int attn_kv_map(const float* pool, size_t kv_dim, size_t head_dim, const 
 int paged_attention(const float* q, size_t ldq, const float* pool, size_t page_floats, const int32_t* block_tables,
                     size_t max_pages, const int32_t* ctx_lens, size_t max_ctx, size_t lanes, size_t layer,
                     size_t num_heads, size_t num_kv_heads, size_t head_dim, float* out, size_t ldo, float* workspace,
-                    size_t workspace_floats, int chunk, cudaStream_t stream, SplitOut so, StepProfiler* prof,
+                    size_t workspace_floats, int seg_cap, cudaStream_t stream, SplitOut so, StepProfiler* prof,
                     int combine_kind) {
   GLC_REQUIRE(q && pool && block_tables && ctx_lens && (out || so.xs) && workspace, "paged_attention: null argument");
   GLC_REQUIRE(num_kv_heads > 0 && num_heads % num_kv_heads == 0, "paged_attention: heads %zu / kv heads %zu",
@@ -570,9 +639,9 @@ int paged_attention(const float* q, size_t ldq, const float* pool, size_t page_f
               "paged_attention: group %zu / head_dim %zu outside the kernel contract", group, head_dim);
   GLC_REQUIRE(max_ctx > 0 && max_ctx <= max_pages * 16, "paged_attention: context %zu exceeds the block table",
               max_ctx);
-  if (chunk <= 0) chunk = attention_chunk(lanes, num_heads, num_kv_heads, max_ctx);
-  GLC_REQUIRE(chunk % 16 == 0, "paged_attention: chunk must be whole pages");
-  const int nsplit = (int)ceil_div(max_ctx, (size_t)chunk);
+  if (seg_cap <= 1) seg_cap = attention_segments(lanes, num_heads, head_dim, max_ctx);
+  GLC_REQUIRE(lanes <= (size_t)kMaxPlanLanes, "paged_attention: at most %d lanes per launch", kMaxPlanLanes);
+  const int nsplit = seg_cap;
   GLC_REQUIRE(workspace_floats >= attention_workspace_floats(lanes, num_heads, head_dim, nsplit),
               "paged_attention: workspace too small");
   AttnParams prm;
@@ -588,7 +657,8 @@ int paged_attention(const float* q, size_t ldq, const float* pool, size_t page_f
   prm.num_kv_heads = (int)num_kv_heads;
   prm.head_dim = (int)head_dim;
   prm.group = (int)group;
-  prm.chunk = chunk;
+  const int grid = sm_count();
+  prm.warps = grid * kAttnWarps;
   prm.nsplit = nsplit;
   prm.scale = 1.0f / sqrtf((float)head_dim);
   // Workspace: two work counters (4 floats reserved), then the chunk partials.
@@ -601,7 +671,7 @@ int paged_attention(const float* q, size_t ldq, const float* pool, size_t page_f
   int rc = attn_kv_map(pool, kv_dim, head_dim, &kvmap);
   if (rc) return rc;
   const size_t smem = (size_t)kAttnWarps * kAttnStages * 2 * kStageRows * head_dim * sizeof(float);
-  using Kern = void (*)(const CUtensorMap, const AttnParams, int, int, int*, int*);
+  using Kern = void (*)(const CUtensorMap, const AttnParams, int, int, int*);
   Kern kern = nullptr;
 #define GLC_ATTN_CASE(hd, ng) \
   if (head_dim == hd && group == ng) kern = attn_tma_kernel<hd, ng>;
@@ -614,22 +684,17 @@ int paged_attention(const float* q, size_t ldq, const float* pool, size_t page_f
   if ((rc = allow_dynamic_smem((const void*)kern, (int)smem))) return rc;
   int* err = device_symbol_address(g_attn_error);
   GLC_REQUIRE(err != nullptr, "paged_attention: device status word unavailable");
-  const size_t items = lanes * num_kv_heads * (size_t)nsplit;
-  // Up to one CTA per item: with few items (few lanes) their K/V streams still
-  // spread over as many SMs as there are items.
-  const int grid = (int)std::min<size_t>((size_t)sm_count(), items);
-  // The two work counters at the start of the workspace start at zero (the
-  // caller clears them once) and the kernel leaves them at zero.
-  int* counter = reinterpret_cast<int*>(workspace);
+  // One CTA per SM; every warp streams the same number of K/V stages.
   if ((rc = launch_pdl(kern, dim3(grid), dim3(kAttnWarps * 32), smem, stream, 1, *kvmap, prm, (int)lanes,
-                       (int)(page_floats / kv_dim), counter, err)))
+                       (int)(page_floats / kv_dim), err)))
     return rc;
   if (prof) prof->mark(combine_kind, stream);
   {
     GLC_REQUIRE(head_dim % 8 == 0 && ldo % 4 == 0 && (num_heads * head_dim) / 8 <= 1024,
                 "paged_attention: combine geometry %zu x %zu unsupported", num_heads, head_dim);
     const size_t csmem = num_heads * (size_t)nsplit * sizeof(float);
-    GLC_REQUIRE(csmem <= 48 * 1024, "paged_attention: %d chunks per lane exceed the combine's shared memory", nsplit);
+    GLC_REQUIRE(csmem <= 48 * 1024, "paged_attention: %d segments per lane exceed the combine's shared memory",
+                nsplit);
     // The split output needs the lane's row max over all heads (one block per
     // lane); fp32 output with few lanes takes a block per (lane, head).
     if (!so.xs && lanes * num_heads < (size_t)sm_count()) {
@@ -638,10 +703,10 @@ int paged_attention(const float* q, size_t ldq, const float* pool, size_t page_f
       if (nsplit > 64)
         return launch_pdl(attn_combine_head_kernel<32>, hgrid, dim3(1024), (size_t)nsplit * sizeof(float), stream, 1,
                           (const float*)prm.part_o, (const float*)prm.part_ml, nsplit, (int)head_dim,
-                          (int)num_heads, out, ldo, ctx_lens, chunk);
+                          (int)num_heads, out, ldo, ctx_lens, (int)lanes, (int)num_kv_heads, prm.warps);
       return launch_pdl(attn_combine_head_kernel<8>, hgrid, dim3(256), (size_t)nsplit * sizeof(float), stream, 1,
                         (const float*)prm.part_o, (const float*)prm.part_ml, nsplit, (int)head_dim, (int)num_heads,
-                        out, ldo, ctx_lens, chunk);
+                        out, ldo, ctx_lens, (int)lanes, (int)num_kv_heads, prm.warps);
     }
     const size_t hpb = num_heads;
     // One warp per head for the weights (up to 32 warps), enough threads for 8 values each.
@@ -650,7 +715,7 @@ int paged_attention(const float* q, size_t ldq, const float* pool, size_t page_f
     const dim3 cgrid((unsigned)lanes, (unsigned)ceil_div(num_heads, hpb));
     if ((rc = launch_pdl(attn_combine_kernel, cgrid, dim3(threads), hpb * (size_t)nsplit * sizeof(float), stream, 1,
                          (const float*)prm.part_o, (const float*)prm.part_ml, nsplit, (int)head_dim, (int)num_heads,
-                         out, ldo, so, ctx_lens, chunk, (int)hpb)))
+                         out, ldo, so, ctx_lens, (int)lanes, (int)num_kv_heads, prm.warps, (int)hpb)))
       return rc;
   }
   return GLACIER_CUDA_OK;

@@ -328,6 +328,15 @@ enum glacier_cuda_step_kind {
 int glacier_cuda_model_profile(glacier_cuda_model *model, int enable);
 int glacier_cuda_model_profile_read(glacier_cuda_model *model, double *ms, uint64_t *regions, size_t kinds);
 
+/* Step selection, no reference counterpart.  A model reserved for one lane runs each greedy
+ * decode step (glacier_cuda_decode_step) as one persistent kernel over every SM, with the
+ * phases of the step separated by grid barriers, when enable = 1; enable = 0 (the default)
+ * runs the multi-kernel step (the same operators, one launch per kernel class).  Returns 1 when the persistent step is built for the current reservation, 0 when the
+ * model or reservation is outside its contract (more than one lane; not group 32 with fp16
+ * scales; head dim other than 64 / 128), negative on error.  With profiling on, its phases
+ * are filed under the kernel classes they replace. */
+int glacier_cuda_model_persistent(glacier_cuda_model *model, int enable);
+
 /* ------------------------------------------------------------------------
  * Persistent INT4 weight handles: the Metal persistent-weight API
  * (src/backends/metal/backend.zig:571-595, shim.m:4005-4111, 5502-5624) on
