@@ -299,10 +299,11 @@ def run_glacier(args):
     t0 = time.time()
     cfg, model = bench_model(args)
     if tp > 1:
-        dm = DeviceModel(TensorParallelShard(model, rank, tp), max_positions=max_pages * 16)
+        shard = TensorParallelShard(model, rank, tp)
+        dm = DeviceModel(shard, max_positions=max_pages * 16)
         uid = [tp_unique_id() if rank == 0 else None]
         torch.distributed.broadcast_object_list(uid, src=0)
-        dm.enable_tensor_parallel(rank, tp, uid[0])
+        dm.enable_tensor_parallel(rank, tp, uid[0], shard.lane_groups, shard.lane_index)
     else:
         dm = DeviceModel(model, max_positions=max_pages * 16)
     sess = DecodeSession(dm, lanes, max_pages)
@@ -923,22 +924,23 @@ def strong_scaling(torch, dm, cfg, args, ws, rank, lanes_total: int = 64) -> dic
 def tp_pass(torch, model, cfg, args, ws, rank) -> dict:
     """Tensor parallelism over the N ranks (Megatron split: each rank holds H/N q heads, Hkv/N kv
     heads, F/N FFN rows and the matching o / down columns; an NCCL all-reduce after o and after
-    down): one 64-lane job with the headline's contexts.  Reports whole-job tok/s (max over
+    down; with more ranks than kv heads, N/Hkv ranks share a kv-head group and split its lanes):
+    one 64-lane job with the headline's contexts.  Reports whole-job tok/s (max over
     ranks of the device time) and the all-reduce share of the profiled step."""
     import ctypes as C
     from glacier_b200 import _lib
     from glacier_b200.model import DecodeSession, DeviceModel, TensorParallelShard, tp_unique_id
-    c = model.cfg
-    if c["num_heads"] % ws or c["num_kv_heads"] % ws or c["hidden"] % (ws * c["group"]):
-        return {"unavailable": f"{c['num_heads']} q / {c['num_kv_heads']} kv heads do not split over {ws} GPUs "
-                               "(the Megatron split needs whole kv heads per GPU)"}
+    try:
+        shard = TensorParallelShard(model, rank, ws)
+    except ValueError as e:
+        return {"unavailable": str(e)}
     lanes = 64
     ctxs = lane_contexts(args, lanes, 0)
     max_pages = -(-(int(ctxs.max()) + args.warmup + args.steps + args.profile_steps + 2) // 16)
-    dm = DeviceModel(TensorParallelShard(model, rank, ws), max_positions=max_pages * 16)
+    dm = DeviceModel(shard, max_positions=max_pages * 16)
     uid = [tp_unique_id() if rank == 0 else None]
     torch.distributed.broadcast_object_list(uid, src=0)
-    dm.enable_tensor_parallel(rank, ws, uid[0])
+    dm.enable_tensor_parallel(rank, ws, uid[0], shard.lane_groups, shard.lane_index)
     sess = DecodeSession(dm, lanes, max_pages)
     _random_pages(torch, sess, args.seed + 99 + rank)
     sess.tokens.fill_(1)
@@ -977,7 +979,9 @@ def tp_pass(torch, model, cfg, args, ws, rank) -> dict:
     ms, share = max_over_ranks([ms, share], ws, torch.device("cuda", torch.cuda.current_device()))
     return {"lanes": lanes, "tp": ws, "tok_s": lanes * args.steps / (ms / 1e3), "ms_per_step": ms / args.steps,
             "all_reduce_share": share, "scaling": "strong",
-            "parallelism": f"tensor parallel x{ws} (Megatron split, NCCL all-reduce of o and down, 2 per layer)"}
+            "parallelism": f"tensor parallel x{ws} (Megatron split, NCCL all-reduce of o and down, 2 per layer"
+                           + (f"; {shard.lane_groups} ranks per kv-head group split its lanes)" if shard.lane_groups > 1
+                              else ")")}
 
 
 def run_prefill(args):

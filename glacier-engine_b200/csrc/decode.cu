@@ -126,11 +126,16 @@ __global__ void prefill_rows_kernel(const int32_t* __restrict__ table, int max_p
   for (int j = threadIdx.x; j < max_pages; j += blockDim.x) tables[(size_t)i * max_pages + j] = table[j];
 }
 
-__global__ void ctx_from_pos_kernel(const int32_t* __restrict__ pos, int32_t* __restrict__ ctx, int n) {
+// Attention context of each lane: position + 1.  With a lane split (tensor
+// parallelism with more ranks than kv heads) a rank attends only the lanes
+// b with b % groups == index; the others get context 0, so their attention
+// output is zero and the all-reduce of o sums each lane's heads from its owners.
+__global__ void ctx_from_pos_kernel(const int32_t* __restrict__ pos, int32_t* __restrict__ ctx, int n, int groups,
+                                    int index) {
   griddep_launch();
   griddep_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < n) ctx[i] = pos[i] + 1;
+  if (i < n) ctx[i] = (i % groups == index) ? pos[i] + 1 : 0;
 }
 
 struct DevBuf {
@@ -265,6 +270,7 @@ struct glacier_cuda_model {
   // Tensor parallelism: this rank's NCCL communicator (nullptr: one GPU).
   void* tp_comm = nullptr;
   int tp_rank = 0, tp_world = 1;
+  int tp_lane_groups = 1, tp_lane_index = 0;  // lanes this rank attends: b % groups == index
   // One-lane reservations: the whole decode step as one persistent kernel
   // (decode_persistent.cu) when switched on (glacier_cuda_model_persistent).
   PersistState* ps = nullptr;
@@ -653,7 +659,7 @@ static int step_impl(glacier_cuda_model* m, glacier_cuda_kv* kv, size_t lanes, c
   };
   mark(GLACIER_CUDA_STEP_EMBED);
   if ((rc = launch_pdl(ctx_from_pos_kernel, dim3((unsigned)ceil_div(B, 128)), dim3(128), 0, st, 1, positions,
-                       m->ctx.as<int32_t>(), (int)B)))
+                       m->ctx.as<int32_t>(), (int)B, m->tp_lane_groups, m->tp_lane_index)))
     return rc;
   if ((rc = m->emb_f32 ? embed_gather(m->embedding.as<float>(), c.vocab, D, tokens, B, x, D, st)
                        : embed_gather(m->embedding.as<__half>(), c.vocab, D, tokens, B, x, D, st)))
@@ -833,6 +839,14 @@ int glacier_cuda_model_tp_init(glacier_cuda_model* m, int rank, int world, const
   m->tp_comm = comm;
   m->tp_rank = rank;
   m->tp_world = world;
+  return GLACIER_CUDA_OK;
+}
+
+int glacier_cuda_model_tp_lanes(glacier_cuda_model* m, int groups, int index) {
+  GLC_REQUIRE(m && m->tp_comm, "model_tp_lanes: tensor parallelism not set up");
+  GLC_REQUIRE(groups >= 1 && index >= 0 && index < groups, "model_tp_lanes: lane group %d of %d", index, groups);
+  m->tp_lane_groups = groups;
+  m->tp_lane_index = index;
   return GLACIER_CUDA_OK;
 }
 

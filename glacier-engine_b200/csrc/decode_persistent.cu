@@ -53,6 +53,7 @@ constexpr int kStage = kNib + kScl;
 constexpr int kMaxB = 4;
 constexpr int kMaxG = 8;
 constexpr int kNumMats = 5;              // qkv, o, gate_up, down, lm_head
+constexpr int kSegSlots = 32;            // per-CTA segment counters (a warp runs at most a ring ahead)
 enum { kQKV = 0, kO = 1, kGU = 2, kDN = 3, kLM = 4 };
 // Device error words: 1 = a wait gave up, 2 = a token or position out of range.
 constexpr int kErrBadInput = 2;
@@ -211,6 +212,7 @@ struct Smem {
   unsigned* relcnt;  // [ring] warps that released the slot's current stage
   int* nstage;       // [5] stages of each matrix per layer (this CTA), [5] = all stages
   unsigned* issued;  // [1] highest stage sequence number issued + 1
+  unsigned* segcnt;  // [kSegSlots] warps that ended the CTA's segment of that sequence number
   uint4* xfrag;   // [slots][8 blocks][8 * B lanes]
   float* xs;      // [B][D] normalised rows / scratch
   float* qs;      // [G][hd] rotated, scaled q of the current attention item
@@ -226,6 +228,7 @@ struct Ctx {
   int cta, nct, tid, warp, lane;
   unsigned target;      // grid barrier arrivals expected so far (thread 0)
   unsigned ring_pos;    // consumer position in the stage sequence
+  unsigned seg_seq;     // segments this warp has ended
   int ring_slot;        // ring_pos mod ring
   uint32_t ring_par;    // (ring_pos / ring) & 1
   bool ok;
@@ -386,87 +389,75 @@ __device__ void issue_stage(const PParams& p, Smem& s, int cta, unsigned seq) {
   atomicMax(s.issued, seq + 1);
 }
 
-// Tile fixup, run by the CTA that finished a tile's K range last: every row of
-// the tile is the sum of its 2 * nseg partial rows (segments in order, each one's
-// two K-halves in order; four threads per row take consecutive quarters, added
-// in quarter order), written to out[m].  For the LM head it also leaves the
-// tile's best eligible logit per lane (argmaxEligible, sampling.zig:55-107:
-// lowest index among equal values, eligible NaN flagged, eligible count).
-__device__ void tile_fixup(Ctx& c, int m, int tile) {
+// Tile fixup by one warp of the CTA that finished a tile's K range last (the
+// other warps keep streaming): every row of the tile is the sum of its
+// 2 * nseg partial rows in order (segments in order, each one's two K-halves in
+// order), written to out[m]; lane L takes rows L, L + 32, L + 64, L + 96.  For
+// the LM head it also leaves the tile's best eligible logit per lane
+// (argmaxEligible, sampling.zig:55-107: lowest index among equal values,
+// eligible NaN flagged, eligible count).
+__device__ void warp_fixup(Ctx& c, int m, int tile) {
   const PParams& p = c.p;
   const MatPlan& mp = p.mp[m];
   const int n = 2 * seg_count(mp, tile);
   const int rows = min(kTileRows, mp.M - tile * kTileRows);
-  const int item = c.tid >> 2, q = c.tid & 3;  // 128 rows of 4 threads
-  const int per_q = (n + 3) / 4;
   const size_t stride = (size_t)p.B * mp.M;
+  __threadfence();  // acquire: the other warps' and CTAs' partial rows are published
   for (int b = 0; b < p.B; ++b) {
-    const int row = tile * kTileRows + item;
-    float v = 0.f;
-    if (item < rows) {
-      const float* base = p.part[m] + (size_t)b * mp.M + row;
-      const int j0 = q * per_q, j1 = min(n, j0 + per_q);
-      float t[8];
+    const float* base = p.part[m] + (size_t)b * mp.M + tile * kTileRows;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int j0 = 0; j0 < n; j0 += 4) {
+      float t[4][4];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) t[u] = j0 + u < j1 ? __ldcg(base + (size_t)(j0 + u) * stride) : 0.f;
+      for (int u = 0; u < 4; ++u)
 #pragma unroll
-      for (int u = 0; u < 8; ++u)
-        if (j0 + u < j1) v += t[u];
-      for (int j = j0 + 8; j < j1; ++j) v += __ldcg(base + (size_t)j * stride);
-    }
-    // Quarters in order: lane q = 0 of each row ends with ((s0 + s1) + s2) + s3.
-    const float s1 = __shfl_down_sync(0xffffffffu, v, 1), s2 = __shfl_down_sync(0xffffffffu, v, 2),
-                s3 = __shfl_down_sync(0xffffffffu, v, 3);
-    const bool own = q == 0 && item < rows;
-    const float y = ((v + s1) + s2) + s3;
-    if (own && p.out[m]) p.out[m][(size_t)b * mp.M + row] = y;
-    if (m == kLM) {
-      // The tile's best eligible logit of lane b.
-      const uint64_t* wr = p.words ? p.words + (size_t)b * p.word_count : nullptr;
-      const bool elig = own && (!wr || ((wr[row >> 6] >> (row & 63)) & 1ull));
-      Cand cd{0.f, -1};
-      int nan = 0;
-      if (elig) {
-        if (y != y) nan = 1;
-        else cd = Cand{y, row};
-      }
-      cd = warp_best(cd);
-      nan = __reduce_or_sync(0xffffffffu, nan);
-      const int cnt = __reduce_add_sync(0xffffffffu, elig ? 1 : 0);
-      float* rv = c.s.red;
-      int* ri = reinterpret_cast<int*>(c.s.red + 16);
-      int* rf = reinterpret_cast<int*>(c.s.red + 32);
-      if (c.lane == 0) {
-        rv[c.warp] = cd.v;
-        ri[c.warp] = cd.i;
-        rf[2 * c.warp] = nan;
-        rf[2 * c.warp + 1] = cnt;
-      }
-      cbar();
-      if (c.tid == 0) {
-        Cand bb{rv[0], ri[0]};
-        int fl = rf[0], el = rf[1];
-        for (int w = 1; w < kCW; ++w) {
-          const Cand t{rv[w], ri[w]};
-          if (better(t, bb)) bb = t;
-          fl |= rf[2 * w];
-          el += rf[2 * w + 1];
+        for (int r = 0; r < 4; ++r) {
+          const int row = c.lane + 32 * r;
+          t[u][r] = (j0 + u < n && row < rows) ? __ldcg(base + (size_t)(j0 + u) * stride + row) : 0.f;
         }
-        const size_t o = (size_t)b * mp.T + tile;
-        p.tw_v[o] = bb.v;
-        p.tw_i[o] = bb.i;
-        p.tw_f[2 * o] = fl;
-        p.tw_f[2 * o + 1] = el;
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+          if (j0 + u < n) v[r] += t[u][r];
+    }
+    Cand best{0.f, -1};
+    int nan = 0, cnt = 0;
+    const uint64_t* wr = p.words ? p.words + (size_t)b * p.word_count : nullptr;
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int lr = c.lane + 32 * r;
+      if (lr >= rows) continue;
+      const int row = tile * kTileRows + lr;
+      if (p.out[m]) p.out[m][(size_t)b * mp.M + row] = v[r];
+      if (m == kLM && (!wr || ((wr[row >> 6] >> (row & 63)) & 1ull))) {
+        ++cnt;
+        if (v[r] != v[r]) nan = 1;
+        else if (better(Cand{v[r], row}, best)) best = Cand{v[r], row};
       }
-      cbar();
+    }
+    if (m == kLM) {
+      best = warp_best(best);
+      nan = __reduce_or_sync(0xffffffffu, nan);
+      cnt = __reduce_add_sync(0xffffffffu, cnt);
+      if (c.lane == 0) {
+        const size_t o = (size_t)b * mp.T + tile;
+        p.tw_v[o] = best.v;
+        p.tw_i[o] = best.i;
+        p.tw_f[2 * o] = nan;
+        p.tw_f[2 * o + 1] = cnt;
+      }
     }
   }
 }
 
 // This CTA's stages of matrix m from the ring: warp w takes 16 rows (w mod 8)
 // and half of each stage's eight 32-code blocks (w / 8); the partials of each
-// tile segment go to part[m][2 * segment + half][b][row], and the CTA that
-// completes a tile's K range sums its partials into the final rows.
+// tile segment go to part[m][2 * segment + half][b][row].  A warp that ends a
+// segment publishes its rows and counts itself in a per-CTA slot; the CTA's
+// last such warp counts the CTA in the tile's global counter, and the warp
+// that completes the tile's K range sums its partials (warp_fixup).  No other
+// warp waits.
 __device__ void gemv(Ctx& c, int m) {
   const PParams& p = c.p;
   const MatPlan& mp = p.mp[m];
@@ -541,19 +532,28 @@ __device__ void gemv(Ctx& c, int m) {
         if (row + 8 < mp.M) dst[row + 8] = acc1;
       }
       acc0 = acc1 = 0.f;
-      __threadfence();
-      cbar();
-      if (c.tid == 0) {
-        unsigned* cnt = p.tilecnt + p.tile_off[m] + tile;
-        const bool last = atomicAdd(cnt, 1u) == (unsigned)seg_count(mp, tile) - 1;
-        if (last) {
-          *cnt = 0;  // ready for the next layer
-          __threadfence();
+      __syncwarp();
+      int fix = 0;
+      if (c.lane == 0) {
+        __threadfence();  // this warp's partial rows, visible to every CTA
+        unsigned* sc = &c.s.segcnt[c.seg_seq & (kSegSlots - 1)];
+        if (atomicAdd(sc, 1u) == (unsigned)kCW - 1) {
+          *sc = 0;
+          const int nseg = seg_count(mp, tile);
+          if (nseg == 1) {
+            fix = 1;
+          } else {
+            unsigned* cnt = p.tilecnt + p.tile_off[m] + tile;
+            if (atomicAdd(cnt, 1u) == (unsigned)nseg - 1) {
+              *cnt = 0;  // ready for the next layer
+              __threadfence();
+              fix = 1;
+            }
+          }
         }
-        c.s.flag[2] = last ? 1 : 0;
       }
-      cbar();
-      if (c.s.flag[2]) tile_fixup(c, m, tile);
+      ++c.seg_seq;
+      if (__shfl_sync(0xffffffffu, fix, 0)) warp_fixup(c, m, tile);
     }
     if (++kst == mp.S) {
       kst = 0;
@@ -863,6 +863,7 @@ __global__ void __launch_bounds__(kThreadsP, 1) persistent_decode_kernel(const _
   s.flag = reinterpret_cast<int*>(s.red + 64);
   s.nstage = s.flag + 4;
   s.issued = reinterpret_cast<unsigned*>(s.nstage + 6);
+  s.segcnt = s.issued + 1;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nct = gridDim.x, cta = blockIdx.x;
@@ -905,6 +906,7 @@ __global__ void __launch_bounds__(kThreadsP, 1) persistent_decode_kernel(const _
     }
     s.nstage[5] = all;
     *s.issued = 0;
+    for (int i = 0; i < kSegSlots; ++i) s.segcnt[i] = 0;
   }
   __syncthreads();
   if (sh_bad) {
@@ -923,7 +925,7 @@ __global__ void __launch_bounds__(kThreadsP, 1) persistent_decode_kernel(const _
 
   // ---------------- the step ----------------
   auto run = [&]() {
-    Ctx c{p, s, cta, nct, tid, warp, lane, 0u, 0u, 0, 0u, true, 0ull};
+    Ctx c{p, s, cta, nct, tid, warp, lane, 0u, 0u, 0u, 0, 0u, true, 0ull};
     if (tid == 0 && cta == 0 && p.phase_ns) c.t_phase = globaltimer_ns();
     const int D = p.D, F = p.F;
     for (int l = 0; l < p.L; ++l) {
@@ -1117,7 +1119,7 @@ int persist_create(const PersistModel& pm, size_t max_lanes, size_t max_pages, P
   // The attention merge's weight table ([G][chunks]) also lives here.
   const size_t xs = std::max({(size_t)B * pm.D * 4, ((size_t)G * pm.hd * 9 + (size_t)8 * G * 2) * 4,
                               (size_t)G * max_pages * 4});
-  const size_t fixed = 1024 + frag + xs + 64 * 4 + 16 + 64;
+  const size_t fixed = 1024 + frag + xs + 64 * 4 + 16 + 64 + kSegSlots * 4;
   int dev_max = 0;
   GLC_CHECK_CUDA(cudaDeviceGetAttribute(&dev_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, st->device));
   const size_t avail = (size_t)dev_max - 1024;  // room for the kernel's static shared memory

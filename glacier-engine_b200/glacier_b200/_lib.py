@@ -101,6 +101,7 @@ SIGNATURES = {
     "glacier_cuda_prefill": ([vp, vp, vp, sz, i32, vp, sz, vp, sz, vp, vp, vp, vp], i32),
     "glacier_cuda_tp_unique_id": ([vp], i32),
     "glacier_cuda_model_tp_init": ([vp, C.c_int, C.c_int, vp], i32),
+    "glacier_cuda_model_tp_lanes": ([vp, C.c_int, C.c_int], i32),
     "glacier_cuda_model_profile": ([vp, C.c_int], i32),
     "glacier_cuda_model_profile_read": ([vp, vp, vp, sz], i32),
     "glacier_cuda_model_persistent": ([vp, C.c_int], i32),

@@ -144,16 +144,27 @@ class TensorParallelShard:
     slice, the matching input columns of o and down; norms, biases of its heads,
     embedding and LM head as in the full model.  Its config carries the local
     head counts and FFN width, so the device model is self-consistent; the
-    decode step all-reduces the o and down projections over the ranks."""
+    decode step all-reduces the o and down projections over the ranks.
+
+    With more ranks than kv heads (world a multiple of Hkv: 7B at 8 GPUs), each
+    kv-head group is shared by lane_groups = world / Hkv ranks: rank r holds
+    group r % Hkv's heads and attends the lanes b with b % lane_groups ==
+    r // Hkv (lane_index); the FFN is still split over all ranks."""
 
     def __init__(self, m: SyntheticModel, rank: int, world: int):
         c = dict(m.cfg)
         H, Hkv, hd, F, D, g = c["num_heads"], c["num_kv_heads"], c["head_dim"], c["hidden"], c["dim"], c["group"]
-        if H % world or Hkv % world or F % (world * g) or (H // world * hd) % g:
+        if Hkv % world == 0:
+            heads_split, self.lane_groups, self.lane_index, hr = world, 1, 0, rank
+        elif world % Hkv == 0:
+            heads_split, self.lane_groups, self.lane_index, hr = Hkv, world // Hkv, rank // Hkv, rank % Hkv
+        else:
+            heads_split = 0
+        if not heads_split or H % heads_split or F % (world * g) or (H // heads_split * hd) % g:
             raise ValueError(f"a {H}/{Hkv}-head, {F}-wide model does not split over {world} GPUs")
-        hl, kl, fl = H // world, Hkv // world, F // world
-        q0, q1 = rank * hl * hd, (rank + 1) * hl * hd
-        k0, k1 = rank * kl * hd, (rank + 1) * kl * hd
+        hl, kl, fl = H // heads_split, Hkv // heads_split, F // world
+        q0, q1 = hr * hl * hd, (hr + 1) * hl * hd
+        k0, k1 = hr * kl * hd, (hr + 1) * kl * hd
         f0, f1 = rank * fl, (rank + 1) * fl
         self.cfg = dict(c, num_heads=hl, num_kv_heads=kl, hidden=fl)
         self.config = m.config
@@ -260,10 +271,15 @@ class DeviceModel:
             raise
         return self
 
-    def enable_tensor_parallel(self, rank: int, world: int, unique_id: bytes):
-        """Joins the tensor-parallel group (blocks until every rank has joined)."""
+    def enable_tensor_parallel(self, rank: int, world: int, unique_id: bytes, lane_groups: int = 1,
+                               lane_index: int = 0):
+        """Joins the tensor-parallel group (blocks until every rank has joined); with
+        lane_groups > 1 this rank attends the lanes b with b % lane_groups == lane_index
+        (TensorParallelShard gives both)."""
         buf = (C.c_uint8 * 128).from_buffer_copy(unique_id)
         _lib.call("glacier_cuda_model_tp_init", self.h, rank, world, buf)
+        if lane_groups > 1:
+            _lib.call("glacier_cuda_model_tp_lanes", self.h, lane_groups, lane_index)
 
     def _int4(self, layer, kind, packed, scales):
         packed = np.ascontiguousarray(packed, np.uint8)

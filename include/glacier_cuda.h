@@ -301,6 +301,13 @@ int glacier_cuda_prefill(glacier_cuda_model *model, glacier_cuda_kv *kv, const i
 #define GLACIER_CUDA_TP_ID_BYTES 128
 int glacier_cuda_tp_unique_id(void *id_out);
 int glacier_cuda_model_tp_init(glacier_cuda_model *model, int rank, int world, const void *id);
+/* More ranks than kv heads (7B at 8 GPUs: 4 kv heads): the ranks of one kv-head group
+ * split the lanes.  This rank attends lanes b with b % groups == index only (it still writes
+ * the other lanes' K/V rows to its pages, which nothing reads); its attention output for the
+ * other lanes is zero, so the all-reduce of the o projection sums every lane's heads from the
+ * ranks that own it.  Call after
+ * glacier_cuda_model_tp_init; groups = 1 (the default) attends every lane. */
+int glacier_cuda_model_tp_lanes(glacier_cuda_model *model, int groups, int index);
 
 /* Diagnostics, no reference counterpart: per kernel class device time of decode steps.
  * glacier_cuda_model_profile(model, 1) makes later decode steps record CUDA events on their

@@ -104,7 +104,7 @@ def test_config2_05b_full_model_prefill_then_batch1_decode():
     """Config 2 at its full shape: 24 layers, D 896, FFN 4864, 14/2 heads of 64, vocab 151936.
     The lane's first 496 positions are random K/V rows; a 16-token prompt chunk then runs through
     glacier_cuda_prefill (positions 496..511, context 512) on a 4-lane reservation, and greedy
-    batch-1 decode follows from context 512 on a one-lane reservation (the persistent step)."""
+    batch-1 decode follows from context 512 on a one-lane reservation."""
     from glacier_b200.model import PRESETS, DecodeSession, DeviceModel, SyntheticModel
     cfg = PRESETS["qwen2.5-0.5b"]
     seed, ctx0, prompt_len, steps = 21, 496, 16, 12
@@ -122,10 +122,9 @@ def test_config2_05b_full_model_prefill_then_batch1_decode():
     tok = int(sess.prefill(prompt, start=ctx0, logits=lg).cpu()[0])
     assert int(sess.last_status.cpu()[0]) == 0
     assert max_err_vs_row_max(lg.cpu().numpy(), ol) <= DECODE_LOGIT_TOL
-    # Decode on a one-lane reservation: the persistent step (the bench's batch-1 path).
+    # Decode on a one-lane reservation (the bench's batch-1 path).
     from glacier_b200 import _lib
     _lib.call("glacier_cuda_model_reserve", dm.h, 1, max_pages)
-    assert _lib.lib().glacier_cuda_model_persistent(dm.h, 1) == 1
     compared = 0
     pos = ctx0 + prompt_len
     step_lg = torch.empty((1, cfg.vocab), dtype=torch.float32, device="cuda")

@@ -19,8 +19,11 @@ from helpers import DECODE_LOGIT_TOL, REL_TOL, max_err_vs_row_max, max_rel_err
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
-def _cfg():
+def _cfg(kind="small"):
     from glacier_b200.model import ModelConfig
+    if kind == "7b-heads":  # the 7B head layout (28 / 4 heads of 128): 8 ranks share 4 kv-head groups
+        return ModelConfig(num_layers=2, dim=512, hidden=2048, num_heads=28, num_kv_heads=4, head_dim=128,
+                           vocab=1000)
     return ModelConfig(num_layers=2, dim=256, hidden=512, num_heads=8, num_kv_heads=2, head_dim=64, vocab=1000)
 
 
@@ -60,7 +63,10 @@ def test_tp_rejects_uneven_splits():
     from glacier_b200.model import SyntheticModel, TensorParallelShard
     m = SyntheticModel(_cfg(), seed=1)
     with pytest.raises(ValueError):
-        TensorParallelShard(m, 0, 4)  # 2 kv heads do not split over 4 GPUs
+        TensorParallelShard(m, 0, 3)  # 3 GPUs neither divide 2 kv heads nor a multiple of them
+    s = TensorParallelShard(m, 3, 4)  # 4 GPUs over 2 kv heads: two ranks per kv-head group
+    assert (s.lane_groups, s.lane_index) == (2, 1)
+    assert s.cfg["num_heads"] == 4 and s.cfg["num_kv_heads"] == 1 and s.cfg["hidden"] == 128
 
 
 def _free_port() -> int:
@@ -69,7 +75,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _tp_worker(rank, world, port, lanes, prompt_len, new_tokens, out):
+def _tp_worker(rank, world, port, lanes, prompt_len, new_tokens, out, kind):
     sys.path.insert(0, ROOT)
     sys.path.insert(0, os.path.join(ROOT, "glacier-engine_b200"))
     import torch
@@ -78,13 +84,14 @@ def _tp_worker(rank, world, port, lanes, prompt_len, new_tokens, out):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     torch.cuda.set_device(rank)
     dist.init_process_group("gloo", rank=rank, world_size=world)
-    cfg = _cfg()
+    cfg = _cfg(kind)
     m = SyntheticModel(cfg, seed=5)
     max_pages = -(-(prompt_len + new_tokens) // 16)
-    dm = DeviceModel(TensorParallelShard(m, rank, world), max_positions=max_pages * 16)
+    shard = TensorParallelShard(m, rank, world)
+    dm = DeviceModel(shard, max_positions=max_pages * 16)
     uid = [tp_unique_id() if rank == 0 else None]
     dist.broadcast_object_list(uid, src=0)
-    dm.enable_tensor_parallel(rank, world, uid[0])
+    dm.enable_tensor_parallel(rank, world, uid[0], shard.lane_groups, shard.lane_index)
     sess = DecodeSession(dm, lanes, max_pages, reserve_lanes=max(lanes, 8))
     rng = np.random.default_rng(9)
     prompts = rng.integers(0, cfg.vocab, size=(lanes, prompt_len)).astype(np.int32)
@@ -102,18 +109,26 @@ def _tp_worker(rank, world, port, lanes, prompt_len, new_tokens, out):
 
 
 @pytest.mark.gpu
-def test_tp2_decode_matches_oracle():
+@pytest.mark.parametrize("world,kind", [(2, "small"), (4, "small"), (8, "7b-heads")])
+def test_tp_decode_matches_oracle(world, kind):
+    """TP decode over `world` GPUs vs the oracle: a head split at 2 GPUs; at 4 GPUs on 2 kv heads
+    and at 8 GPUs on the 7B head layout (4 kv heads), two ranks share each kv-head group and
+    split its lanes."""
     torch = pytest.importorskip("torch")
-    if torch.cuda.device_count() < 2:
-        pytest.skip("tensor parallelism needs 2 GPUs")
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"tensor parallelism over {world} GPUs needs {world} GPUs")
     import torch.multiprocessing as mp
     from glacier_b200.model import SyntheticModel
     lanes, prompt_len, new_tokens = 8, 6, 4  # 8 lanes: tensor-core projections
     out = mp.get_context("spawn").Manager().dict()
-    mp.start_processes(_tp_worker, args=(2, _free_port(), lanes, prompt_len, new_tokens, out), nprocs=2,
-                       start_method="spawn", join=True)
-    r0, r1 = out[0], out[1]
-    cfg = _cfg()
+    mp.start_processes(_tp_worker, args=(world, _free_port(), lanes, prompt_len, new_tokens, out, kind),
+                       nprocs=world, start_method="spawn", join=True)
+    r0 = out[0]
+    for r in range(1, world):
+        for (_, ta, _), (_, tb, _) in zip(r0, out[r]):
+            assert np.array_equal(ta, tb)  # every rank produces the same tokens
+    r1 = out[1]
+    cfg = _cfg(kind)
     m = SyntheticModel(cfg, seed=5)
     max_pages = -(-(prompt_len + new_tokens) // 16)
     om = oracle.OracleModel(m, rope_positions=max_pages * 16, threads=4)
