@@ -167,6 +167,21 @@ def max_over_ranks(values, world_size: int, device) -> list:
     return [float(v) for v in t.tolist()]
 
 
+def pin_cores(local: int, local_world: int) -> int:
+    """Under torchrun, gives each rank its own slice of the host cores (so the ranks' launch
+    threads do not compete); returns the cores this process may use."""
+    try:
+        cpus = sorted(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+    if local_world > 1 and len(cpus) >= local_world:
+        per = len(cpus) // local_world
+        mine = cpus[local * per:(local + 1) * per]
+        os.sched_setaffinity(0, mine)
+        return len(mine)
+    return len(cpus)
+
+
 def cpu_threads() -> int:
     try:
         return max(1, min(16, len(os.sched_getaffinity(0))))
@@ -283,6 +298,7 @@ def run_glacier(args):
 
     ws, rank, local = dist_setup()
     torch.cuda.set_device(local)
+    pinned = pin_cores(local, ws)
     if ws > 1:
         import datetime
         import torch.distributed as dist
@@ -294,7 +310,9 @@ def run_glacier(args):
     # Tensor parallel: every rank serves the same lanes; lane partition: each rank its own.
     ctxs = lane_contexts(args, lanes, 0 if tp > 1 else rank)
     total_steps = args.warmup + 2 * args.steps + args.profile_steps + 4
-    max_pages = -(-(int(ctxs.max()) + total_steps + 1) // 16)
+    # The strong-scaling pass under torchrun reuses this upload for its share of rank 0's lanes.
+    longest = max(int(ctxs.max()), int(lane_contexts(args, 64, 0).max()) if ws > 1 else 0)
+    max_pages = -(-(longest + total_steps + 1) // 16)
 
     t0 = time.time()
     cfg, model = bench_model(args)
@@ -340,8 +358,10 @@ def run_glacier(args):
     clk.start_window()
     torch.cuda.nvtx.range_push("timed_steps")  # lets a profiler select the timed launches
     e0.record(stream)
+    h0 = time.perf_counter()
     for _ in range(args.steps):
         device_step()
+    enqueue_ms = (time.perf_counter() - h0) * 1e3  # host time to launch the steps (no sync inside)
     e1.record(stream)
     torch.cuda.synchronize()
     torch.cuda.nvtx.range_pop()
@@ -398,6 +418,12 @@ def run_glacier(args):
         extras["config2"] = config2_decode(torch, args)
         extras["config3"] = config3_decode(torch, args)
 
+    per_rank = [{"rank": rank, "ms_per_step": dev_ms / args.steps,
+                 "host_enqueue_ms_per_step": enqueue_ms / args.steps, "cores": pinned}]
+    if ws > 1:
+        gathered = [None] * ws
+        torch.distributed.all_gather_object(gathered, per_rank[0])
+        per_rank = gathered
     dev_ms, e2e_ms = max_over_ranks([dev_ms, e2e_s * 1e3], ws, dev)
     tokens_total = lanes * args.steps * (1 if tp > 1 else ws)
     value = tokens_total / (dev_ms / 1e3)
@@ -436,6 +462,7 @@ def run_glacier(args):
             "gpu_launches": int(launches),
             "clocks": clk.summary(),
             "peaks_source": peaks.get("_source"),
+            "per_rank": per_rank,
         }
         print(json.dumps(line), flush=True)
     if ws > 1:

@@ -574,12 +574,13 @@ size_t attention_workspace_floats(size_t lanes, size_t num_heads, size_t head_di
 }
 
 // Segment slots per (lane, kv head): as many as the combine's weight table (one
-// float per head and segment in 48 KB of shared memory) and a 64 MiB partial
+// float per head and segment in 44 KB of shared memory) and a 64 MiB partial
 // buffer allow, and no more than a context of max_ctx can use.  Few lanes get
 // many slots (one context spread over every warp); 64 lanes get ~70, while the
 // even share of such a batch cuts a pair into about a dozen segments.
 int attention_segments(size_t lanes, size_t num_heads, size_t head_dim, size_t max_ctx) {
-  const size_t by_smem = (48 * 1024) / (sizeof(float) * num_heads);
+  // 44 KB: the combine kernels' static shared memory shares the 48 KB a launch gets by default.
+  const size_t by_smem = (44 * 1024) / (sizeof(float) * num_heads);
   const size_t by_mem = ((size_t)64 << 20) / (lanes * num_heads * (head_dim + 2) * sizeof(float));
   const size_t by_ctx = ceil_div(max_ctx, (size_t)kStagePositions) + 1;
   return (int)std::max<size_t>(2, std::min({by_smem, std::max<size_t>(16, by_mem), by_ctx}));
@@ -693,7 +694,7 @@ int paged_attention(const float* q, size_t ldq, const float* pool, size_t page_f
     GLC_REQUIRE(head_dim % 8 == 0 && ldo % 4 == 0 && (num_heads * head_dim) / 8 <= 1024,
                 "paged_attention: combine geometry %zu x %zu unsupported", num_heads, head_dim);
     const size_t csmem = num_heads * (size_t)nsplit * sizeof(float);
-    GLC_REQUIRE(csmem <= 48 * 1024, "paged_attention: %d segments per lane exceed the combine's shared memory",
+    GLC_REQUIRE(csmem <= 44 * 1024, "paged_attention: %d segments per lane exceed the combine's shared memory",
                 nsplit);
     // The split output needs the lane's row max over all heads (one block per
     // lane); fp32 output with few lanes takes a block per (lane, head).

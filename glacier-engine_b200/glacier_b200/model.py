@@ -160,12 +160,19 @@ class TensorParallelShard:
             heads_split, self.lane_groups, self.lane_index, hr = Hkv, world // Hkv, rank // Hkv, rank % Hkv
         else:
             heads_split = 0
-        if not heads_split or H % heads_split or F % (world * g) or (H // heads_split * hd) % g:
+        # FFN slices in whole blocks of 128 columns where the width gives every rank one (the
+        # tensor-core GEMM takes K in multiples of 128), else of one scale group; as even as the
+        # blocks allow.
+        unit = 128 if F % 128 == 0 and F // 128 >= world else g
+        nblk = F // unit if F % unit == 0 else 0
+        if not heads_split or H % heads_split or nblk < world or (H // heads_split * hd) % g:
             raise ValueError(f"a {H}/{Hkv}-head, {F}-wide model does not split over {world} GPUs")
-        hl, kl, fl = H // heads_split, Hkv // heads_split, F // world
+        hl, kl = H // heads_split, Hkv // heads_split
         q0, q1 = hr * hl * hd, (hr + 1) * hl * hd
         k0, k1 = hr * kl * hd, (hr + 1) * kl * hd
-        f0, f1 = rank * fl, (rank + 1) * fl
+        f0, f1 = (rank * nblk // world) * unit, ((rank + 1) * nblk // world) * unit
+        fl = f1 - f0
+        self.ffn_cols = (f0, f1)
         self.cfg = dict(c, num_heads=hl, num_kv_heads=kl, hidden=fl)
         self.config = m.config
         self.rank, self.world = rank, world

@@ -87,6 +87,9 @@ def test_qkv_rope_append_matches_oracle(heads, kv_heads, hd):
     (14, 2, 64, [512, 513]),            # 0.5B geometry
     (12, 2, 128, [2048]),
     (4, 4, 64, [33]),                   # no GQA sharing
+    # 8 lanes of the 7B geometry at long contexts: the most segment slots the combine's
+    # shared-memory weight table holds (the strong-scaling share of one GPU out of 8)
+    (28, 4, 128, [4000, 3000, 100, 4096, 2500, 17, 1200, 3999]),
 ])
 def test_paged_attention_matches_oracle(heads, kv_heads, hd, ctxs):
     from glacier_b200 import ops

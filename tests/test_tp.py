@@ -69,6 +69,20 @@ def test_tp_rejects_uneven_splits():
     assert s.cfg["num_heads"] == 4 and s.cfg["num_kv_heads"] == 1 and s.cfg["hidden"] == 128
 
 
+def test_tp_ffn_slices_are_whole_128_column_blocks():
+    """7B's FFN (18944 = 148 x 128) over 8 ranks: 18 or 19 blocks of 128 each, so every local
+    down projection keeps K a multiple of 128 (the tensor-core GEMM's chunk); the slices tile F."""
+    from glacier_b200.model import ModelConfig, SyntheticModel, TensorParallelShard
+    cfg = ModelConfig(num_layers=1, dim=64, hidden=18944, num_heads=28, num_kv_heads=4, head_dim=128, vocab=64)
+    m = SyntheticModel(cfg, seed=2)
+    for world in (2, 4, 8):
+        cols = [TensorParallelShard(m, r, world).ffn_cols for r in range(world)]
+        assert cols[0][0] == 0 and cols[-1][1] == cfg.hidden
+        assert all(a[1] == b[0] for a, b in zip(cols, cols[1:]))
+        assert all((f1 - f0) % 128 == 0 and f1 > f0 for f0, f1 in cols)
+        assert max(f1 - f0 for f0, f1 in cols) - min(f1 - f0 for f0, f1 in cols) <= 128
+
+
 def _free_port() -> int:
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
