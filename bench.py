@@ -152,8 +152,14 @@ class ClockSampler:
 
 
 def lane_contexts(args, lanes: int, rank: int) -> np.ndarray:
-    rng = np.random.default_rng(args.seed + 1000 * rank)
-    return rng.integers(args.ctx_min, args.ctx_max + 1, size=lanes).astype(np.int32)
+    """Contexts of a rank's lanes: one seeded draw from U[ctx_min, ctx_max], the same multiset on
+    every rank (in a rank-specific order), so that per-GPU KV bytes -- and with them per-GPU work
+    -- stay fixed as the lane partition grows (independent draws per rank differ by about 10% in
+    total context at 64 lanes, and the slowest rank sets the job's time)."""
+    ctx = np.random.default_rng(args.seed).integers(args.ctx_min, args.ctx_max + 1, size=lanes)
+    if rank:
+        ctx = np.random.default_rng(args.seed + 1000 * rank).permutation(ctx)
+    return ctx.astype(np.int32)
 
 
 def max_over_ranks(values, world_size: int, device) -> list:
@@ -418,7 +424,7 @@ def run_glacier(args):
         extras["config2"] = config2_decode(torch, args)
         extras["config3"] = config3_decode(torch, args)
 
-    per_rank = [{"rank": rank, "ms_per_step": dev_ms / args.steps,
+    per_rank = [{"rank": rank, "ms_per_step": dev_ms / args.steps, "mean_ctx": float(ctxs.mean()),
                  "host_enqueue_ms_per_step": enqueue_ms / args.steps, "cores": pinned}]
     if ws > 1:
         gathered = [None] * ws

@@ -134,6 +134,7 @@ struct Int4Weight {
   size_t M = 0, K = 0, group = 0;
   bool tc = false;                  // tensor-core GEMV eligible (group 32, maps valid)
   bool tcg = false;                 // tensor-core GEMM maps valid (group 8, 16 or 32)
+  bool nonfinite = false;           // fp16 scales hold an infinity or NaN: exact-conversion kernels
   CUtensorMap tmap_w, tmap_s;
 };
 
@@ -154,6 +155,26 @@ int int4_linear_q8(const Int4Weight& w, const float* x, size_t ldx, size_t batch
 // row stride ld); GLACIER_CUDA_EUNSUPPORTED when that kernel does not apply.
 int int4_linear_swiglu(const Int4Weight& w, const float* gate, const float* up, size_t ld, size_t batch,
                        const float* bias, float* y, size_t ldy, cudaStream_t stream);
+
+// Epilogue of the LM head's GEMV: the eligible argmax of each row (the semantics
+// of argmax_rows) from per-tile winners, which a second kernel reduces.
+// `partials` holds gemv_argmax_partials_bytes(M) bytes.
+struct ArgmaxEpi {
+  const uint64_t* words = nullptr;  // eligibility bitset rows of word_count words, or null
+  int word_count = 0;
+  int32_t* tokens = nullptr;
+  int32_t* status = nullptr;
+  glacier_argmax_result* results = nullptr;  // optional per-row records
+  int4* partials = nullptr;
+};
+
+// y = x W^T on the tensor-core GEMV (up to 4 rows, no bias; y may be null: no
+// logits), then the eligible argmax of each row into a.tokens / a.status.
+// GLACIER_CUDA_EUNSUPPORTED when the tensor-core GEMV does not apply.
+int int4_linear_argmax(const Int4Weight& w, const float* x, size_t ldx, size_t batch, float* y, size_t ldy,
+                       const ArgmaxEpi& a, cudaStream_t stream);
+size_t gemv_argmax_partials_bytes(size_t M);
+int* ops_error_word();
 
 // Destination of an activation block that feeds the tensor-core GEMM: rows of
 // fp16 hi / lo parts ([2*np, K]: hi rows 0..np-1, lo rows np..2np-1) in the
@@ -400,12 +421,17 @@ __device__ __forceinline__ void store_split8(const SplitOut& so, int r, size_t K
 // unit: the magnitude bits shifted into an fp32 field give the value times
 // 2^-112 for normal and subnormal inputs alike (the fp32 result of a subnormal
 // input is itself subnormal), and the power-of-two product is exact.  Finite
-// inputs only (scales are).  In hot loops this keeps the fp16 -> fp32 scale
-// conversions off the narrow special-function pipe.
+// inputs only: weights whose fp16 scales hold an infinity or NaN are flagged at
+// load (Int4Weight::nonfinite) and read through the conversion instruction.  In
+// hot loops this keeps the fp16 -> fp32 scale conversions off the narrow
+// special-function pipe.
 __device__ __forceinline__ float half_to_float_bits(uint32_t h) {
   const uint32_t b = ((h & 0x8000u) << 16) | ((h & 0x7FFFu) << 13);
   return __uint_as_float(b) * 0x1p112f;
 }
+
+// fp16 scale bits with exponent 31 (infinity or NaN).
+__host__ __device__ inline bool half_bits_nonfinite(uint16_t h) { return (h & 0x7C00u) == 0x7C00u; }
 
 // Scale loads: the library keeps fp16 scale mirrors (as the reference's
 // int4_weights.withF16Scales does) but also accepts fp32 scales.

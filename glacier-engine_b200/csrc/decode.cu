@@ -130,12 +130,24 @@ __global__ void prefill_rows_kernel(const int32_t* __restrict__ table, int max_p
 // parallelism with more ranks than kv heads) a rank attends only the lanes
 // b with b % groups == index; the others get context 0, so their attention
 // output is zero and the all-reduce of o sums each lane's heads from its owners.
+// Context length of each lane (position + 1; 0 for lanes another tensor-parallel
+// rank attends).  A position outside [0, limit) -- past the RoPE table or the
+// lane's block table -- gives context 0, so attention never reads past the
+// block table, and raises the bad-input word (the RoPE / append kernel also
+// skips that lane).
 __global__ void ctx_from_pos_kernel(const int32_t* __restrict__ pos, int32_t* __restrict__ ctx, int n, int groups,
-                                    int index) {
+                                    int index, int limit, int* __restrict__ bad) {
   griddep_launch();
   griddep_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < n) ctx[i] = (i % groups == index) ? pos[i] + 1 : 0;
+  if (i >= n) return;
+  const int p = pos[i];
+  if (p < 0 || p >= limit) {
+    ctx[i] = 0;
+    atomicExch(bad, 1);
+    return;
+  }
+  ctx[i] = (i % groups == index) ? p + 1 : 0;
 }
 
 struct DevBuf {
@@ -217,6 +229,7 @@ struct FusedWeight {
           // Round-to-nearest-even fp16 mirror (int4_weights.zig:348-358 withF16Scales).
           const __half h = __float2half_rn(s);
           memcpy(&host[(r * scale_stride + g) * 2], &h, 2);
+          if (half_bits_nonfinite(__half_as_ushort(h))) w.nonfinite = true;
         } else {
           memcpy(&host[(r * scale_stride + g) * 4], &s, 4);
         }
@@ -258,6 +271,8 @@ struct glacier_cuda_model {
   // Reserved step workspace.
   size_t max_lanes = 0, max_pages = 0;
   DevBuf x, hn, qkv, q, attn, proj, gu, act, down, logits, ctx, att_ws, arg_ws, status;
+  // GEMV-mode LM head with the eligible argmax in its epilogue: per-tile winners.
+  DevBuf lm_arg;
   size_t att_floats = 0, arg_bytes = 0;
   int att_segs = 0;
   // Tensor-core GEMM mode (more than 4 lanes): activations in split fp16 form.
@@ -549,7 +564,7 @@ int glacier_cuda_model_reserve(glacier_cuda_model* m, size_t max_lanes, size_t m
       (rc = m->down.alloc(L * c.dim * 4)) || (rc = m->logits.alloc(L * (size_t)c.vocab * 4)) ||
       (rc = m->ctx.alloc(L * 4)) || (rc = m->att_ws.alloc(m->att_floats * 4)) ||
       (rc = m->arg_ws.alloc(m->arg_bytes)) || (rc = m->status.alloc(L * 4)) || (rc = m->pf_pos.alloc(L * 4)) ||
-      (rc = m->pf_bt.alloc(L * max_pages * 4)))
+      (rc = m->pf_bt.alloc(L * max_pages * 4)) || (rc = m->lm_arg.alloc(gemv_argmax_partials_bytes(c.vocab))))
     return rc;
   m->max_lanes = max_lanes;
   m->max_pages = max_pages;
@@ -658,9 +673,23 @@ static int step_impl(glacier_cuda_model* m, glacier_cuda_kv* kv, size_t lanes, c
     if (prof) prof->mark(kind, st);
   };
   mark(GLACIER_CUDA_STEP_EMBED);
+  const int pos_limit = (int)std::min<size_t>(max_ctx, c.max_positions);
   if ((rc = launch_pdl(ctx_from_pos_kernel, dim3((unsigned)ceil_div(B, 128)), dim3(128), 0, st, 1, positions,
-                       m->ctx.as<int32_t>(), (int)B, m->tp_lane_groups, m->tp_lane_index)))
+                       m->ctx.as<int32_t>(), (int)B, m->tp_lane_groups, m->tp_lane_index, pos_limit,
+                       ops_error_word())))
     return rc;
+  int32_t* st_out = status_out ? status_out : m->status.as<int32_t>();
+  // GEMV mode: the LM head's epilogue picks the tokens (no argmax pass, and the
+  // logits are written only when the caller asks for them).
+  auto lm_head_argmax = [&](const float* xin, size_t rows) -> int {
+    ArgmaxEpi ae;
+    ae.words = eligible;
+    ae.word_count = (int)eligible_words;
+    ae.tokens = tokens_out;
+    ae.status = st_out;
+    ae.partials = m->lm_arg.as<int4>();
+    return int4_linear_argmax(m->lm.w, xin, D, rows, logits_out, c.vocab, ae, st);
+  };
   if ((rc = m->emb_f32 ? embed_gather(m->embedding.as<float>(), c.vocab, D, tokens, B, x, D, st)
                        : embed_gather(m->embedding.as<__half>(), c.vocab, D, tokens, B, x, D, st)))
     return rc;
@@ -756,12 +785,17 @@ static int step_impl(glacier_cuda_model* m, glacier_cuda_kv* kv, size_t lanes, c
     if ((rc = add_rmsnorm(x + r * D, D, m->down.as<float>() + r * D, D, B * D, sd, x + r * D, D,
                           m->final_norm.as<float>(), c.rms_eps, hn, D, 1, D, st)))
       return rc;
-    float* logits = logits_out ? logits_out : m->logits.as<float>();
     mark(GLACIER_CUDA_STEP_LM_HEAD);
+    rc = lm_head_argmax(hn, 1);
+    if (rc != GLACIER_CUDA_EUNSUPPORTED) {
+      mark(-1);
+      return rc;
+    }
+    float* logits = logits_out ? logits_out : m->logits.as<float>();
     if ((rc = int4_linear(m->lm.w, hn, D, 1, nullptr, logits, c.vocab, st))) return rc;
     mark(GLACIER_CUDA_STEP_ARGMAX);
-    rc = argmax_rows(logits, c.vocab, 1, c.vocab, eligible, eligible_words, nullptr, tokens_out,
-                     status_out ? status_out : m->status.as<int32_t>(), m->arg_ws.p, m->arg_bytes, st);
+    rc = argmax_rows(logits, c.vocab, 1, c.vocab, eligible, eligible_words, nullptr, tokens_out, st_out,
+                     m->arg_ws.p, m->arg_bytes, st);
     mark(-1);
     return rc;
   }
@@ -769,12 +803,19 @@ static int step_impl(glacier_cuda_model* m, glacier_cuda_kv* kv, size_t lanes, c
   if ((rc = add_rmsnorm(x, D, m->down.as<float>(), D, B * D, sd, x, D, m->final_norm.as<float>(), c.rms_eps,
                         m->gemm ? nullptr : hn, D, B, D, st, so_d)))
     return rc;
-  float* logits = logits_out ? logits_out : m->logits.as<float>();
   mark(GLACIER_CUDA_STEP_LM_HEAD);
+  if (!m->gemm) {
+    rc = lm_head_argmax(hn, B);
+    if (rc != GLACIER_CUDA_EUNSUPPORTED) {
+      mark(-1);
+      return rc;
+    }
+  }
+  float* logits = logits_out ? logits_out : m->logits.as<float>();
   if ((rc = project(m->lm.w, hn, D, so_d, m->map_d, logits, c.vocab, 1))) return rc;
   mark(GLACIER_CUDA_STEP_ARGMAX);
-  rc = argmax_rows(logits, c.vocab, B, c.vocab, eligible, eligible_words, nullptr, tokens_out,
-                   status_out ? status_out : m->status.as<int32_t>(), m->arg_ws.p, m->arg_bytes, st);
+  rc = argmax_rows(logits, c.vocab, B, c.vocab, eligible, eligible_words, nullptr, tokens_out, st_out,
+                   m->arg_ws.p, m->arg_bytes, st);
   mark(-1);
   return rc;
 }

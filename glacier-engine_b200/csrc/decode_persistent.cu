@@ -1074,7 +1074,7 @@ int persist_create(const PersistModel& pm, size_t max_lanes, size_t max_pages, P
   if (pm.hd != 64 && pm.hd != 128) return GLACIER_CUDA_EUNSUPPORTED;
   if (pm.H % pm.Hkv != 0 || pm.H / pm.Hkv > kMaxG || pm.D % 4 != 0) return GLACIER_CUDA_EUNSUPPORTED;
   for (const Int4Weight* w : pm.w)
-    if (!w || !w->tc || !w->f16 || w->group != 32) return GLACIER_CUDA_EUNSUPPORTED;
+    if (!w || !w->tc || !w->f16 || w->nonfinite || w->group != 32) return GLACIER_CUDA_EUNSUPPORTED;
   auto st = std::make_unique<PersistState>();
   GLC_CHECK_CUDA(cudaGetDevice(&st->device));
   const int nct = sm_count();

@@ -493,6 +493,7 @@ int ops_device_error(int clear) {
 }
 
 static int* ops_err_ptr() { return device_symbol_address(g_ops_error); }
+int* ops_error_word() { return ops_err_ptr(); }
 
 // Cluster size for a row of `dim` values: about 1024 values per CTA, at most 8.
 static int row_cluster(size_t dim) {

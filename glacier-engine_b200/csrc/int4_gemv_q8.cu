@@ -363,8 +363,10 @@ int int4_linear_q8(const Int4Weight& w, const float* x, size_t ldx, size_t batch
   const size_t M = w.M, K = w.K, ag = w.group == 8 ? 32 : w.group;
   if (M > 65536 || K > (size_t)kQ8MaxK || ceil_div(K, ag) > 2048) return int4_linear(w, x, ldx, batch, bias, y, ldy, stream);
   const size_t stride = w.scale_stride ? w.scale_stride : K / w.group;
-  const bool tc = w.group == 32 && K % 256 == 0 && stride == K / 32 && (uintptr_t)w.packed % 16 == 0 &&
-                  (uintptr_t)w.scales % 16 == 0 && (uintptr_t)x % 16 == 0 && ldx % 4 == 0;
+  // (Weights with a non-finite fp16 scale take the generic kernel, which converts scales exactly.)
+  const bool tc = !w.nonfinite && w.group == 32 && K % 256 == 0 && stride == K / 32 &&
+                  (uintptr_t)w.packed % 16 == 0 && (uintptr_t)w.scales % 16 == 0 && (uintptr_t)x % 16 == 0 &&
+                  ldx % 4 == 0;
   if (tc) {
     for (size_t b = 0; b < batch; b += 4) {
       const size_t nb = batch - b < 4 ? batch - b : 4;

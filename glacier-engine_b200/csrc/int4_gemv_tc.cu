@@ -20,10 +20,14 @@
 //    fp32 group scale once per group (one FFMA per row per group).
 //  * A K-split across the CTAs of a thread-block cluster is reduced through
 //    distributed shared memory in rank order (deterministic, no workspace).
+//  * The LM head's instantiation ends with the eligible argmax of each row:
+//    each warp reduces the 32 results it writes to one winner record, which a
+//    one-CTA-per-row kernel reduces (logits are written only on request).
 //  * Every mbarrier wait is bounded; on timeout the kernel raises a device
 //    error word, drains its own TMA copies and leaves through the cluster
 //    barriers so no CTA is left waiting.
 #include <algorithm>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -54,6 +58,30 @@ struct GemvParams {
   int* err;
   const float* xu;     // SwiGLU input: x = silu(x) * xu elementwise (same leading dimension), or null
 };
+
+struct NoEpi {};  // the plain instantiation's (empty) epilogue argument
+
+// Argmax candidate order of argmaxEligible (sampling.zig:55-107): larger value,
+// equal values to the lower index; i < 0 is "none".
+__device__ __forceinline__ bool arg_better(float av, int ai, float bv, int bi) {
+  if (ai < 0) return false;
+  if (bi < 0) return true;
+  return av > bv || (av == bv && ai < bi);
+}
+
+__device__ __forceinline__ void arg_warp_reduce(float& v, int& i, int& nan, int& elig) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float tv = __shfl_xor_sync(0xffffffffu, v, o);
+    const int ti = __shfl_xor_sync(0xffffffffu, i, o);
+    if (arg_better(tv, ti, v, i)) {
+      v = tv;
+      i = ti;
+    }
+    nan |= __shfl_xor_sync(0xffffffffu, nan, o);
+    elig += __shfl_xor_sync(0xffffffffu, elig, o);
+  }
+}
 
 __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                           uint32_t b0, uint32_t b1) {
@@ -115,6 +143,20 @@ struct RowScales<__half> {
     return half_to_float_bits((g & 1) ? (w >> 16) : (w & 0xFFFFu));
   }
 };
+// fp16 scales of a weight that holds a non-finite one: the conversion
+// instruction keeps infinities and NaNs (rare; the fast form assumes finite).
+struct HalfExact {
+  uint16_t bits;
+};
+template <>
+struct RowScales<HalfExact> {
+  uint4 v;
+  __device__ void load(const uint8_t* p) { v = *reinterpret_cast<const uint4*>(p); }
+  __device__ float get(int g) const {
+    const uint32_t w = g < 2 ? v.x : g < 4 ? v.y : g < 6 ? v.z : v.w;
+    return __half2float(__ushort_as_half((unsigned short)((g & 1) ? (w >> 16) : (w & 0xFFFFu))));
+  }
+};
 template <>
 struct RowScales<float> {
   float4 a, b;
@@ -129,10 +171,13 @@ struct RowScales<float> {
   }
 };
 
-template <typename ScaleT>
+// Epi: NoEpi (y = W x + bias) or ArgmaxEpi (the LM head: y optional, then the
+// eligible argmax of each row).
+template <typename ScaleT, typename Epi>
 __global__ void __launch_bounds__(kThreads, 2) gemv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w,
                                                               const __grid_constant__ CUtensorMap tmap_s,
-                                                              const GemvParams p) {
+                                                              const GemvParams p, const Epi epi) {
+  constexpr bool kArgmax = std::is_same<Epi, ArgmaxEpi>::value;
   // Weights do not depend on the previous kernel: the producer streams them at
   // once; the consumers wait for its writes (griddep_wait) before reading x, and
   // every thread waits before the stores of y.
@@ -283,20 +328,102 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_tc_kernel(const __grid_const
     for (int idx = threadIdx.x; idx < p.batch * kRows; idx += kThreads) {
       const int b = idx / kRows, rr = idx % kRows;
       const int row = row0 + rr;
+      float v = 0.f;
       if (row < p.M) {
         const uint32_t local = smem_u32(&red[b * kRows + rr]);
-        float v = 0.f;
         for (uint32_t q = 0; q < nrank; ++q) v += ld_dsmem_f32(mapa_shared(local, q));
-        p.y[b * p.ldy + row] = v + (p.bias ? p.bias[row] : 0.f);
+        v += p.bias ? p.bias[row] : 0.f;
+        if (!kArgmax || p.y) p.y[b * p.ldy + row] = v;
+      }
+      if constexpr (kArgmax) {
+        // The warp's 32 consecutive rows (one batch row b: kRows is a multiple of
+        // 32) reduce to one winner record; argmax_tiles_kernel reduces the records.
+        bool ok = row < p.M;
+        if (ok && epi.words) ok = (epi.words[(size_t)b * epi.word_count + (row >> 6)] >> (row & 63)) & 1ull;
+        int nan = ok && v != v, elig = ok;
+        float bv = v;
+        int bi = ok && !nan ? row : -1;
+        arg_warp_reduce(bv, bi, nan, elig);
+        if (lane == 0)
+          epi.partials[(size_t)b * (gridDim.x / nrank) * (kRows / 32) + (size_t)tile * (kRows / 32) + rr / 32] =
+              make_int4(__float_as_int(bv), bi, nan, elig);
       }
     }
   }
   cluster_sync_all();
 }
 
-template <typename ScaleT>
+// The LM head's argmax, second part: row b's winner records (one per 32 rows)
+// reduced by one CTA.
+// The order (value, then lowest index) is total, so this gives the result of
+// argmax_rows whatever the tiling; the statuses follow argmax_final_kernel.
+__global__ void __launch_bounds__(1024) argmax_tiles_kernel(const ArgmaxEpi a, int tiles, int n) {
+  griddep_launch();
+  griddep_wait();
+  __shared__ float sv[32];
+  __shared__ int si[32], sn[32], se[32];
+  const int b = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float bv = 0.f;
+  int bi = -1, nan = 0, elig = 0;
+  const int4* rec = a.partials + (size_t)b * tiles;
+  // Four independent loads in flight per thread before any is compared.
+  for (int t0 = threadIdx.x; t0 < tiles; t0 += 4 * blockDim.x) {
+    int4 r[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int t = t0 + u * blockDim.x;
+      r[u] = t < tiles ? rec[t] : make_int4(0, -1, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (arg_better(__int_as_float(r[u].x), r[u].y, bv, bi)) {
+        bv = __int_as_float(r[u].x);
+        bi = r[u].y;
+      }
+      nan |= r[u].z;
+      elig += r[u].w;
+    }
+  }
+  arg_warp_reduce(bv, bi, nan, elig);
+  if (lane == 0) {
+    sv[warp] = bv;
+    si[warp] = bi;
+    sn[warp] = nan;
+    se[warp] = elig;
+  }
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  for (int w = 1; w < (int)(blockDim.x >> 5); ++w) {
+    if (arg_better(sv[w], si[w], bv, bi)) {
+      bv = sv[w];
+      bi = si[w];
+    }
+    nan |= sn[w];
+    elig += se[w];
+  }
+  int tail = 0;
+  if (a.words && (n & 63)) {
+    const uint64_t valid = (1ull << (n & 63)) - 1;
+    tail = (a.words[(size_t)b * a.word_count + a.word_count - 1] & ~valid) != 0;
+  }
+  int st = GLACIER_CUDA_OK;
+  if (a.words && (tail || elig == 0)) st = GLACIER_CUDA_EMASK;
+  else if (nan) st = GLACIER_CUDA_ENAN;
+  else if (bi < 0) st = GLACIER_CUDA_EMASK;
+  if (a.tokens) a.tokens[b] = st == GLACIER_CUDA_OK ? bi : -1;
+  if (a.status) a.status[b] = st;
+  if (a.results) {
+    glacier_argmax_result& r = a.results[b];
+    r.value = bi >= 0 ? bv : -INFINITY;
+    r.index = bi >= 0 ? (size_t)bi : 0;
+    r.valid = st == GLACIER_CUDA_OK;
+    r.saw_nan = nan;
+  }
+}
+
+template <typename ScaleT, typename Epi>
 int launch_gemv_tc(const Int4Weight& w, const float* x, const float* xu, size_t ldx, size_t batch, const float* bias,
-                   float* y, size_t ldy, cudaStream_t stream) {
+                   float* y, size_t ldy, cudaStream_t stream, const Epi& epi) {
   const size_t M = w.M, K = w.K;
   int rc = 0;
   const int tiles = (int)ceil_div(M, kRows);
@@ -317,11 +444,11 @@ int launch_gemv_tc(const Int4Weight& w, const float* x, const float* xu, size_t 
   const size_t smem = 1024 + (size_t)kStages * stage_bytes + (size_t)spc * kBlocksPerStage * 8 * batch * 16 +
                       4 * kRows * sizeof(float) + 2 * kStages * sizeof(uint64_t);
   GLC_REQUIRE(smem <= 200 * 1024, "int4 gemv: K slice too long for shared memory (K=%zu)", K);
-  auto kern = gemv_tc_kernel<ScaleT>;
+  auto kern = gemv_tc_kernel<ScaleT, Epi>;
   rc = allow_dynamic_smem((const void*)kern, (int)smem);
   if (rc) return rc;
-  int* err = nullptr;
-  GLC_CHECK_CUDA(cudaGetSymbolAddress((void**)&err, g_gemv_error));
+  int* err = device_symbol_address(g_gemv_error);
+  GLC_REQUIRE(err != nullptr, "int4 gemv: device status word unavailable");
   GemvParams prm{x, ldx, bias, y, ldy, (int)M, (int)K, (int)batch, stages, spc, err, xu};
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(tiles * cs);
@@ -337,7 +464,7 @@ int launch_gemv_tc(const Int4Weight& w, const float* x, const float* xu, size_t 
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  GLC_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, w.tmap_w, w.tmap_s, prm));
+  GLC_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, w.tmap_w, w.tmap_s, prm, epi));
   note_launch();
   return GLACIER_CUDA_OK;
 }
@@ -370,8 +497,26 @@ int int4_weight_prepare(Int4Weight& w) {
 
 int gemv_int4_tc(const Int4Weight& w, const float* x, size_t ldx, size_t batch, const float* bias, float* y,
                  size_t ldy, cudaStream_t stream, const float* xu) {
-  return w.f16 ? launch_gemv_tc<__half>(w, x, xu, ldx, batch, bias, y, ldy, stream)
-               : launch_gemv_tc<float>(w, x, xu, ldx, batch, bias, y, ldy, stream);
+  if (!w.f16) return launch_gemv_tc<float>(w, x, xu, ldx, batch, bias, y, ldy, stream, NoEpi());
+  return w.nonfinite ? launch_gemv_tc<HalfExact>(w, x, xu, ldx, batch, bias, y, ldy, stream, NoEpi())
+                     : launch_gemv_tc<__half>(w, x, xu, ldx, batch, bias, y, ldy, stream, NoEpi());
+}
+
+size_t gemv_argmax_partials_bytes(size_t M) { return 4 * ceil_div(M, (size_t)kRows) * (kRows / 32) * sizeof(int4); }
+
+int int4_linear_argmax(const Int4Weight& w, const float* x, size_t ldx, size_t batch, float* y, size_t ldy,
+                       const ArgmaxEpi& a, cudaStream_t stream) {
+  GLC_REQUIRE(x && batch > 0 && a.partials, "int4 linear argmax: null argument");
+  const bool aligned = (uintptr_t)x % 16 == 0 && ldx % 4 == 0;
+  if (!w.tc || !aligned || batch > 4) return GLACIER_CUDA_EUNSUPPORTED;
+  GLC_REQUIRE(!a.words || (size_t)a.word_count == ceil_div(w.M, (size_t)64),
+              "int4 linear argmax: eligible mask needs %zu words per row", ceil_div(w.M, (size_t)64));
+  const int rc = !w.f16 ? launch_gemv_tc<float>(w, x, nullptr, ldx, batch, nullptr, y, ldy, stream, a)
+                 : w.nonfinite ? launch_gemv_tc<HalfExact>(w, x, nullptr, ldx, batch, nullptr, y, ldy, stream, a)
+                               : launch_gemv_tc<__half>(w, x, nullptr, ldx, batch, nullptr, y, ldy, stream, a);
+  if (rc) return rc;
+  return launch_pdl(argmax_tiles_kernel, dim3((unsigned)batch), dim3(1024), 0, stream, 1, a,
+                    (int)(ceil_div(w.M, (size_t)kRows) * (kRows / 32)), (int)w.M);
 }
 
 int gemv_device_error(int clear) {

@@ -44,6 +44,12 @@ struct AttnParams {
 };
 
 constexpr int kStagePositions = 8;  // positions per pipeline stage
+
+// A lane's context as the kernels use it: clamped to [0, cap] (cap = the block
+// table's positions), so a context past the table never reads past it.
+__device__ __forceinline__ int lane_ctx(const int32_t* __restrict__ ctx_lens, int l, int cap) {
+  return min(max(ctx_lens[l], 0), cap);
+}
 constexpr int kMaxPlanLanes = 128;  // lanes one stage plan covers (4 per thread of a warp)
 
 // Static work split shared by the attention and combine kernels (stream-K):
@@ -54,13 +60,13 @@ constexpr int kMaxPlanLanes = 128;  // lanes one stage plan covers (4 per thread
 // raised when needed so no pair has more than seg_cap segments.  Run by one
 // warp; C[l] = first stage of lane l (C[lanes] = total); plan = {total, Q}.
 __device__ __forceinline__ void attn_stage_plan(const int32_t* __restrict__ ctx_lens, int lanes, int hkv, int warps,
-                                                int seg_cap, int* C, int* plan) {
+                                                int seg_cap, int* C, int* plan, int ctx_cap) {
   const int lane = threadIdx.x & 31;
   int v[4], sum = 0, mx = 0;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int idx = 4 * lane + i;
-    const int ns = idx < lanes ? (max(ctx_lens[idx], 0) + kStagePositions - 1) / kStagePositions : 0;
+    const int ns = idx < lanes ? (lane_ctx(ctx_lens, idx, ctx_cap) + kStagePositions - 1) / kStagePositions : 0;
     v[i] = hkv * ns;
     sum += v[i];
     mx = max(mx, ns);
@@ -89,8 +95,9 @@ __device__ __forceinline__ void attn_stage_plan(const int32_t* __restrict__ ctx_
 }
 
 // Segments of pair (lane l, kv head h): its stages [P, P + ns) over warps of Q stages.
-__device__ __forceinline__ int attn_pair_segments(const int* C, const int32_t* ctx_lens, int l, int h, int q) {
-  const int ns = (max(ctx_lens[l], 0) + kStagePositions - 1) / kStagePositions;
+__device__ __forceinline__ int attn_pair_segments(const int* C, const int32_t* ctx_lens, int l, int h, int q,
+                                                  int ctx_cap) {
+  const int ns = (lane_ctx(ctx_lens, l, ctx_cap) + kStagePositions - 1) / kStagePositions;
   if (ns == 0) return 0;
   const int P = C[l] + h * ns;
   return (P + ns - 1) / q - P / q + 1;
@@ -153,7 +160,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
   float2* prb = prb_all[warp];
   constexpr int G = NG;
   const int Hkv = p.num_kv_heads;
-  if (warp == 0) attn_stage_plan(p.ctx_lens, lanes, Hkv, p.warps, p.nsplit, Cs, plan);
+  const int ctx_cap = p.max_pages * 16;
+  if (warp == 0) attn_stage_plan(p.ctx_lens, lanes, Hkv, p.warps, p.nsplit, Cs, plan, ctx_cap);
   if (lane == 0) {
     for (int i = 0; i < kAttnStages; ++i) mbar_init(&bars[warp][i], 1);
     fence_mbar_init();
@@ -166,7 +174,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
   auto pair_span = [&](int pair, int& lid, int& kvh, int& P, int& sb, int& se) {
     lid = pair / Hkv;
     kvh = pair - lid * Hkv;
-    const int ns = (max(p.ctx_lens[lid], 0) + kStageRows - 1) / kStageRows;
+    const int ns = (lane_ctx(p.ctx_lens, lid, ctx_cap) + kStageRows - 1) / kStageRows;
     P = Cs[lid] + kvh * ns;
     sb = max(0, g0 - P);
     se = min(ns, g1 - P);
@@ -179,7 +187,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
       const int mid = (lo + hi + 1) >> 1;
       if (Cs[mid] <= g0) lo = mid; else hi = mid - 1;
     }
-    const int ns = (max(p.ctx_lens[lo], 0) + kStageRows - 1) / kStageRows;
+    const int ns = (lane_ctx(p.ctx_lens, lo, ctx_cap) + kStageRows - 1) / kStageRows;
     first_pair = lo * Hkv + min(Hkv - 1, (g0 - Cs[lo]) / max(ns, 1));
   }
 
@@ -240,7 +248,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
     if (item < 0) break;
     int lid, kvh, P, sb, se;
     pair_span(item, lid, kvh, P, sb, se);
-    const int nst = se - sb, ctx = p.ctx_lens[lid];
+    const int nst = se - sb, ctx = lane_ctx(p.ctx_lens, lid, ctx_cap);
     const size_t part_base = ((size_t)lid * p.num_heads + (size_t)kvh * G) * p.nsplit + (gw - P / Q);
     // q of the G heads, scaled by 1/sqrt(hd) * log2(e) (softmax in base 2), this
     // lane's dims 4*l16 + 64*i + c.
@@ -421,7 +429,8 @@ __global__ void __launch_bounds__(1024) attn_combine_kernel(const float* __restr
                                                             int head_dim, int num_heads, float* __restrict__ out,
                                                             size_t ldo, SplitOut so,
                                                             const int32_t* __restrict__ ctx_lens, int lanes,
-                                                            int num_kv_heads, int warps_total, int heads_per_block) {
+                                                            int num_kv_heads, int warps_total, int heads_per_block,
+                                                            int ctx_cap) {
   griddep_launch();
   griddep_wait();
   extern __shared__ float wts[];  // [num_heads][nsplit] segment weights
@@ -433,11 +442,11 @@ __global__ void __launch_bounds__(1024) attn_combine_kernel(const float* __restr
   const int nh = min(heads_per_block, num_heads - head0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
   // The segments each head of this lane was cut into (the attention kernel's plan).
-  if (warp == 0) attn_stage_plan(ctx_lens, lanes, num_kv_heads, warps_total, nsplit, Cs, plan);
+  if (warp == 0) attn_stage_plan(ctx_lens, lanes, num_kv_heads, warps_total, nsplit, Cs, plan, ctx_cap);
   __syncthreads();
   const int group = num_heads / num_kv_heads;
   for (int t = threadIdx.x; t < nh; t += blockDim.x)
-    segs[t] = attn_pair_segments(Cs, ctx_lens, lane_id, (head0 + t) / group, plan[1]);
+    segs[t] = attn_pair_segments(Cs, ctx_lens, lane_id, (head0 + t) / group, plan[1], ctx_cap);
   __syncthreads();
   for (int t = warp; t < nh; t += nwarps) {
     const int nsplit_lane = segs[t];
@@ -509,7 +518,7 @@ __global__ void __launch_bounds__(W * 32) attn_combine_head_kernel(const float* 
                                                                    int head_dim, int num_heads,
                                                                    float* __restrict__ out, size_t ldo,
                                                                    const int32_t* __restrict__ ctx_lens, int lanes,
-                                                                   int num_kv_heads, int warps_total) {
+                                                                   int num_kv_heads, int warps_total, int ctx_cap) {
   griddep_launch();
   griddep_wait();
   extern __shared__ float wts[];  // [nsplit]
@@ -517,9 +526,10 @@ __global__ void __launch_bounds__(W * 32) attn_combine_head_kernel(const float* 
   __shared__ int Cs[kMaxPlanLanes + 1], plan[2];
   const int lane_id = blockIdx.x, head = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (warp == 0) attn_stage_plan(ctx_lens, lanes, num_kv_heads, warps_total, nsplit, Cs, plan);
+  if (warp == 0) attn_stage_plan(ctx_lens, lanes, num_kv_heads, warps_total, nsplit, Cs, plan, ctx_cap);
   __syncthreads();
-  const int nsplit_lane = attn_pair_segments(Cs, ctx_lens, lane_id, head / (num_heads / num_kv_heads), plan[1]);
+  const int nsplit_lane =
+      attn_pair_segments(Cs, ctx_lens, lane_id, head / (num_heads / num_kv_heads), plan[1], ctx_cap);
   const size_t base = ((size_t)lane_id * num_heads + head) * nsplit;
   if (warp == 0) {
     float M = -INFINITY;
@@ -704,10 +714,11 @@ int paged_attention(const float* q, size_t ldq, const float* pool, size_t page_f
       if (nsplit > 64)
         return launch_pdl(attn_combine_head_kernel<32>, hgrid, dim3(1024), (size_t)nsplit * sizeof(float), stream, 1,
                           (const float*)prm.part_o, (const float*)prm.part_ml, nsplit, (int)head_dim,
-                          (int)num_heads, out, ldo, ctx_lens, (int)lanes, (int)num_kv_heads, prm.warps);
+                          (int)num_heads, out, ldo, ctx_lens, (int)lanes, (int)num_kv_heads, prm.warps,
+                          (int)max_pages * 16);
       return launch_pdl(attn_combine_head_kernel<8>, hgrid, dim3(256), (size_t)nsplit * sizeof(float), stream, 1,
                         (const float*)prm.part_o, (const float*)prm.part_ml, nsplit, (int)head_dim, (int)num_heads,
-                        out, ldo, ctx_lens, (int)lanes, (int)num_kv_heads, prm.warps);
+                        out, ldo, ctx_lens, (int)lanes, (int)num_kv_heads, prm.warps, (int)max_pages * 16);
     }
     const size_t hpb = num_heads;
     // One warp per head for the weights (up to 32 warps), enough threads for 8 values each.
@@ -716,7 +727,8 @@ int paged_attention(const float* q, size_t ldq, const float* pool, size_t page_f
     const dim3 cgrid((unsigned)lanes, (unsigned)ceil_div(num_heads, hpb));
     if ((rc = launch_pdl(attn_combine_kernel, cgrid, dim3(threads), hpb * (size_t)nsplit * sizeof(float), stream, 1,
                          (const float*)prm.part_o, (const float*)prm.part_ml, nsplit, (int)head_dim, (int)num_heads,
-                         out, ldo, so, ctx_lens, (int)lanes, (int)num_kv_heads, prm.warps, (int)hpb)))
+                         out, ldo, so, ctx_lens, (int)lanes, (int)num_kv_heads, prm.warps, (int)hpb,
+                         (int)max_pages * 16)))
       return rc;
   }
   return GLACIER_CUDA_OK;

@@ -70,6 +70,7 @@ struct glacier_cuda_int4_weight {
   int device = 0;
   uint32_t in_f = 0, out_f = 0, group = 0;
   DeviceBuffer packed, scales, input, output, logits, argmax_ws, argmax_out, matmul_ws;
+  DeviceBuffer lm_arg;  // LM-head argmax in the GEMV epilogue: per-tile winners
   Int4Weight w;
 };
 
@@ -161,6 +162,10 @@ glacier_cuda_int4_weight* glacier_cuda_int4_weight_create_ex(glacier_cuda_contex
             !h->input.ensure((size_t)in_features * 4) && !h->output.ensure((size_t)out_features * 4);
   if (ok) {
     ok = cudaMemcpy(h->packed.p, packed, need_packed, cudaMemcpyHostToDevice) == cudaSuccess;
+    if (scale_dtype == 1) {
+      const uint16_t* hs = static_cast<const uint16_t*>(scales);
+      for (uint64_t i = 0; i < need_scales && !w.nonfinite; ++i) w.nonfinite = half_bits_nonfinite(hs[i]);
+    }
     if (ok && rows) {
       std::vector<uint8_t> staged((size_t)out_features * stride * esz, 0);
       const uint8_t* src = static_cast<const uint8_t*>(scales);
@@ -272,6 +277,28 @@ int glacier_cuda_int4_weight_lmhead_argmax(glacier_cuda_int4_weight* weight, con
   int rc = bind(weight->device);
   if (rc) return rc;
   const size_t n = weight->out_f;
+  const cudaStream_t s = (cudaStream_t)stream;
+  if (!status_out) {
+    if ((rc = weight->argmax_out.ensure(batch * 4))) return rc;
+    status_out = (int32_t*)weight->argmax_out.p;
+  }
+  // Up to four rows on the tensor-core GEMV: the argmax runs in its epilogue and
+  // no logits are written unless logits_out is given.
+  if (batch <= 4 && weight->w.tc) {
+    if ((rc = weight->lm_arg.ensure(gemv_argmax_partials_bytes(n)))) return rc;
+    ArgmaxEpi ae;
+    ae.words = eligible_words;
+    ae.word_count = (int)word_count;
+    ae.tokens = tokens_out;
+    ae.status = status_out;
+    ae.results = results_out;
+    ae.partials = static_cast<int4*>(weight->lm_arg.p);
+    if (eligible_words)
+      GLC_REQUIRE(word_count == ceil_div(n, 64), "argmax: eligible mask needs %zu words per row, got %zu",
+                  ceil_div(n, 64), word_count);
+    rc = int4_linear_argmax(weight->w, x, weight->in_f, batch, logits_out, n, ae, s);
+    if (rc != GLACIER_CUDA_EUNSUPPORTED) return rc;
+  }
   float* logits = logits_out;
   if (!logits) {
     if ((rc = weight->logits.ensure(batch * n * 4))) return rc;
@@ -279,11 +306,6 @@ int glacier_cuda_int4_weight_lmhead_argmax(glacier_cuda_int4_weight* weight, con
   }
   const size_t ws = argmax_workspace_bytes(batch, n);
   if ((rc = weight->argmax_ws.ensure(ws))) return rc;
-  if (!status_out) {
-    if ((rc = weight->argmax_out.ensure(batch * 4))) return rc;
-    status_out = (int32_t*)weight->argmax_out.p;
-  }
-  const cudaStream_t s = (cudaStream_t)stream;
   if ((rc = int4_linear(weight->w, x, weight->in_f, batch, nullptr, logits, n, s))) return rc;
   return argmax_rows(logits, n, batch, n, eligible_words, word_count, results_out, tokens_out, status_out,
                      weight->argmax_ws.p, ws, s);

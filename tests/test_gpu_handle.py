@@ -125,6 +125,92 @@ def test_lmhead_argmax_with_masks(ctx):
         L.lib().glacier_cuda_int4_weight_destroy(w)
 
 
+def test_lmhead_argmax_epilogue_matches_the_two_pass_argmax(ctx):
+    """Up to four rows take the GEMV with the argmax in its epilogue; five rows take the GEMV
+    then the two-pass argmax.  Both give the same records (value, index, valid, saw_nan),
+    tokens and statuses, with and without a mask, and with a NaN row (scales of one output
+    row set to NaN) eligible or masked out."""
+    import ctypes as C
+    L = lib()
+    rng = np.random.default_rng(9)
+    vocab, dim, group = 3000, 512, 32
+    packed, scales = make(rng, vocab, dim, group)
+    scales = scales.copy()
+    scales.reshape(vocab, -1)[1234] = np.nan
+    w = L.handle(L.lib().glacier_cuda_int4_weight_create(ctx, p(packed), packed.size, p(scales), scales.size,
+                                                         group, dim, vocab))
+
+    class Rec(C.Structure):
+        _fields_ = [("value", C.c_float), ("index", C.c_size_t), ("valid", C.c_int), ("saw_nan", C.c_int)]
+
+    try:
+        x = rng.standard_normal((5, dim)).astype(np.float32)
+        xd = torch.from_numpy(x).cuda()
+        nw = -(-vocab // 64)
+        masks = {
+            "none": None,
+            "nan_masked_out": np.full((5, nw), -1, np.int64),
+            "sparse": rng.integers(0, 2**63, size=(5, nw), dtype=np.int64),
+        }
+        masks["nan_masked_out"][:, 1234 // 64] &= ~(1 << (1234 % 64))
+        for m in masks.values():
+            if m is not None:
+                m[:, -1] &= (1 << (vocab % 64)) - 1
+        for name, m in masks.items():
+            got = {}
+            for batch in (4, 5):
+                toks = torch.zeros(batch, dtype=torch.int32, device="cuda")
+                st = torch.zeros(batch, dtype=torch.int32, device="cuda")
+                rec = torch.zeros((batch, C.sizeof(Rec)), dtype=torch.uint8, device="cuda")
+                wd = None if m is None else torch.from_numpy(m[:batch].copy()).cuda()
+                L.call("glacier_cuda_int4_weight_lmhead_argmax", w, xd.data_ptr(), batch,
+                       None if wd is None else wd.data_ptr(), 0 if wd is None else nw, toks.data_ptr(),
+                       st.data_ptr(), rec.data_ptr(), None, None)
+                torch.cuda.synchronize()
+                recs = [Rec.from_buffer_copy(rec[b].cpu().numpy().tobytes()) for b in range(batch)]
+                got[batch] = (toks.cpu().tolist()[:4], st.cpu().tolist()[:4],
+                              [(r.value, r.index, r.valid, r.saw_nan) for r in recs[:4]])
+            assert got[4] == got[5], name
+            if name == "none":
+                assert got[4][1] == [L.ENAN] * 4 and got[4][0] == [-1] * 4
+            if name == "nan_masked_out":
+                assert got[4][1] == [0] * 4
+    finally:
+        L.lib().glacier_cuda_int4_weight_destroy(w)
+
+
+def test_fp16_scales_with_inf_and_nan_propagate(ctx):
+    """A weight whose fp16 scales hold an infinity and a NaN: the NaN row comes out NaN and the
+    infinity row non-finite, as in the oracle, not as the large finite numbers a finite-only
+    conversion makes; every other row matches the oracle."""
+    L = lib()
+    rng = np.random.default_rng(11)
+    M, K, G = 640, 512, 32
+    packed, scales = make(rng, M, K, G)
+    s16 = scales.astype(np.float16)
+    s16.reshape(M, -1)[7, 3] = np.inf
+    s16.reshape(M, -1)[300, 0] = np.nan
+    ref_scales = s16.astype(np.float32)
+    bits = s16.view(np.uint16)
+    w = L.handle(L.lib().glacier_cuda_int4_weight_create_ex(ctx, p(packed), packed.size, p(bits), bits.size, 1, G,
+                                                            K, M))
+    try:
+        x = rng.standard_normal((2, K)).astype(np.float32)
+        xd = torch.from_numpy(x).cuda()
+        y = torch.empty((2, M), device="cuda")
+        L.call("glacier_cuda_int4_weight_matmul", w, xd.data_ptr(), K, y.data_ptr(), M, 2, None, None)
+        torch.cuda.synchronize()
+        got = y.cpu().numpy()
+        ref = oracle.linear_int4(x, packed, ref_scales, M, K, G)
+        assert np.isnan(got[:, 300]).all() and np.isnan(ref[:, 300]).all()
+        assert not np.isfinite(got[:, 7]).any() and not np.isfinite(ref[:, 7]).any()
+        rest = np.ones(M, bool)
+        rest[[7, 300]] = False
+        assert np.isfinite(got[:, rest]).all() and max_rel_err(got[:, rest], ref[:, rest]) <= REL_TOL
+    finally:
+        L.lib().glacier_cuda_int4_weight_destroy(w)
+
+
 @pytest.mark.parametrize("bad", [None, np.nan, np.inf, -np.inf])
 def test_all_finite(bad):
     L = lib()

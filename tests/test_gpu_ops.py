@@ -110,6 +110,25 @@ def test_paged_attention_matches_oracle(heads, kv_heads, hd, ctxs):
         assert max_rel_err(out[b], ref) <= REL_TOL, b
 
 
+def test_paged_attention_clamps_a_context_past_the_block_table():
+    """A context longer than the block table covers (here 70 positions over 4 pages) is
+    clamped to the table's 64 positions: the kernels never index past the lane's table row,
+    and the lane attends exactly what the table holds."""
+    from glacier_b200 import ops
+    rng = np.random.default_rng(5)
+    heads, kv_heads, hd, layer, L = 8, 2, 64, 0, 1
+    pf = oracle.page_floats(L, kv_heads * hd)
+    max_pages = 4
+    bt = np.arange(2 * max_pages, dtype=np.int32).reshape(2, max_pages)
+    pool = rng.standard_normal(2 * max_pages * pf, dtype=np.float32)
+    q = rng.standard_normal((2, heads * hd), dtype=np.float32)
+    out = host(ops.paged_attention_f32(dev(q), dev(pool), pf, dev(bt), dev(np.array([40, 70], np.int32)),
+                                       max_pages * 16, layer, heads, kv_heads, hd))
+    for b, c in enumerate([40, 64]):
+        ref = oracle.paged_attention(q[b], pool, pf, bt[b], c, layer, heads, kv_heads, hd)
+        assert max_rel_err(out[b], ref) <= REL_TOL, b
+
+
 def test_argmax_eligible_semantics():
     from glacier_b200 import ops
     # sampling.zig:252-286 cases, one per row, n = 130 (3 words per row).
