@@ -154,8 +154,6 @@ bool gemm_tc_supported(const Int4Weight& w);
 int split_activation(const float* x, size_t ldx, size_t n, size_t K, size_t np, __half* xs, float* xscale,
                      cudaStream_t stream);
 int encode_split_map(CUtensorMap* map, const __half* xs, size_t np, size_t K);
-int gemm_int4_tc(const Int4Weight& w, const CUtensorMap& xmap, const float* xscale, size_t n, size_t np, float* y,
-                 size_t ldy, int nsplit, size_t split_stride, const float* bias, cudaStream_t stream);
 int gemm_device_error(int clear);
 int attn_device_error(int clear);
 int persist_device_error(int clear);

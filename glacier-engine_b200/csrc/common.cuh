@@ -156,9 +156,12 @@ int int4_linear_q8(const Int4Weight& w, const float* x, size_t ldx, size_t batch
 int int4_linear_swiglu(const Int4Weight& w, const float* gate, const float* up, size_t ld, size_t batch,
                        const float* bias, float* y, size_t ldy, cudaStream_t stream);
 
-// Epilogue of the LM head's GEMV: the eligible argmax of each row (the semantics
-// of argmax_rows) from per-tile winners, which a second kernel reduces.
-// `partials` holds gemv_argmax_partials_bytes(M) bytes.
+// Epilogue of the LM head's GEMV (up to 4 rows): the eligible argmax of each
+// activation row (the semantics of argmax_rows).  Every warp reduces the 32
+// output columns it produced to one winner record {value, index, NaN seen,
+// eligible count} at partials[row * records + column / 32]; a one-CTA-per-row
+// kernel (argmax_records_reduce) reduces the records.  `partials` holds
+// argmax_records_bytes(rows, M) bytes.
 struct ArgmaxEpi {
   const uint64_t* words = nullptr;  // eligibility bitset rows of word_count words, or null
   int word_count = 0;
@@ -173,7 +176,14 @@ struct ArgmaxEpi {
 // GLACIER_CUDA_EUNSUPPORTED when the tensor-core GEMV does not apply.
 int int4_linear_argmax(const Int4Weight& w, const float* x, size_t ldx, size_t batch, float* y, size_t ldy,
                        const ArgmaxEpi& a, cudaStream_t stream);
-size_t gemv_argmax_partials_bytes(size_t M);
+size_t argmax_records_bytes(size_t rows, size_t M);
+
+// The tcgen05 GEMM on split-form activations (int4_gemm_tc.cu): y[b, :] for the
+// n live rows of np, nsplit K-split partials split_stride apart.
+int gemm_int4_tc(const Int4Weight& w, const CUtensorMap& xmap, const float* xscale, size_t n, size_t np, float* y,
+                 size_t ldy, int nsplit, size_t split_stride, const float* bias, cudaStream_t stream);
+// Tokens, statuses and records of `rows` rows from their `records` winner records each.
+int argmax_records_reduce(const ArgmaxEpi& a, size_t rows, size_t records, size_t n, cudaStream_t stream);
 int* ops_error_word();
 
 // Destination of an activation block that feeds the tensor-core GEMM: rows of
@@ -428,6 +438,28 @@ __device__ __forceinline__ void store_split8(const SplitOut& so, int r, size_t K
 __device__ __forceinline__ float half_to_float_bits(uint32_t h) {
   const uint32_t b = ((h & 0x8000u) << 16) | ((h & 0x7FFFu) << 13);
   return __uint_as_float(b) * 0x1p112f;
+}
+
+// Argmax candidate order of argmaxEligible (sampling.zig:55-107): larger value,
+// equal values to the lower index; i < 0 is "none".
+__device__ __forceinline__ bool arg_better(float av, int ai, float bv, int bi) {
+  if (ai < 0) return false;
+  if (bi < 0) return true;
+  return av > bv || (av == bv && ai < bi);
+}
+
+__device__ __forceinline__ void arg_warp_reduce(float& v, int& i, int& nan, int& elig) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float tv = __shfl_xor_sync(0xffffffffu, v, o);
+    const int ti = __shfl_xor_sync(0xffffffffu, i, o);
+    if (arg_better(tv, ti, v, i)) {
+      v = tv;
+      i = ti;
+    }
+    nan |= __shfl_xor_sync(0xffffffffu, nan, o);
+    elig += __shfl_xor_sync(0xffffffffu, elig, o);
+  }
 }
 
 // fp16 scale bits with exponent 31 (infinity or NaN).

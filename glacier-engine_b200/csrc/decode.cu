@@ -68,8 +68,6 @@ int split_activation(const float* x, size_t ldx, size_t n, size_t K, size_t np, 
                      cudaStream_t stream);
 int encode_split_map(CUtensorMap* map, const __half* xs, size_t np, size_t K);
 int gemm_splits(size_t M, size_t K);
-int gemm_int4_tc(const Int4Weight& w, const CUtensorMap& xmap, const float* xscale, size_t n, size_t np, float* y,
-                 size_t ldy, int nsplit, size_t split_stride, const float* bias, cudaStream_t stream);
 
 void StepProfiler::mark(int kind, cudaStream_t stream) {
   if (!on) return;
@@ -564,7 +562,7 @@ int glacier_cuda_model_reserve(glacier_cuda_model* m, size_t max_lanes, size_t m
       (rc = m->down.alloc(L * c.dim * 4)) || (rc = m->logits.alloc(L * (size_t)c.vocab * 4)) ||
       (rc = m->ctx.alloc(L * 4)) || (rc = m->att_ws.alloc(m->att_floats * 4)) ||
       (rc = m->arg_ws.alloc(m->arg_bytes)) || (rc = m->status.alloc(L * 4)) || (rc = m->pf_pos.alloc(L * 4)) ||
-      (rc = m->pf_bt.alloc(L * max_pages * 4)) || (rc = m->lm_arg.alloc(gemv_argmax_partials_bytes(c.vocab))))
+      (rc = m->pf_bt.alloc(L * max_pages * 4)) || (rc = m->lm_arg.alloc(argmax_records_bytes(L, c.vocab))))
     return rc;
   m->max_lanes = max_lanes;
   m->max_pages = max_pages;
@@ -679,15 +677,15 @@ static int step_impl(glacier_cuda_model* m, glacier_cuda_kv* kv, size_t lanes, c
                        ops_error_word())))
     return rc;
   int32_t* st_out = status_out ? status_out : m->status.as<int32_t>();
-  // GEMV mode: the LM head's epilogue picks the tokens (no argmax pass, and the
-  // logits are written only when the caller asks for them).
+  // The LM head's epilogue picks the tokens (no argmax pass over the logits,
+  // which are written only when the caller asks for them).
+  ArgmaxEpi ae;
+  ae.words = eligible;
+  ae.word_count = (int)eligible_words;
+  ae.tokens = tokens_out;
+  ae.status = st_out;
+  ae.partials = m->lm_arg.as<int4>();
   auto lm_head_argmax = [&](const float* xin, size_t rows) -> int {
-    ArgmaxEpi ae;
-    ae.words = eligible;
-    ae.word_count = (int)eligible_words;
-    ae.tokens = tokens_out;
-    ae.status = st_out;
-    ae.partials = m->lm_arg.as<int4>();
     return int4_linear_argmax(m->lm.w, xin, D, rows, logits_out, c.vocab, ae, st);
   };
   if ((rc = m->emb_f32 ? embed_gather(m->embedding.as<float>(), c.vocab, D, tokens, B, x, D, st)
@@ -804,6 +802,9 @@ static int step_impl(glacier_cuda_model* m, glacier_cuda_kv* kv, size_t lanes, c
                         m->gemm ? nullptr : hn, D, B, D, st, so_d)))
     return rc;
   mark(GLACIER_CUDA_STEP_LM_HEAD);
+  // GEMV mode: the argmax runs in the LM head's epilogue.  The tcgen05 GEMM
+  // writes the logits and the two-pass argmax reads them: an epilogue argmax
+  // there (64 cross-row warp reductions per tile) doubled the LM head's time.
   if (!m->gemm) {
     rc = lm_head_argmax(hn, B);
     if (rc != GLACIER_CUDA_EUNSUPPORTED) {

@@ -61,27 +61,6 @@ struct GemvParams {
 
 struct NoEpi {};  // the plain instantiation's (empty) epilogue argument
 
-// Argmax candidate order of argmaxEligible (sampling.zig:55-107): larger value,
-// equal values to the lower index; i < 0 is "none".
-__device__ __forceinline__ bool arg_better(float av, int ai, float bv, int bi) {
-  if (ai < 0) return false;
-  if (bi < 0) return true;
-  return av > bv || (av == bv && ai < bi);
-}
-
-__device__ __forceinline__ void arg_warp_reduce(float& v, int& i, int& nan, int& elig) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float tv = __shfl_xor_sync(0xffffffffu, v, o);
-    const int ti = __shfl_xor_sync(0xffffffffu, i, o);
-    if (arg_better(tv, ti, v, i)) {
-      v = tv;
-      i = ti;
-    }
-    nan |= __shfl_xor_sync(0xffffffffu, nan, o);
-    elig += __shfl_xor_sync(0xffffffffu, elig, o);
-  }
-}
 
 __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                           uint32_t b0, uint32_t b1) {
@@ -502,7 +481,13 @@ int gemv_int4_tc(const Int4Weight& w, const float* x, size_t ldx, size_t batch, 
                      : launch_gemv_tc<__half>(w, x, xu, ldx, batch, bias, y, ldy, stream, NoEpi());
 }
 
-size_t gemv_argmax_partials_bytes(size_t M) { return 4 * ceil_div(M, (size_t)kRows) * (kRows / 32) * sizeof(int4); }
+size_t argmax_records_bytes(size_t rows, size_t M) {
+  return rows * ceil_div(M, (size_t)kRows) * (kRows / 32) * sizeof(int4);  // one record per 32 rows of a 128-row tile
+}
+
+int argmax_records_reduce(const ArgmaxEpi& a, size_t rows, size_t records, size_t n, cudaStream_t stream) {
+  return launch_pdl(argmax_tiles_kernel, dim3((unsigned)rows), dim3(1024), 0, stream, 1, a, (int)records, (int)n);
+}
 
 int int4_linear_argmax(const Int4Weight& w, const float* x, size_t ldx, size_t batch, float* y, size_t ldy,
                        const ArgmaxEpi& a, cudaStream_t stream) {
@@ -515,8 +500,7 @@ int int4_linear_argmax(const Int4Weight& w, const float* x, size_t ldx, size_t b
                  : w.nonfinite ? launch_gemv_tc<HalfExact>(w, x, nullptr, ldx, batch, nullptr, y, ldy, stream, a)
                                : launch_gemv_tc<__half>(w, x, nullptr, ldx, batch, nullptr, y, ldy, stream, a);
   if (rc) return rc;
-  return launch_pdl(argmax_tiles_kernel, dim3((unsigned)batch), dim3(1024), 0, stream, 1, a,
-                    (int)(ceil_div(w.M, (size_t)kRows) * (kRows / 32)), (int)w.M);
+  return argmax_records_reduce(a, batch, ceil_div(w.M, (size_t)kRows) * (kRows / 32), w.M, stream);
 }
 
 int gemv_device_error(int clear) {

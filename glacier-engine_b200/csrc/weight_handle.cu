@@ -70,7 +70,7 @@ struct glacier_cuda_int4_weight {
   int device = 0;
   uint32_t in_f = 0, out_f = 0, group = 0;
   DeviceBuffer packed, scales, input, output, logits, argmax_ws, argmax_out, matmul_ws;
-  DeviceBuffer lm_arg;  // LM-head argmax in the GEMV epilogue: per-tile winners
+  DeviceBuffer lm_arg;  // LM-head argmax in the GEMV epilogue: winner records per 32 rows
   Int4Weight w;
 };
 
@@ -285,7 +285,7 @@ int glacier_cuda_int4_weight_lmhead_argmax(glacier_cuda_int4_weight* weight, con
   // Up to four rows on the tensor-core GEMV: the argmax runs in its epilogue and
   // no logits are written unless logits_out is given.
   if (batch <= 4 && weight->w.tc) {
-    if ((rc = weight->lm_arg.ensure(gemv_argmax_partials_bytes(n)))) return rc;
+    if ((rc = weight->lm_arg.ensure(argmax_records_bytes(batch, n)))) return rc;
     ArgmaxEpi ae;
     ae.words = eligible_words;
     ae.word_count = (int)word_count;

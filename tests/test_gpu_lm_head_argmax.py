@@ -1,10 +1,10 @@
-"""The GEMV-mode decode step's LM head (4 lanes or fewer) with the eligible argmax in its
-epilogue, against the semantics of argmaxEligible (src/sampling.zig:55-107): logitless steps,
-masks, tail bits, NaN rows; and a position past the block table (context clamped to 0, the
-bad-input word raised, the next step unharmed).
+"""The decode step's greedy selection against the semantics of argmaxEligible
+(src/sampling.zig:55-107) -- logitless steps, masks, tail bits, NaN rows -- in both forms: the
+argmax in the LM head GEMV's epilogue (4 lanes or fewer) and the tcgen05 GEMM's logits followed
+by the two-pass argmax (more lanes).  And a position past the block table: context clamped to 0,
+the bad-input word raised, the next step unharmed.
 
-Decode parity against the oracle runs through tests/test_gpu_decode.py and test_gpu_configs.py,
-whose GEMV-mode cases take this LM head.
+Decode parity against the oracle runs through tests/test_gpu_decode.py and test_gpu_configs.py.
 """
 import numpy as np
 import pytest
@@ -31,64 +31,80 @@ def _session(model, lanes, max_pages=8, seed=1):
     return dm, sess
 
 
-def test_logitless_step_picks_the_argmax_of_the_logits_step():
+@pytest.mark.parametrize("lanes", [3, 9])
+def test_logitless_step_picks_the_argmax_of_the_logits_step(lanes):
     """Without a logits buffer the LM head writes no logits; the ids equal those of the same step
     with logits, which are the first maximum of each row."""
     from glacier_b200.model import SyntheticModel
-    dm, sess = _session(SyntheticModel(_cfg(), seed=4), 3)
+    dm, sess = _session(SyntheticModel(_cfg(), seed=4), lanes)
     start = sess.pages().clone()
-    lg = torch.full((3, 2048), float("nan"), dtype=torch.float32, device="cuda")
-    with_logits = sess.step(tokens=[5, 6, 7], positions=[30, 31, 32], logits=lg).cpu().tolist()
+    toks, pos = list(range(5, 5 + lanes)), list(range(30, 30 + lanes))
+    lg = torch.full((lanes, 2048), float("nan"), dtype=torch.float32, device="cuda")
+    with_logits = sess.step(tokens=toks, positions=pos, logits=lg).cpu().tolist()
     rows = lg.cpu().numpy()
     assert with_logits == [int(np.argmax(r)) for r in rows]
     sess.pages().copy_(start)
-    logitless = sess.step(tokens=[5, 6, 7], positions=[30, 31, 32]).cpu().tolist()
-    assert logitless == with_logits and sess.status.cpu().tolist() == [0, 0, 0]
+    logitless = sess.step(tokens=toks, positions=pos).cpu().tolist()
+    assert logitless == with_logits and sess.status.cpu().tolist() == [0] * lanes
     sess.close()
     dm.close()
 
 
-def test_argmax_epilogue_masks_tail_bits_and_empty_masks():
-    """Lane 0: tokens 192..207 only; lane 1: every token; lane 2: a bit past the vocabulary
-    (InvalidEligibleMask); lane 3: no bit set (InvalidEligibleMask)."""
+@pytest.mark.parametrize("lanes", [4, 12])
+def test_argmax_epilogue_masks_tail_bits_and_empty_masks(lanes):
+    """Lane i follows pattern i % 4.  0: tokens 192..207 only; 1: every token; 2: token 0 only;
+    3: no bit set (InvalidEligibleMask).  Then a vocabulary that is not a multiple of 64: a bit
+    past it (InvalidEligibleMask) or the last token alone."""
     from glacier_b200 import _lib
     from glacier_b200.model import SyntheticModel
     cfg = _cfg()
-    dm, sess = _session(SyntheticModel(cfg, seed=6), 4)
-    start = sess.pages().clone()
-    words = np.zeros((4, cfg.vocab // 64), np.uint64)
-    words[0, 3] = 0xFFFF
-    words[1, :] = np.uint64(0xFFFFFFFFFFFFFFFF)
-    words[2, 0] = 1
-    lg = torch.empty((4, cfg.vocab), dtype=torch.float32, device="cuda")
+    dm, sess = _session(SyntheticModel(cfg, seed=6), lanes)
+    words = np.zeros((lanes, cfg.vocab // 64), np.uint64)
+    for b in range(lanes):
+        if b % 4 == 0:
+            words[b, 3] = 0xFFFF
+        elif b % 4 == 1:
+            words[b, :] = np.uint64(0xFFFFFFFFFFFFFFFF)
+        elif b % 4 == 2:
+            words[b, 0] = 1
+    lg = torch.empty((lanes, cfg.vocab), dtype=torch.float32, device="cuda")
     elig = torch.from_numpy(words.view(np.int64)).cuda()
-    toks, pos = [1, 2, 3, 4], [20, 21, 22, 23]
+    toks, pos = list(range(1, 1 + lanes)), list(range(20, 20 + lanes))
     out = sess.step(tokens=toks, positions=pos, eligible=elig, logits=lg).cpu().tolist()
     rows = lg.cpu().numpy()
     st = sess.status.cpu().tolist()
-    assert out[0] == 192 + int(np.argmax(rows[0, 192:208])) and st[0] == 0
-    assert out[1] == int(np.argmax(rows[1])) and st[1] == 0
-    assert st[2] == 0 and out[2] == 0  # bit 0 only: token 0 (the vocabulary is a multiple of 64)
-    assert st[3] == _lib.EMASK and out[3] == -1
-    # A vocabulary that is not a multiple of 64 leaves tail bits in the last word.
+    for b in range(lanes):
+        if b % 4 == 0:
+            assert out[b] == 192 + int(np.argmax(rows[b, 192:208])) and st[b] == 0, b
+        elif b % 4 == 1:
+            assert out[b] == int(np.argmax(rows[b])) and st[b] == 0, b
+        elif b % 4 == 2:
+            assert out[b] == 0 and st[b] == 0, b
+        else:
+            assert out[b] == -1 and st[b] == _lib.EMASK, b
     sess.close()
     dm.close()
     from glacier_b200.model import ModelConfig
     cfg2 = ModelConfig(num_layers=1, dim=256, hidden=512, num_heads=8, num_kv_heads=2, head_dim=64, vocab=1000)
-    dm, sess = _session(SyntheticModel(cfg2, seed=2), 2)
-    w2 = np.zeros((2, -(-cfg2.vocab // 64)), np.uint64)
-    w2[0, -1] = np.uint64(1) << np.uint64(1000 % 64)  # bit 1000: past the vocabulary
-    w2[0, 0] = 1
-    w2[1, -1] = np.uint64(1) << np.uint64(1000 % 64 - 1)  # bit 999: the last token
-    out = sess.step(tokens=[1, 2], positions=[3, 4], eligible=torch.from_numpy(w2.view(np.int64)).cuda())
-    assert sess.status.cpu().tolist() == [_lib.EMASK, 0]
-    assert out.cpu().tolist() == [-1, 999]
+    dm, sess = _session(SyntheticModel(cfg2, seed=2), lanes)
+    w2 = np.zeros((lanes, -(-cfg2.vocab // 64)), np.uint64)
+    for b in range(lanes):
+        if b % 2 == 0:
+            w2[b, -1] = np.uint64(1) << np.uint64(1000 % 64)  # bit 1000: past the vocabulary
+            w2[b, 0] = 1
+        else:
+            w2[b, -1] = np.uint64(1) << np.uint64(1000 % 64 - 1)  # bit 999: the last token
+    out = sess.step(tokens=list(range(lanes)), positions=list(range(3, 3 + lanes)),
+                    eligible=torch.from_numpy(w2.view(np.int64)).cuda())
+    assert sess.status.cpu().tolist() == [_lib.EMASK if b % 2 == 0 else 0 for b in range(lanes)]
+    assert out.cpu().tolist() == [-1 if b % 2 == 0 else 999 for b in range(lanes)]
     assert _lib.lib().glacier_cuda_device_status(1) == 0
     sess.close()
     dm.close()
 
 
-def test_argmax_epilogue_reports_an_eligible_nan_row():
+@pytest.mark.parametrize("lanes", [2, 8])
+def test_argmax_epilogue_reports_an_eligible_nan_row(lanes):
     """An LM-head row whose scales are NaN gives a NaN logit: EligibleLogitNaN for every lane
     unless the mask leaves that token out."""
     from glacier_b200 import _lib
@@ -99,18 +115,19 @@ def test_argmax_epilogue_reports_an_eligible_nan_row():
     scales = scales.copy().reshape(cfg.vocab, -1)
     scales[777] = np.nan
     m.lm_head = (packed, scales.ravel())
-    dm, sess = _session(m, 2)
-    out = sess.step(tokens=[3, 4], positions=[10, 11]).cpu().tolist()
-    assert sess.status.cpu().tolist() == [_lib.ENAN, _lib.ENAN] and out == [-1, -1]
-    words = np.full((2, cfg.vocab // 64), np.uint64(0xFFFFFFFFFFFFFFFF), np.uint64)
+    dm, sess = _session(m, lanes)
+    toks, pos = list(range(3, 3 + lanes)), list(range(10, 10 + lanes))
+    out = sess.step(tokens=toks, positions=pos).cpu().tolist()
+    assert sess.status.cpu().tolist() == [_lib.ENAN] * lanes and out == [-1] * lanes
+    words = np.full((lanes, cfg.vocab // 64), np.uint64(0xFFFFFFFFFFFFFFFF), np.uint64)
     words[:, 777 // 64] &= ~(np.uint64(1) << np.uint64(777 % 64))
-    lg = torch.empty((2, cfg.vocab), dtype=torch.float32, device="cuda")
-    out = sess.step(tokens=[3, 4], positions=[10, 11], eligible=torch.from_numpy(words.view(np.int64)).cuda(),
+    lg = torch.empty((lanes, cfg.vocab), dtype=torch.float32, device="cuda")
+    out = sess.step(tokens=toks, positions=pos, eligible=torch.from_numpy(words.view(np.int64)).cuda(),
                     logits=lg).cpu().tolist()
     rows = lg.cpu().numpy()
     assert np.isnan(rows[:, 777]).all()
     rows[:, 777] = -np.inf
-    assert sess.status.cpu().tolist() == [0, 0] and out == [int(np.argmax(r)) for r in rows]
+    assert sess.status.cpu().tolist() == [0] * lanes and out == [int(np.argmax(r)) for r in rows]
     sess.close()
     dm.close()
 
