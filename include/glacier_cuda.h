@@ -271,7 +271,11 @@ size_t glacier_cuda_kv_page_floats(const glacier_cuda_kv *kv);
  * tokens[b] at position positions[b] (its K/V row is written there; context = positions[b]+1)
  * through block_tables[b][0..max_pages).  eligible (NULL = all tokens) holds
  * ceil(vocab/64) words per lane.  tokens_out[b] = next token or -1; status_out[b] (may be
- * NULL) = 0 / GLACIER_CUDA_EMASK / GLACIER_CUDA_ENAN; logits_out [lanes, vocab] may be NULL. */
+ * NULL) = 0 / GLACIER_CUDA_EMASK / GLACIER_CUDA_ENAN; logits_out [lanes, vocab] may be NULL.
+ * With 4 lanes or fewer the eligible argmax runs in the LM head's epilogue (logitless greedy,
+ * int4_neon.c:1075-1254): logits are written only to a given logits_out.  A position outside
+ * the RoPE table or past the block table gives that lane context 0, writes no K/V and raises
+ * the bad-input device status (glacier_cuda_device_status = 2). */
 int glacier_cuda_decode_step(glacier_cuda_model *model, glacier_cuda_kv *kv, size_t lanes,
                              const int32_t *tokens, const int32_t *positions, const int32_t *block_tables,
                              size_t max_pages, const uint64_t *eligible, size_t eligible_words,
@@ -327,8 +331,8 @@ enum glacier_cuda_step_kind {
   GLACIER_CUDA_STEP_PROJ_GATE_UP,  /* fused gate/up INT4 projection */
   GLACIER_CUDA_STEP_SILU,
   GLACIER_CUDA_STEP_PROJ_DOWN,
-  GLACIER_CUDA_STEP_LM_HEAD,
-  GLACIER_CUDA_STEP_ARGMAX,
+  GLACIER_CUDA_STEP_LM_HEAD,       /* with 4 lanes or fewer: the projection and its epilogue argmax */
+  GLACIER_CUDA_STEP_ARGMAX,        /* the two-pass argmax over written logits (more lanes) */
   GLACIER_CUDA_STEP_ALL_REDUCE,    /* tensor parallel: split-K sum + NCCL all-reduce of o / down */
   GLACIER_CUDA_STEP_KINDS
 };
@@ -338,10 +342,11 @@ int glacier_cuda_model_profile_read(glacier_cuda_model *model, double *ms, uint6
 /* Step selection, no reference counterpart.  A model reserved for one lane runs each greedy
  * decode step (glacier_cuda_decode_step) as one persistent kernel over every SM, with the
  * phases of the step separated by grid barriers, when enable = 1; enable = 0 (the default)
- * runs the multi-kernel step (the same operators, one launch per kernel class).  Returns 1 when the persistent step is built for the current reservation, 0 when the
- * model or reservation is outside its contract (more than one lane; not group 32 with fp16
- * scales; head dim other than 64 / 128), negative on error.  With profiling on, its phases
- * are filed under the kernel classes they replace. */
+ * runs the multi-kernel step (the same operators, one launch per kernel class), which is the
+ * faster of the two on B200.  Returns 1 when the persistent step is built for the current
+ * reservation, 0 when the model or reservation is outside its contract (more than one lane;
+ * not group 32 with finite fp16 scales; head dim other than 64 / 128), negative on error.
+ * With profiling on, its phases are filed under the kernel classes they replace. */
 int glacier_cuda_model_persistent(glacier_cuda_model *model, int enable);
 
 /* ------------------------------------------------------------------------
@@ -391,7 +396,8 @@ int glacier_cuda_int4_weight_matmul(glacier_cuda_int4_weight *weight, const floa
 /* LM head + argmaxEligible (sampling.zig:55-107) per row: device x [batch, in],
  * optional eligibility words [batch][word_count], tokens / status / 24-byte
  * results per row as glacier_cuda_argmax_eligible_f32 writes them.  status_out,
- * results_out and logits_out may be NULL. */
+ * results_out and logits_out may be NULL.  Up to 4 rows on the tensor-core GEMV, the argmax
+ * runs in the projection's epilogue and no logits are written unless logits_out is given. */
 int glacier_cuda_int4_weight_lmhead_argmax(glacier_cuda_int4_weight *weight, const float *x, size_t batch,
                                            const uint64_t *eligible_words, size_t word_count, int32_t *tokens_out,
                                            int32_t *status_out, glacier_argmax_result *results_out,
