@@ -23,7 +23,10 @@
 #include <string.h>
 
 #include <algorithm>
+#include <atomic>
 #include <memory>
+#include <mutex>
+#include <thread>
 #include <vector>
 
 #include "persistent.cuh"
@@ -172,6 +175,103 @@ struct DevBuf {
   }
 };
 
+// Host -> device upload of weight bytes through two pinned bounce buffers: the
+// host copy of one chunk overlaps the DMA of the previous one, where a pageable
+// cudaMemcpy stages every byte itself.  Process-wide buffers under a mutex;
+// synchronous for the caller.
+int upload_h2d(void* dst, const void* src, size_t bytes) {
+  constexpr size_t kChunk = (size_t)32 << 20;
+  struct Bounce {
+    std::mutex mu;
+    void* buf[2] = {nullptr, nullptr};
+    cudaStream_t st = nullptr;
+    cudaEvent_t ev[2] = {nullptr, nullptr};
+    int device = -1;
+  };
+  static Bounce bb;
+  if (bytes < ((size_t)4 << 20)) {  // small tensors: one pageable copy
+    GLC_CHECK_CUDA(cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice));
+    return GLACIER_CUDA_OK;
+  }
+  std::lock_guard<std::mutex> lock(bb.mu);
+  int dev = 0;
+  GLC_CHECK_CUDA(cudaGetDevice(&dev));
+  if (bb.device != dev) {  // streams and events belong to the device that made them
+    if (bb.st) {
+      cudaStreamDestroy(bb.st);
+      for (auto& e : bb.ev) cudaEventDestroy(e);
+    }
+    bb.st = nullptr;
+    GLC_CHECK_CUDA(cudaStreamCreateWithFlags(&bb.st, cudaStreamNonBlocking));
+    for (auto& e : bb.ev) GLC_CHECK_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    for (auto& b : bb.buf)
+      if (!b) GLC_CHECK_CUDA(cudaMallocHost(&b, kChunk));
+    bb.device = dev;
+  }
+  const uint8_t* s = static_cast<const uint8_t*>(src);
+  uint8_t* d = static_cast<uint8_t*>(dst);
+  for (size_t off = 0, i = 0; off < bytes; off += kChunk, ++i) {
+    const size_t n = std::min(kChunk, bytes - off);
+    const int k = (int)(i & 1);
+    GLC_CHECK_CUDA(cudaEventSynchronize(bb.ev[k]));  // the DMA that last read this buffer is done
+    memcpy(bb.buf[k], s + off, n);
+    GLC_CHECK_CUDA(cudaMemcpyAsync(d + off, bb.buf[k], n, cudaMemcpyHostToDevice, bb.st));
+    GLC_CHECK_CUDA(cudaEventRecord(bb.ev[k], bb.st));
+  }
+  GLC_CHECK_CUDA(cudaStreamSynchronize(bb.st));
+  return GLACIER_CUDA_OK;
+}
+
+// Prepared runtime-image layouts back to row-major codes, on the device
+// (int4_weights.zig:113-170 rows4_k16; :42-54 PairNibble).  One thread per
+// (4-row tile t, 16-column block b).  In rows4_k16 the block is 32 contiguous
+// bytes ordered [4-column chunk c][row lane l][byte p]; as 16-bit units h[4c + l]
+// it is a 4 x 4 transpose: row l's 8 row-major bytes are h[l], h[4+l], h[8+l],
+// h[12+l].  A PairNibble block is 64 bytes [c][l][byte pair p][lo, hi] holding
+// gate codes in the low nibbles and up codes in the high ones.
+__global__ void rows4_to_rows_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, uint64_t tiles,
+                                     uint32_t blocks, uint64_t row_bytes) {
+  const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= tiles * blocks) return;
+  const uint64_t t = i / blocks, b = i % blocks;
+  const uint4* s = reinterpret_cast<const uint4*>(src + t * 4 * row_bytes + b * 32);
+  const uint4 a = s[0], c = s[1];
+  const uint32_t w[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+  auto h = [&](int k) { return (w[k >> 1] >> (16 * (k & 1))) & 0xFFFFu; };
+#pragma unroll
+  for (int l = 0; l < 4; ++l) {
+    const uint2 v = make_uint2(h(l) | h(4 + l) << 16, h(8 + l) | h(12 + l) << 16);
+    *reinterpret_cast<uint2*>(dst + (t * 4 + l) * row_bytes + b * 8) = v;
+  }
+}
+
+__global__ void pair_nibble_split_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ gate,
+                                         uint8_t* __restrict__ up, uint64_t tiles, uint32_t blocks,
+                                         uint64_t row_bytes) {
+  const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= tiles * blocks) return;
+  const uint64_t t = i / blocks, b = i % blocks;
+  const uint4* s = reinterpret_cast<const uint4*>(src + t * 4 * 2 * row_bytes + b * 64);
+  uint8_t by[64];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) *reinterpret_cast<uint4*>(by + 16 * q) = s[q];
+#pragma unroll
+  for (int l = 0; l < 4; ++l) {
+    uint32_t g[2] = {0, 0}, u[2] = {0, 0};
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+#pragma unroll
+      for (int p = 0; p < 2; ++p) {
+        const uint32_t lo = by[c * 16 + l * 4 + 2 * p], hi = by[c * 16 + l * 4 + 2 * p + 1];
+        const int o = c * 2 + p;  // byte of the row's 8
+        g[o >> 2] |= ((lo & 15u) | (hi & 15u) << 4) << (8 * (o & 3));
+        u[o >> 2] |= ((lo >> 4) | (hi & 0xF0u)) << (8 * (o & 3));
+      }
+    *reinterpret_cast<uint2*>(gate + (t * 4 + l) * row_bytes + b * 8) = make_uint2(g[0], g[1]);
+    *reinterpret_cast<uint2*>(up + (t * 4 + l) * row_bytes + b * 8) = make_uint2(u[0], u[1]);
+  }
+}
+
 // A fused INT4 matrix whose row blocks are uploaded piece by piece.
 struct FusedWeight {
   DevBuf packed, scales;
@@ -205,35 +305,108 @@ struct FusedWeight {
     return GLACIER_CUDA_OK;
   }
 
-  // One part given in the reference's Int4WeightData form: row-major packed
-  // codes and one f32 scale per group along the flat index.
-  int load_part(size_t part, const uint8_t* pk, size_t pk_bytes, const float* sc, size_t sc_count) {
+  size_t part_row0(size_t part) const {
+    size_t row0 = 0;
+    for (size_t i = 0; i < part; ++i) row0 += part_rows[i];
+    return row0;
+  }
+
+  int check_part(size_t part, size_t pk_bytes, size_t sc_count) const {
     GLC_REQUIRE(part < part_rows.size(), "weight part %zu out of range", part);
     const size_t rows = part_rows[part], K = w.K, group = w.group;
-    const size_t groups = K / group;
     GLC_REQUIRE(K % 2 == 0 && K % group == 0, "weight rows must hold whole bytes and groups (K=%zu g=%zu)", K,
                 group);
     GLC_REQUIRE(pk_bytes == rows * K / 2, "packed bytes %zu != %zu", pk_bytes, rows * K / 2);
-    GLC_REQUIRE(sc_count == rows * groups, "scale count %zu != %zu", sc_count, rows * groups);
-    size_t row0 = 0;
-    for (size_t i = 0; i < part; ++i) row0 += part_rows[i];
-    GLC_CHECK_CUDA(cudaMemcpy(packed.as<uint8_t>() + row0 * K / 2, pk, pk_bytes, cudaMemcpyHostToDevice));
+    GLC_REQUIRE(sc_count == rows * (K / group), "scale count %zu != %zu", sc_count, rows * (K / group));
+    return GLACIER_CUDA_OK;
+  }
+
+  // One part given in the reference's Int4WeightData form: row-major packed
+  // codes and one f32 scale per group along the flat index.
+  int load_part(size_t part, const uint8_t* pk, size_t pk_bytes, const float* sc, size_t sc_count) {
+    int rc = check_part(part, pk_bytes, sc_count);
+    if (rc) return rc;
+    if ((rc = upload_h2d(packed.as<uint8_t>() + part_row0(part) * w.K / 2, pk, pk_bytes))) return rc;
+    return load_scales(part, sc);
+  }
+
+  // The same with the codes in rows4_k16 order: uploaded as they are and put in
+  // row-major order by the device (the host never permutes them).
+  int load_part_rows4(size_t part, const uint8_t* pk, size_t pk_bytes, const float* sc, size_t sc_count) {
+    int rc = check_part(part, pk_bytes, sc_count);
+    if (rc) return rc;
+    const size_t rows = part_rows[part], K = w.K;
+    GLC_REQUIRE(rows % 4 == 0 && K % 16 == 0, "rows4_k16 needs rows %% 4 == 0 and K %% 16 == 0 (%zu x %zu)", rows,
+                K);
+    DevBuf stage;
+    if ((rc = stage.alloc(pk_bytes))) return rc;
+    if ((rc = upload_h2d(stage.p, pk, pk_bytes))) return rc;
+    const uint64_t tiles = rows / 4, blocks = K / 16, n = tiles * blocks;
+    rows4_to_rows_kernel<<<(unsigned)ceil_div(n, (size_t)256), 256>>>(
+        stage.as<uint8_t>(), packed.as<uint8_t>() + part_row0(part) * K / 2, tiles, (uint32_t)blocks, K / 2);
+    GLC_CHECK_LAUNCH();
+    GLC_CHECK_CUDA(cudaDeviceSynchronize());  // the staging buffer is freed on return
+    return load_scales(part, sc);
+  }
+
+  // A PairNibble record into parts 0 (gate) and 1 (up) of this fused matrix: the
+  // pair bytes are uploaded as they are and split on the device.
+  int load_pair(const uint8_t* pairs, size_t pair_bytes, const float* gate_sc, const float* up_sc, size_t sc_count) {
+    GLC_REQUIRE(part_rows.size() == 2 && part_rows[0] == part_rows[1], "PairNibble needs a gate/up matrix");
+    const size_t rows = part_rows[0], K = w.K;
+    int rc = check_part(0, pair_bytes / 2, sc_count);
+    if (rc) return rc;
+    GLC_REQUIRE(pair_bytes == rows * K && rows % 4 == 0 && K % 16 == 0, "PairNibble geometry (%zu bytes, %zu x %zu)",
+                pair_bytes, rows, K);
+    DevBuf stage;
+    if ((rc = stage.alloc(pair_bytes))) return rc;
+    if ((rc = upload_h2d(stage.p, pairs, pair_bytes))) return rc;
+    const uint64_t tiles = rows / 4, blocks = K / 16, n = tiles * blocks;
+    uint8_t* gate = packed.as<uint8_t>();
+    pair_nibble_split_kernel<<<(unsigned)ceil_div(n, (size_t)256), 256>>>(stage.as<uint8_t>(), gate,
+                                                                          gate + rows * K / 2, tiles,
+                                                                          (uint32_t)blocks, K / 2);
+    GLC_CHECK_LAUNCH();
+    GLC_CHECK_CUDA(cudaDeviceSynchronize());
+    if ((rc = load_scales(0, gate_sc))) return rc;
+    return load_scales(1, up_sc);
+  }
+
+  // Group scales of one part (f32, row-major): the fp16 mirror or the f32 copy.
+  int load_scales(size_t part, const float* sc) {
+    const size_t rows = part_rows[part], K = w.K, group = w.group;
+    const size_t groups = K / group;
+    const size_t row0 = part_row0(part);
     const size_t esz = f16 ? 2 : 4;
     std::vector<uint8_t> host(rows * scale_stride * esz, 0);
-    for (size_t r = 0; r < rows; ++r)
-      for (size_t g = 0; g < groups; ++g) {
-        const float s = sc[r * groups + g];
-        if (f16) {
-          // Round-to-nearest-even fp16 mirror (int4_weights.zig:348-358 withF16Scales).
-          const __half h = __float2half_rn(s);
-          memcpy(&host[(r * scale_stride + g) * 2], &h, 2);
-          if (half_bits_nonfinite(__half_as_ushort(h))) w.nonfinite = true;
-        } else {
-          memcpy(&host[(r * scale_stride + g) * 4], &s, 4);
+    // Rows spread over the host's cores (a 152064-row LM head has 17M scales).
+    std::atomic<bool> nonfinite{false};
+    auto convert = [&](size_t r0, size_t r1) {
+      bool nf = false;
+      for (size_t r = r0; r < r1; ++r)
+        for (size_t g = 0; g < groups; ++g) {
+          const float s = sc[r * groups + g];
+          if (f16) {
+            // Round-to-nearest-even fp16 mirror (int4_weights.zig:348-358 withF16Scales).
+            const uint16_t h = __half_as_ushort(__float2half_rn(s));
+            memcpy(&host[(r * scale_stride + g) * 2], &h, 2);
+            nf = nf || half_bits_nonfinite(h);
+          } else {
+            memcpy(&host[(r * scale_stride + g) * 4], &s, 4);
+          }
         }
-      }
-    GLC_CHECK_CUDA(cudaMemcpy(scales.as<uint8_t>() + row0 * scale_stride * esz, host.data(), host.size(),
-                              cudaMemcpyHostToDevice));
+      if (nf) nonfinite = true;
+    };
+    const unsigned nt = rows * groups < ((size_t)1 << 20)
+                            ? 1u
+                            : std::max(1u, std::min(std::thread::hardware_concurrency(), 32u));
+    std::vector<std::thread> pool;
+    for (unsigned t = 1; t < nt; ++t) pool.emplace_back(convert, rows * t / nt, rows * (t + 1) / nt);
+    convert(0, rows / nt);
+    for (auto& th : pool) th.join();
+    if (nonfinite) w.nonfinite = true;
+    const int rc = upload_h2d(scales.as<uint8_t>() + row0 * scale_stride * esz, host.data(), host.size());
+    if (rc) return rc;
     loaded[part] = true;
     return GLACIER_CUDA_OK;
   }
@@ -441,6 +614,44 @@ int glacier_cuda_model_load_int4(glacier_cuda_model* m, int layer, int kind, con
   const int rc = bind_device(m);
   if (rc) return rc;
   return fw->load_part(part, packed, packed_bytes, scales, scale_count);
+}
+
+int glacier_cuda_model_load_int4_rows4(glacier_cuda_model* m, int layer, int kind, const uint8_t* packed,
+                                       size_t packed_bytes, const float* scales, size_t scale_count) {
+  GLC_REQUIRE(m && packed && scales, "model_load_int4_rows4: null argument");
+  GLC_REQUIRE(!m->finalized, "model_load_int4_rows4: model already finalized");
+  size_t part = 0;
+  FusedWeight* fw = weight_slot(m, layer, kind, &part);
+  GLC_REQUIRE(fw, "model_load_int4_rows4: bad layer %d / kind %d", layer, kind);
+  const int rc = bind_device(m);
+  if (rc) return rc;
+  return fw->load_part_rows4(part, packed, packed_bytes, scales, scale_count);
+}
+
+int glacier_cuda_model_load_pair_nibble(glacier_cuda_model* m, int layer, const uint8_t* pairs, size_t pair_bytes,
+                                        const uint16_t* pair_scales, size_t scale_count) {
+  GLC_REQUIRE(m && pairs && pair_scales, "model_load_pair_nibble: null argument");
+  GLC_REQUIRE(!m->finalized, "model_load_pair_nibble: model already finalized");
+  GLC_REQUIRE(layer >= 0 && layer < (int)m->layers.size(), "model_load_pair_nibble: bad layer %d", layer);
+  const size_t F = m->cfg.hidden, D = m->cfg.dim, group = m->cfg.group_size;
+  GLC_REQUIRE(F % 4 == 0 && D % group == 0 && scale_count == 2 * F * (D / group),
+              "model_load_pair_nibble: %zu scales for a %zu x %zu pair (group %zu)", scale_count, F, D, group);
+  // Scale grid [tile][group][branch][lane] (int4_weights.zig:322-331) to row-major f32 per branch.
+  const size_t per_row = D / group;
+  std::vector<float> gs(F * per_row), us(F * per_row);
+  for (size_t t = 0; t < F / 4; ++t)
+    for (size_t g = 0; g < per_row; ++g)
+      for (size_t l = 0; l < 4; ++l) {
+        const size_t base = (t * per_row + g) * 8;
+        __half hg, hu;
+        memcpy(&hg, &pair_scales[base + l], 2);
+        memcpy(&hu, &pair_scales[base + 4 + l], 2);
+        gs[(t * 4 + l) * per_row + g] = __half2float(hg);
+        us[(t * 4 + l) * per_row + g] = __half2float(hu);
+      }
+  const int rc = bind_device(m);
+  if (rc) return rc;
+  return m->layers[layer]->gu.load_pair(pairs, pair_bytes, gs.data(), us.data(), gs.size());
 }
 
 int glacier_cuda_model_load_qio(glacier_cuda_model* m, int layer, int kind, const uint8_t* payload,

@@ -524,16 +524,10 @@ void rows4_to_row_major(const uint8_t* src, uint8_t* dst, uint64_t out_f, uint64
   });
 }
 
-// One INT4 record as row-major codes and row-major f32 scales.  Scale choice:
-// the f32 stream when present (the portable numerics), else the row-major
-// fp16 mirror, else the rows4 fp16 grid; fp16 widens to f32 exactly.
-void int4_row_major(const Image& im, const Rec& x, std::vector<uint8_t>* packed, std::vector<float>* scales) {
-  const uint8_t* pk = im.b + x.s[S_PACKED].off;
-  packed->resize(x.n / 2 + x.n % 2);
-  if (x.layout == LAY_ROW_MAJOR)
-    memcpy(packed->data(), pk, packed->size());
-  else
-    rows4_to_row_major(pk, packed->data(), x.out_f, x.in_f);
+// One INT4 record's row-major f32 scales.  Scale choice: the f32 stream when
+// present (the portable numerics), else the row-major fp16 mirror, else the
+// rows4 fp16 grid; fp16 widens to f32 exactly.
+void int4_scales(const Image& im, const Rec& x, std::vector<float>* scales) {
   const uint64_t groups = x.n / x.group + (x.n % x.group != 0);
   scales->resize(groups);
   if (x.s[S_F32].len) {
@@ -548,6 +542,17 @@ void int4_row_major(const Image& im, const Rec& x, std::vector<uint8_t>* packed,
         for (uint64_t l = 0; l < 4; ++l)
           (*scales)[(t * 4 + l) * per_row + g] = half_to_float(rd<uint16_t>(s4 + 2 * ((t * per_row + g) * 4 + l)));
   }
+}
+
+// One INT4 record as row-major codes (permuted on the host) and row-major f32 scales.
+void int4_row_major(const Image& im, const Rec& x, std::vector<uint8_t>* packed, std::vector<float>* scales) {
+  const uint8_t* pk = im.b + x.s[S_PACKED].off;
+  packed->resize(x.n / 2 + x.n % 2);
+  if (x.layout == LAY_ROW_MAJOR)
+    memcpy(packed->data(), pk, packed->size());
+  else
+    rows4_to_row_major(pk, packed->data(), x.out_f, x.in_f);
+  int4_scales(im, x, scales);
 }
 
 // A PairNibble record split into row-major gate and up tensors: the byte at
@@ -822,11 +827,16 @@ int glacier_cuda_model_load_glrt(glacier_cuda_model* model, const uint8_t* bytes
               "model_load_glrt: rms_eps / rope_theta differ from the image's");
   const uint64_t D = c.dim, F = c.hidden, KV = (uint64_t)c.num_kv_heads * c.head_dim;
 
-  std::vector<uint8_t> pk, pk2;
-  std::vector<float> sc, sc2;
+  std::vector<uint8_t> pk;
+  std::vector<float> sc;
+  // Codes go up as the image stores them; rows4_k16 is put in row-major order on the device.
   auto upload_int4 = [&](const Rec* r, int layer, int kind) {
-    int4_row_major(im, *r, &pk, &sc);
-    return glacier_cuda_model_load_int4(model, layer, kind, pk.data(), pk.size(), sc.data(), sc.size());
+    int4_scales(im, *r, &sc);
+    const uint8_t* codes = bytes + r->s[S_PACKED].off;
+    const size_t nbytes = r->n / 2 + r->n % 2;
+    if (r->layout == LAY_ROW_MAJOR)
+      return glacier_cuda_model_load_int4(model, layer, kind, codes, nbytes, sc.data(), sc.size());
+    return glacier_cuda_model_load_int4_rows4(model, layer, kind, codes, nbytes, sc.data(), sc.size());
   };
   auto upload_raw = [&](const Rec* r, int layer, int kind) {
     return glacier_cuda_model_load_f32(model, layer, kind, reinterpret_cast<const float*>(bytes + r->s[S_RAW].off),
@@ -860,16 +870,10 @@ int glacier_cuda_model_load_glrt(glacier_cuda_model* model, const uint8_t* bytes
         (rc = upload_int4(o, L, GLACIER_CUDA_W_O)) || (rc = upload_int4(down, L, GLACIER_CUDA_W_DOWN)))
       return rc;
     if (pair) {
-      pk.assign(F * D / 2, 0);
-      pk2.assign(F * D / 2, 0);
-      sc.assign(F * D / pair->group, 0.f);
-      sc2.assign(F * D / pair->group, 0.f);
-      pair_split(bytes + pair->s[S_PACKED].off, bytes + pair->s[S_ROWS4].off, F, D, pair->group, pk.data(),
-                 pk2.data(), sc.data(), sc2.data());
-      if ((rc = glacier_cuda_model_load_int4(model, L, GLACIER_CUDA_W_GATE, pk.data(), pk.size(), sc.data(),
-                                             sc.size())) ||
-          (rc = glacier_cuda_model_load_int4(model, L, GLACIER_CUDA_W_UP, pk2.data(), pk2.size(), sc2.data(),
-                                             sc2.size())))
+      // The pair bytes go up as stored and are split into gate and up rows on the device.
+      if ((rc = glacier_cuda_model_load_pair_nibble(
+               model, L, bytes + pair->s[S_PACKED].off, F * D,
+               reinterpret_cast<const uint16_t*>(bytes + pair->s[S_ROWS4].off), 2 * F * D / pair->group)))
         return rc;
     } else if ((rc = upload_int4(gate, L, GLACIER_CUDA_W_GATE)) || (rc = upload_int4(up, L, GLACIER_CUDA_W_UP))) {
       return rc;

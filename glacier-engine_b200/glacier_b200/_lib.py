@@ -58,6 +58,8 @@ SIGNATURES = {
     "glacier_cuda_model_create": ([vp], vp),
     "glacier_cuda_model_destroy": ([vp], None),
     "glacier_cuda_model_load_int4": ([vp, i32, i32, vp, sz, vp, sz], i32),
+    "glacier_cuda_model_load_int4_rows4": ([vp, i32, i32, vp, sz, vp, sz], i32),
+    "glacier_cuda_model_load_pair_nibble": ([vp, i32, vp, sz, vp, sz], i32),
     "glacier_cuda_model_load_qio": ([vp, i32, i32, vp, sz], i32),
     "glacier_cuda_model_load_f32": ([vp, i32, i32, vp, sz], i32),
     "glacier_cuda_model_load_embedding_f16": ([vp, vp, sz], i32),

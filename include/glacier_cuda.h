@@ -237,6 +237,18 @@ void glacier_cuda_model_destroy(glacier_cuda_model *model);
 int glacier_cuda_model_load_int4(glacier_cuda_model *model, int layer, int kind, const uint8_t *packed,
                                  size_t packed_bytes, const float *scales, size_t scale_count);
 
+/* Same with the codes in the prepared rows4_k16 nibble order (src/int4_weights.zig:113-170):
+ * uploaded as they are and put in row-major order on the device (rows % 4 == 0, in % 16 == 0). */
+int glacier_cuda_model_load_int4_rows4(glacier_cuda_model *model, int layer, int kind, const uint8_t *packed,
+                                       size_t packed_bytes, const float *scales, size_t scale_count);
+
+/* A layer's gate/up PairNibble record (src/int4_weights.zig:42-54, :322-331): pair bytes in
+ * rows4_k16 order (gate codes in the low nibbles, up in the high) and the fp16 scale grid
+ * [tile][group][branch][lane] (2 * hidden * dim / group values).  The pairs are split on the
+ * device into the gate and up rows. */
+int glacier_cuda_model_load_pair_nibble(glacier_cuda_model *model, int layer, const uint8_t *pairs,
+                                        size_t pair_bytes, const uint16_t *pair_scales, size_t scale_count);
+
 /* Same from a quantized page payload (src/model/qio.zig:73-113 encodePage layout). */
 int glacier_cuda_model_load_qio(glacier_cuda_model *model, int layer, int kind, const uint8_t *payload,
                                 size_t payload_bytes);
