@@ -488,9 +488,10 @@ def load_peaks() -> dict:
 # DRAM bytes (dram__bytes_read + write) per algorithmic byte, from one ncu capture of a smaller
 # case of the same kernel (profiles/); traffic scales with the K/V rows a launch reads.
 DRAM_TRAFFIC_RATIO = {
-    "attention": (269.455e6 / 265.1e6, "ncu dram__bytes_read.sum + dram__bytes_write.sum of the stream-K kernel: "
-                                       "265.7 MB read + 3.8 MB written for 265.1 MB algorithmic (1 layer, 32 lanes, "
-                                       "mean ctx 2015), scaled to this launch's K/V bytes"),
+    "attention": (269.894e6 / 265.1e6, "ncu dram__bytes_read.sum + dram__bytes_write.sum of the stream-K kernel "
+                                       "(12 warps x 2 stages): 265.7 MB read + 4.2 MB written for 265.1 MB "
+                                       "algorithmic (1 layer, 32 lanes, mean ctx 2015), scaled to this launch's K/V "
+                                       "bytes"),
 }
 
 STEP_KINDS = ("embed", "norm", "proj_qkv", "rope_append", "attention", "attn_combine", "proj_o", "proj_gate_up",
