@@ -141,6 +141,122 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// One half-page stage of one warp: base-2 scores of its 8 positions for the NG
+// heads, the online-softmax update of (m, l, acc) and P.V.  Kt / Vt: the stage's
+// K and V rows in shared memory; nvalid: positions inside the context; scr / prb:
+// the warp's score and probability scratch.  Shared by the stream-K kernel and
+// the cluster kernel for few lanes.
+template <int HD, int NG>
+__device__ __forceinline__ void attn_stage_math(const float* __restrict__ Kt, const float* __restrict__ Vt,
+                                                int nvalid, const float2 (&q2)[NG][HD / 32], float (&m)[NG],
+                                                float (&l)[NG], float2 (&acc)[NG][HD / 64], float* scr, float2* prb,
+                                                int lane) {
+  constexpr int DL4 = HD / 64;  // score phase: float4 loads per lane (16 lanes per position)
+  constexpr int VD = HD / 32;   // P.V phase: dims per lane
+  constexpr int G = NG;
+  const int l16 = lane & 15, ph = lane >> 4;
+  // -- scores (base-2 logits) for 8 positions, 2 per step --
+#pragma unroll
+  for (int step = 0; step < kStageRows / 2; ++step) {
+    const int pos = 2 * step + ph;
+    float4 kv[DL4];
+#pragma unroll
+    for (int i = 0; i < DL4; ++i) kv[i] = *reinterpret_cast<const float4*>(Kt + pos * HD + 4 * l16 + 64 * i);
+    float v[kMaxGroup];
+#pragma unroll
+    for (int g = NG; g < kMaxGroup; ++g) v[g] = 0.f;
+#pragma unroll
+    for (int g = 0; g < NG; ++g) {
+      float2 a = __fmul2_rn(q2[g][0], make_float2(kv[0].x, kv[0].y));
+      a = __ffma2_rn(q2[g][1], make_float2(kv[0].z, kv[0].w), a);
+#pragma unroll
+      for (int i = 1; i < DL4; ++i) {
+        a = __ffma2_rn(q2[g][2 * i], make_float2(kv[i].x, kv[i].y), a);
+        a = __ffma2_rn(q2[g][2 * i + 1], make_float2(kv[i].z, kv[i].w), a);
+      }
+      v[g] = a.x + a.y;
+    }
+    // Butterfly over the 16 lanes of this position: lanes 2h, 2h+1 end with head h.
+    const bool b8 = (l16 & 8) != 0, b4 = (l16 & 4) != 0, b2 = (l16 & 2) != 0;
+    float w4[4], w2[2];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float send = b8 ? v[k] : v[k + 4];
+      const float keep = b8 ? v[k + 4] : v[k];
+      w4[k] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+    }
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const float send = b4 ? w4[k] : w4[k + 2];
+      const float keep = b4 ? w4[k + 2] : w4[k];
+      w2[k] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+    }
+    const float send = b2 ? w2[0] : w2[1];
+    const float keep = b2 ? w2[1] : w2[0];
+    float sc = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+    sc += __shfl_xor_sync(0xffffffffu, sc, 1);
+    const int h = l16 >> 1;
+    if (h >= G || (nvalid < kStageRows && pos >= nvalid)) sc = -INFINITY;
+    if ((l16 & 1) == 0) scr[pos * kMaxGroup + h] = sc;
+  }
+  __syncwarp();
+  // -- online softmax over this stage: lane = (head lane & 7, positions (lane >> 3) + 4k) --
+  const int hh = lane & 7, r0 = lane >> 3;
+  const float s0 = scr[r0 * kMaxGroup + hh], s1 = scr[(r0 + 4) * kMaxGroup + hh];
+  float mp = fmaxf(s0, s1);
+  mp = fmaxf(mp, __shfl_xor_sync(0xffffffffu, mp, 8));
+  mp = fmaxf(mp, __shfl_xor_sync(0xffffffffu, mp, 16));
+  float alpha[NG], mh = 0.f;
+#pragma unroll
+  for (int g = 0; g < NG; ++g) {
+    const float mn = fmaxf(m[g], __shfl_sync(0xffffffffu, mp, g));
+    alpha[g] = (m[g] == -INFINITY) ? 0.f : ex2_approx(m[g] - mn);
+    m[g] = mn;
+    if (g == hh) mh = mn;
+  }
+  // Masked scores are -inf and give ex2(-inf) = 0; padding heads (hh >= G) are zeroed.
+  const float e0 = hh < G ? ex2_approx(s0 - mh) : 0.f;
+  const float e1 = hh < G ? ex2_approx(s1 - mh) : 0.f;
+  prb[r0 * kMaxGroup + hh] = make_float2(e0, e0);
+  prb[(r0 + 4) * kMaxGroup + hh] = make_float2(e1, e1);
+  float ps = e0 + e1;
+  ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+  ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+#pragma unroll
+  for (int g = 0; g < NG; ++g) {
+    l[g] = l[g] * alpha[g] + __shfl_sync(0xffffffffu, ps, g);
+    const float2 a2 = make_float2(alpha[g], alpha[g]);
+#pragma unroll
+    for (int i = 0; i < VD / 2; ++i) acc[g][i] = __fmul2_rn(acc[g][i], a2);
+  }
+  __syncwarp();
+  // -- P.V over the stage (positions past the context carry probability 0
+  //    and are skipped, so stale rows never enter the sum) --
+  auto pv_row = [&](int pos) {
+    float vv[VD];
+    if constexpr (VD == 4) {
+      const float4 t = *reinterpret_cast<const float4*>(Vt + pos * HD + 4 * lane);
+      vv[0] = t.x; vv[1] = t.y; vv[2] = t.z; vv[3] = t.w;
+    } else {
+      const float2 t = *reinterpret_cast<const float2*>(Vt + pos * HD + 2 * lane);
+      vv[0] = t.x; vv[1] = t.y;
+    }
+#pragma unroll
+    for (int g = 0; g < NG; ++g) {
+      const float2 pp = prb[pos * kMaxGroup + g];
+#pragma unroll
+      for (int i = 0; i < VD / 2; ++i)
+        acc[g][i] = __ffma2_rn(pp, make_float2(vv[2 * i], vv[2 * i + 1]), acc[g][i]);
+    }
+  };
+  if (nvalid == kStageRows) {
+#pragma unroll
+    for (int pos = 0; pos < kStageRows; ++pos) pv_row(pos);
+  } else {
+    for (int pos = 0; pos < nvalid; ++pos) pv_row(pos);
+  }
+}
+
 // NG = query heads per kv head (compile time); HD = head dim; kAttnWarps and
 // kAttnStages as above.
 template <int HD, int NG, int kAttnWarps, int kAttnStages>
@@ -163,7 +279,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
   griddep_launch();
   griddep_wait();  // q, the KV pages and the context lengths come from earlier kernels
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int l16 = lane & 15, ph = lane >> 4;
+  const int l16 = lane & 15;
   float* ring = sm + (size_t)warp * kAttnStages * 2 * TILE;
   float* scr = scr_all[warp];
   float2* prb = prb_all[warp];
@@ -291,106 +407,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
       const float* Kt = ring + (size_t)s * 2 * TILE;
       const float* Vt = Kt + TILE;
       const int nvalid = min(kStageRows, ctx - kStageRows * (sb + st));
-      // -- scores (base-2 logits) for 8 positions, 2 per step --
-#pragma unroll
-      for (int step = 0; step < kStageRows / 2; ++step) {
-        const int pos = 2 * step + ph;
-        float4 kv[DL4];
-#pragma unroll
-        for (int i = 0; i < DL4; ++i) kv[i] = *reinterpret_cast<const float4*>(Kt + pos * HD + 4 * l16 + 64 * i);
-        float v[kMaxGroup];
-#pragma unroll
-        for (int g = NG; g < kMaxGroup; ++g) v[g] = 0.f;
-#pragma unroll
-        for (int g = 0; g < NG; ++g) {
-          float2 a = __fmul2_rn(q2[g][0], make_float2(kv[0].x, kv[0].y));
-          a = __ffma2_rn(q2[g][1], make_float2(kv[0].z, kv[0].w), a);
-#pragma unroll
-          for (int i = 1; i < DL4; ++i) {
-            a = __ffma2_rn(q2[g][2 * i], make_float2(kv[i].x, kv[i].y), a);
-            a = __ffma2_rn(q2[g][2 * i + 1], make_float2(kv[i].z, kv[i].w), a);
-          }
-          v[g] = a.x + a.y;
-        }
-        // Butterfly over the 16 lanes of this position: lanes 2h, 2h+1 end with head h.
-        const bool b8 = (l16 & 8) != 0, b4 = (l16 & 4) != 0, b2 = (l16 & 2) != 0;
-        float w4[4], w2[2];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const float send = b8 ? v[k] : v[k + 4];
-          const float keep = b8 ? v[k + 4] : v[k];
-          w4[k] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
-        }
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-          const float send = b4 ? w4[k] : w4[k + 2];
-          const float keep = b4 ? w4[k + 2] : w4[k];
-          w2[k] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-        }
-        const float send = b2 ? w2[0] : w2[1];
-        const float keep = b2 ? w2[1] : w2[0];
-        float sc = keep + __shfl_xor_sync(0xffffffffu, send, 2);
-        sc += __shfl_xor_sync(0xffffffffu, sc, 1);
-        const int h = l16 >> 1;
-        if (h >= G || (nvalid < kStageRows && pos >= nvalid)) sc = -INFINITY;
-        if ((l16 & 1) == 0) scr[pos * kMaxGroup + h] = sc;
-      }
-      __syncwarp();
-      // -- online softmax over this stage: lane = (head lane & 7, positions (lane >> 3) + 4k) --
-      const int hh = lane & 7, r0 = lane >> 3;
-      const float s0 = scr[r0 * kMaxGroup + hh], s1 = scr[(r0 + 4) * kMaxGroup + hh];
-      float mp = fmaxf(s0, s1);
-      mp = fmaxf(mp, __shfl_xor_sync(0xffffffffu, mp, 8));
-      mp = fmaxf(mp, __shfl_xor_sync(0xffffffffu, mp, 16));
-      float alpha[NG], mh = 0.f;
-#pragma unroll
-      for (int g = 0; g < NG; ++g) {
-        const float mn = fmaxf(m[g], __shfl_sync(0xffffffffu, mp, g));
-        alpha[g] = (m[g] == -INFINITY) ? 0.f : ex2_approx(m[g] - mn);
-        m[g] = mn;
-        if (g == hh) mh = mn;
-      }
-      // Masked scores are -inf and give ex2(-inf) = 0; padding heads (hh >= G) are zeroed.
-      const float e0 = hh < G ? ex2_approx(s0 - mh) : 0.f;
-      const float e1 = hh < G ? ex2_approx(s1 - mh) : 0.f;
-      prb[r0 * kMaxGroup + hh] = make_float2(e0, e0);
-      prb[(r0 + 4) * kMaxGroup + hh] = make_float2(e1, e1);
-      float ps = e0 + e1;
-      ps += __shfl_xor_sync(0xffffffffu, ps, 8);
-      ps += __shfl_xor_sync(0xffffffffu, ps, 16);
-#pragma unroll
-      for (int g = 0; g < NG; ++g) {
-        l[g] = l[g] * alpha[g] + __shfl_sync(0xffffffffu, ps, g);
-        const float2 a2 = make_float2(alpha[g], alpha[g]);
-#pragma unroll
-        for (int i = 0; i < VD / 2; ++i) acc[g][i] = __fmul2_rn(acc[g][i], a2);
-      }
-      __syncwarp();
-      // -- P.V over the stage (positions past the context carry probability 0
-      //    and are skipped, so stale rows never enter the sum) --
-      auto pv_row = [&](int pos) {
-        float vv[VD];
-        if constexpr (VD == 4) {
-          const float4 t = *reinterpret_cast<const float4*>(Vt + pos * HD + 4 * lane);
-          vv[0] = t.x; vv[1] = t.y; vv[2] = t.z; vv[3] = t.w;
-        } else {
-          const float2 t = *reinterpret_cast<const float2*>(Vt + pos * HD + 2 * lane);
-          vv[0] = t.x; vv[1] = t.y;
-        }
-#pragma unroll
-        for (int g = 0; g < NG; ++g) {
-          const float2 pp = prb[pos * kMaxGroup + g];
-#pragma unroll
-          for (int i = 0; i < VD / 2; ++i)
-            acc[g][i] = __ffma2_rn(pp, make_float2(vv[2 * i], vv[2 * i + 1]), acc[g][i]);
-        }
-      };
-      if (nvalid == kStageRows) {
-#pragma unroll
-        for (int pos = 0; pos < kStageRows; ++pos) pv_row(pos);
-      } else {
-        for (int pos = 0; pos < nvalid; ++pos) pv_row(pos);
-      }
+      attn_stage_math<HD, NG>(Kt, Vt, nvalid, q2, m, l, acc, scr, prb, lane);
       __syncwarp();
       if (lane == 0) {
         fence_async_shared();  // this slot's generic reads precede the next async write into it
@@ -426,6 +443,170 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
   if (lane == 0)
     for (uint32_t i = consumed; i < issued; ++i) mbar_wait(&bars[warp][i % kAttnStages], (i / kAttnStages) & 1, err);
   __syncwarp();
+}
+
+// ---------------------------------------------------------------------------
+// Few lanes (4 or fewer, fp32 output): one cluster of kClusterCtas CTAs per
+// (lane, kv head) and no combine launch.  CTA c of the cluster takes stages
+// [c*ns/C, (c+1)*ns/C) of the pair's ns stages and its warps split those evenly;
+// each warp streams its stages through a private TMA ring (attn_stage_math).  The
+// warps' (max, sum, o) states merge in shared memory (warp g merges head g in
+// warp order), then CTA rank 0 merges the CTAs' states over distributed shared
+// memory in rank order and writes the normalised rows: the reduction order is
+// fixed, so the result is deterministic.  A pair of context 0 writes zeros.
+constexpr int kClusterCtas = 8;
+constexpr int kCWarps = 8, kCStages = 3;
+
+template <int HD, int NG>
+__global__ void __launch_bounds__(kCWarps * 32, 1)
+    attn_cluster_kernel(const __grid_constant__ CUtensorMap kvmap, const AttnParams p, int rows_per_page, int* err,
+                        float* __restrict__ out, size_t ldo) {
+  constexpr int TILE = kStageRows * HD;
+  constexpr int DL = HD / 16, DL4 = DL / 4, VD = HD / 32;
+  constexpr int SLOT = HD + 4;  // acc, then max (base 2) and sum; a multiple of 4 floats keeps float4 stores aligned
+  constexpr float kLog2e = 1.4426950408889634f;
+  extern __shared__ __align__(128) float sm[];
+  __shared__ uint64_t bars[kCWarps][kCStages];
+  __shared__ __align__(16) float scr_all[kCWarps][kStageRows * kMaxGroup];
+  __shared__ __align__(16) float2 prb_all[kCWarps][kStageRows * kMaxGroup];
+
+  griddep_launch();
+  griddep_wait();  // q, the KV pages and the context lengths come from earlier kernels
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, l16 = lane & 15;
+  const uint32_t cr = cluster_ctarank();
+  const int pair = blockIdx.x / kClusterCtas;
+  const int lid = pair / p.num_kv_heads, kvh = pair - lid * p.num_kv_heads;
+  const int ctx = lane_ctx(p.ctx_lens, lid, p.max_pages * 16);
+  const int ns = (ctx + kStageRows - 1) / kStageRows;
+  const int cb = (int)((long long)ns * cr / kClusterCtas), ce = (int)((long long)ns * (cr + 1) / kClusterCtas);
+  const int wb = cb + (ce - cb) * warp / kCWarps, we = cb + (ce - cb) * (warp + 1) / kCWarps;
+  float* ring = sm + (size_t)warp * kCStages * 2 * TILE;
+  if (lane == 0) {
+    for (int i = 0; i < kCStages; ++i) mbar_init(&bars[warp][i], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  // q of the G heads, scaled by 1/sqrt(hd) * log2(e), this lane's dims 4*l16 + 64*i + c.
+  const float qs = p.scale * kLog2e;
+  float2 q2[NG][DL / 2];
+  const float* qrow = p.q + (size_t)lid * p.ldq + (size_t)kvh * NG * HD;
+#pragma unroll
+  for (int g = 0; g < NG; ++g) {
+#pragma unroll
+    for (int i = 0; i < DL4; ++i) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(qrow + (size_t)g * HD + 4 * l16 + 64 * i));
+      q2[g][2 * i] = make_float2(v.x * qs, v.y * qs);
+      q2[g][2 * i + 1] = make_float2(v.z * qs, v.w * qs);
+    }
+  }
+  float m[NG], l[NG];
+  float2 acc[NG][VD / 2];
+#pragma unroll
+  for (int g = 0; g < NG; ++g) {
+    m[g] = -INFINITY;
+    l[g] = 0.f;
+#pragma unroll
+    for (int i = 0; i < VD / 2; ++i) acc[g][i] = make_float2(0.f, 0.f);
+  }
+
+  uint64_t pol = 0;
+  if (lane == 0) {
+    prefetch_tmap(&kvmap);
+    pol = l2_evict_first_policy();
+  }
+  int issued = wb;  // lane 0: next stage to load
+  auto issue = [&](int st) {
+    const int s = (st - wb) % kCStages;
+    const int j = st * kStageRows;  // first position of the stage
+    const int phys = p.block_tables[(size_t)lid * p.max_pages + (j >> 4)];
+    const int yk = phys * rows_per_page + p.layer * 32 + (j & 15);
+    float* dst = ring + (size_t)s * 2 * TILE;
+    mbar_arrive_expect_tx(&bars[warp][s], 2 * TILE * (uint32_t)sizeof(float));
+    tma_load_2d(dst, &kvmap, kvh * HD, yk, &bars[warp][s], pol);
+    tma_load_2d(dst + TILE, &kvmap, kvh * HD, yk + 16, &bars[warp][s], pol);
+  };
+  if (lane == 0)
+    for (; issued < min(we, wb + kCStages); ++issued) issue(issued);
+  int consumed = 0;
+  for (int st = wb; st < we; ++st, ++consumed) {
+    const int s = consumed % kCStages;
+    if (!__all_sync(0xffffffffu, mbar_wait(&bars[warp][s], (consumed / kCStages) & 1, err))) break;
+    const float* Kt = ring + (size_t)s * 2 * TILE;
+    const int nvalid = min(kStageRows, ctx - kStageRows * st);
+    attn_stage_math<HD, NG>(Kt, Kt + TILE, nvalid, q2, m, l, acc, scr_all[warp], prb_all[warp], lane);
+    __syncwarp();
+    if (lane == 0) {
+      fence_async_shared();  // this slot's generic reads precede the next async write into it
+      if (issued < we) issue(issued++);
+    }
+  }
+  // Leave no copy in flight (a wait that gave up leaves some outstanding).
+  if (lane == 0)
+    for (int i = consumed; i < issued - wb; ++i) mbar_wait(&bars[warp][i % kCStages], (i / kCStages) & 1, err);
+  __syncthreads();  // every ring is idle: the states go where the stages were
+
+  float* slots = sm;                         // [kCWarps][NG][SLOT]
+  float* cpart = sm + kCWarps * NG * SLOT;   // [NG][SLOT], read by rank 0 over DSMEM
+#pragma unroll
+  for (int g = 0; g < NG; ++g) {
+    float* d = slots + (warp * NG + g) * SLOT;
+    if constexpr (VD == 4) {
+      *reinterpret_cast<float4*>(d + 4 * lane) = make_float4(acc[g][0].x, acc[g][0].y, acc[g][1].x, acc[g][1].y);
+    } else {
+      *reinterpret_cast<float2*>(d + 2 * lane) = acc[g][0];
+    }
+    if (lane == 0) {
+      d[HD] = m[g];
+      d[HD + 1] = l[g];
+    }
+  }
+  __syncthreads();
+  if (warp < NG) {  // this CTA's state of head `warp`, over its warps in order
+    const int g = warp;
+    float M = -INFINITY;
+    for (int w = 0; w < kCWarps; ++w) M = fmaxf(M, slots[(w * NG + g) * SLOT + HD]);
+    float L = 0.f, a[VD];
+#pragma unroll
+    for (int i = 0; i < VD; ++i) a[i] = 0.f;
+    for (int w = 0; w < kCWarps; ++w) {
+      const float* d = slots + (w * NG + g) * SLOT;
+      const float e = d[HD] == -INFINITY ? 0.f : ex2_approx(d[HD] - M);
+      L = fmaf(d[HD + 1], e, L);
+#pragma unroll
+      for (int i = 0; i < VD; ++i) a[i] = fmaf(d[VD * lane + i], e, a[i]);
+    }
+    float* c = cpart + g * SLOT;
+#pragma unroll
+    for (int i = 0; i < VD; ++i) c[VD * lane + i] = a[i];
+    if (lane == 0) {
+      c[HD] = M;
+      c[HD + 1] = L;
+    }
+  }
+  cluster_sync_all();  // every CTA's state is visible to the cluster
+  if (cr == 0 && warp < NG) {
+    const int g = warp;
+    const uint32_t local = smem_u32(cpart + g * SLOT);
+    float M = -INFINITY;
+    for (uint32_t q = 0; q < kClusterCtas; ++q) M = fmaxf(M, ld_dsmem_f32(mapa_shared(local + 4 * HD, q)));
+    float L = 0.f, a[VD];
+#pragma unroll
+    for (int i = 0; i < VD; ++i) a[i] = 0.f;
+    for (uint32_t q = 0; q < kClusterCtas; ++q) {
+      const uint32_t base = mapa_shared(local, q);
+      const float mq = ld_dsmem_f32(base + 4 * HD);
+      const float e = mq == -INFINITY ? 0.f : ex2_approx(mq - M);
+      L = fmaf(ld_dsmem_f32(base + 4 * (HD + 1)), e, L);
+#pragma unroll
+      for (int i = 0; i < VD; ++i) a[i] = fmaf(ld_dsmem_f32(base + 4 * (VD * lane + i)), e, a[i]);
+    }
+    const float inv = L > 0.f ? 1.0f / L : 0.f;
+    float* o = out + (size_t)lid * ldo + (size_t)(kvh * NG + g) * HD + VD * lane;
+#pragma unroll
+    for (int i = 0; i < VD; ++i) o[i] = a[i] * inv;
+  }
+  cluster_sync_all();  // keep every CTA's shared memory until rank 0 has read it
 }
 
 // out[lane, h, :] = sum_s o_s * e^(m_s - M) / sum_s l_s * e^(m_s - M), in segment
@@ -693,6 +874,28 @@ int paged_attention(const float* q, size_t ldq, const float* pool, size_t page_f
   const CUtensorMap* kvmap = nullptr;
   int rc = attn_kv_map(pool, kv_dim, head_dim, &kvmap);
   if (rc) return rc;
+  if (lanes <= 4 && !so.xs) {
+    // Few lanes: one cluster per (lane, kv head) merges its own partials (no combine launch).
+    using CKern = void (*)(const CUtensorMap, const AttnParams, int, int*, float*, size_t);
+    CKern ck = nullptr;
+#define GLC_ATTN_CLUSTER_CASE(hd, ng) \
+  if (head_dim == hd && group == ng) ck = attn_cluster_kernel<hd, ng>;
+    GLC_ATTN_CLUSTER_CASE(128, 1) GLC_ATTN_CLUSTER_CASE(128, 2) GLC_ATTN_CLUSTER_CASE(128, 3)
+    GLC_ATTN_CLUSTER_CASE(128, 4) GLC_ATTN_CLUSTER_CASE(128, 5) GLC_ATTN_CLUSTER_CASE(128, 6)
+    GLC_ATTN_CLUSTER_CASE(128, 7) GLC_ATTN_CLUSTER_CASE(128, 8) GLC_ATTN_CLUSTER_CASE(64, 1)
+    GLC_ATTN_CLUSTER_CASE(64, 2) GLC_ATTN_CLUSTER_CASE(64, 3) GLC_ATTN_CLUSTER_CASE(64, 4)
+    GLC_ATTN_CLUSTER_CASE(64, 5) GLC_ATTN_CLUSTER_CASE(64, 6) GLC_ATTN_CLUSTER_CASE(64, 7)
+    GLC_ATTN_CLUSTER_CASE(64, 8)
+#undef GLC_ATTN_CLUSTER_CASE
+    GLC_REQUIRE(ck != nullptr, "paged_attention: no kernel for head_dim %zu / group %zu", head_dim, group);
+    GLC_REQUIRE(ldo % 4 == 0 && (uintptr_t)out % 16 == 0, "paged_attention: output rows must be 16-byte aligned");
+    const size_t csmem = (size_t)kCWarps * kCStages * 2 * kStageRows * head_dim * sizeof(float);
+    if ((rc = allow_dynamic_smem((const void*)ck, (int)csmem))) return rc;
+    int* cerr = device_symbol_address(g_attn_error);
+    GLC_REQUIRE(cerr != nullptr, "paged_attention: device status word unavailable");
+    return launch_pdl(ck, dim3((unsigned)(lanes * num_kv_heads * kClusterCtas)), dim3(kCWarps * 32), csmem, stream,
+                      kClusterCtas, *kvmap, prm, (int)(page_floats / kv_dim), cerr, out, ldo);
+  }
   const size_t smem = (size_t)warps_per_cta * stages * 2 * kStageRows * head_dim * sizeof(float);
   using Kern = void (*)(const CUtensorMap, const AttnParams, int, int, int*);
   Kern kern = nullptr;
