@@ -204,8 +204,8 @@ int upload_h2d(void* dst, const void* src, size_t bytes) {
     bb.st = nullptr;
     GLC_CHECK_CUDA(cudaStreamCreateWithFlags(&bb.st, cudaStreamNonBlocking));
     for (auto& e : bb.ev) GLC_CHECK_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
-    for (auto& b : bb.buf)
-      if (!b) GLC_CHECK_CUDA(cudaMallocHost(&b, kChunk));
+    for (auto& b : bb.buf)  // portable: pinned for every device's context, not only the first
+      if (!b) GLC_CHECK_CUDA(cudaHostAlloc(&b, kChunk, cudaHostAllocPortable));
     bb.device = dev;
   }
   const uint8_t* s = static_cast<const uint8_t*>(src);

@@ -627,8 +627,8 @@ __global__ void __launch_bounds__(1024) attn_combine_kernel(const float* __restr
   __shared__ float2 sh[32];
   __shared__ __align__(8) float2 xch;
   __shared__ int Cs[kMaxPlanLanes + 1], plan[2], segs[kMaxPlanLanes];
-  const int lane_id = blockIdx.x;
-  const int head0 = blockIdx.y * heads_per_block;
+  const int lane_id = blockIdx.y;
+  const int head0 = blockIdx.x * heads_per_block;  // the head blocks of a lane form one cluster
   const int nh = min(heads_per_block, num_heads - head0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
   // The segments each head of this lane was cut into (the attention kernel's plan).
@@ -688,8 +688,10 @@ __global__ void __launch_bounds__(1024) attn_combine_kernel(const float* __restr
   if (so.xs) {
     const float2 tot = row_sum_max(0.f, mx, sh, &xch);
     const float scale = split_scale(tot.y);
-    if (active) store_split8(so, lane_id, (size_t)num_heads * head_dim, (size_t)e0, acc, 1.0f / scale);
+    if (active)
+      store_split8(so, lane_id, (size_t)num_heads * head_dim, (size_t)head0 * head_dim + e0, acc, 1.0f / scale);
     if (threadIdx.x == 0) so.xscale[lane_id] = scale;
+    if (cluster_nctarank() > 1) cluster_sync_all();  // no CTA leaves while another reads its row max
   } else if (active) {
     float4* dst = reinterpret_cast<float4*>(out + lane_id * ldo + (size_t)head0 * head_dim + e0);
     dst[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
@@ -937,12 +939,16 @@ int paged_attention(const float* q, size_t ldq, const float* pool, size_t page_f
                         (const float*)prm.part_o, (const float*)prm.part_ml, nsplit, (int)head_dim, (int)num_heads,
                         out, ldo, ctx_lens, (int)lanes, (int)num_kv_heads, prm.warps, (int)max_pages * 16);
     }
-    const size_t hpb = num_heads;
+    // Two head blocks per lane (a cluster of 2, whose row max is combined over
+    // distributed shared memory) while that stays within one CTA per SM.
+    const size_t nblk = 2 * lanes <= (size_t)sm_count() && num_heads >= 2 ? 2 : 1;
+    const size_t hpb = ceil_div(num_heads, nblk);
     // One warp per head for the weights (up to 32 warps), enough threads for 8 values each.
     const size_t vals = ceil_div(hpb * head_dim / 8, (size_t)32) * 32;
     const unsigned threads = (unsigned)std::min<size_t>(1024, std::max(vals, hpb * (size_t)32));
-    const dim3 cgrid((unsigned)lanes, (unsigned)ceil_div(num_heads, hpb));
-    if ((rc = launch_pdl(attn_combine_kernel, cgrid, dim3(threads), hpb * (size_t)nsplit * sizeof(float), stream, 1,
+    const dim3 cgrid((unsigned)ceil_div(num_heads, hpb), (unsigned)lanes);
+    if ((rc = launch_pdl(attn_combine_kernel, cgrid, dim3(threads), hpb * (size_t)nsplit * sizeof(float), stream,
+                         (int)cgrid.x,
                          (const float*)prm.part_o, (const float*)prm.part_ml, nsplit, (int)head_dim, (int)num_heads,
                          out, ldo, so, ctx_lens, (int)lanes, (int)num_kv_heads, prm.warps, (int)hpb,
                          (int)max_pages * 16)))
