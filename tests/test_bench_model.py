@@ -44,3 +44,16 @@ def test_model_files(tmp_path):
     r.write_bytes(bytes(gr.build(gr.model_records(m, emb, mlp="pair"), gr.model_cfg(m))))
     cfg, hm = bench.bench_model(args(model_file=str(r)))
     assert cfg.vocab == 32 and np.array_equal(hm.layers[0]["wg"][0], m.layers[0]["wg"][0])
+
+
+def test_every_rank_decodes_the_same_context_multiset():
+    """Weak scaling keeps per-GPU work fixed: each rank's lanes hold the same contexts (rank 0's
+    seeded draw from U[ctx_min, ctx_max]) in a rank-specific order."""
+    import bench
+    a = argparse.Namespace(seed=2024, ctx_min=256, ctx_max=4096)
+    r0 = bench.lane_contexts(a, 64, 0)
+    assert r0.dtype == np.int32 and r0.min() >= 256 and r0.max() <= 4096
+    assert np.array_equal(r0, np.random.default_rng(2024).integers(256, 4097, size=64).astype(np.int32))
+    for rank in range(1, 8):
+        rk = bench.lane_contexts(a, 64, rank)
+        assert np.array_equal(np.sort(rk), np.sort(r0)) and not np.array_equal(rk, r0)
